@@ -1,0 +1,284 @@
+#!/usr/bin/env python
+"""Headline benchmark: training tokens/s for the ultra-7b MoE architecture on N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mamformer_b200|reference]
+
+For N > 1 launch with torchrun (one process per GPU, NCCL over NVLink); every rank runs the
+same steps and rank 0 prints one JSON line.
+
+Workload: ``configs/ultra-7b.yaml`` (d_model 4096, 32 heads / 8 KV heads, Mamba expand 2 with
+d_state 128, KDA-Diff, 2 shared + 128 routed experts top-8, MTP depth 2, vocab 128000) with
+the depth truncated to ``--layers`` (default 4: layout A S S F - attention-only, two SSM-only,
+one fusion layer, the same per-layer shapes as the full model); sequence length 4096;
+uniform-random token ids; random-init weights; bf16 compute with fp32 master weights and
+AdamW; per-GPU batch = micro_batch x grad_accum sequences (weak scaling).  A step is one full
+optimizer step (forward, backward, gradient reduction, clipping, AdamW).
+
+Timing: W untimed warm-up steps, then K steps between a barrier + device synchronisation,
+measured with CUDA events on the launching stream; the time is the max over ranks.  The
+working set (11+ GB of bf16 weights, GBs of activations) is far larger than the 126 MB L2.
+SM clocks and throttle reasons are sampled with nvidia-smi during the timed region.
+
+End-to-end number (``e2e``): the same metric through the public ``Trainer.train_step`` API
+with each step's token ids copied from pinned host memory and the loss read back to the host
+every step, timed on the host (max over ranks).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "train tokens/s per box, ultra-7b MoE bf16 @1/2/4/8 B200, max over ranks"
+BASELINE_TOKS = None  # the reference publishes no ultra-7b throughput ("not yet measured")
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mamformer_b200", choices=["mamformer_b200", "reference"])
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--micro-batch", type=int, default=1)
+    ap.add_argument("--grad-accum", type=int, default=16)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-launches", type=int, default=1)
+    return ap.parse_args()
+
+
+def bench_config(layers: int, root: str = ROOT) -> dict:
+    sys.path.insert(0, root)
+    from mamformer_b200.config import MamformerConfig
+    d = MamformerConfig.from_yaml(os.path.join(root, "configs", "ultra-7b.yaml")).to_dict()
+    d.update(n_layers=layers, interleave_fusion_layers=[layers - 1], interleave_last_layers_dense=1)
+    return d
+
+
+def _dist_init():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _emit(obj, rank):
+    if rank == 0:
+        print(json.dumps(obj), flush=True)
+
+
+def _count_launches(step_fn, prefix=("mamf::",)):
+    """Run one step under the profiler; return (our kernel launches, all kernel launches)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    ours = total = 0
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA and not ev.name.startswith("Memcpy") \
+                and not ev.name.startswith("Memset"):
+            total += 1
+            if any(p in ev.name for p in prefix):
+                ours += 1
+    return ours, total
+
+
+def run_ours(args, rank, world):
+    import torch
+    import torch.distributed as dist
+    from mamformer_b200 import ops
+    from mamformer_b200.config import MamformerConfig
+    from mamformer_b200.engine import TrainConfig, Trainer
+    from mamformer_b200.models.model import MamformerForCausalLM
+    from mamformer_b200.utils.clocks import ClockSampler
+
+    if not ops.has_native():
+        raise RuntimeError("native extension missing: run python setup.py build_ext --inplace")
+    cfg = MamformerConfig.from_dict(bench_config(args.layers))
+    per_gpu = args.micro_batch * args.grad_accum
+    tcfg = TrainConfig(learning_rate=2e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch,
+                       grad_accum=args.grad_accum)
+    torch.manual_seed(0)
+    model = MamformerForCausalLM(cfg).cuda()
+    group = dist.group.WORLD if world > 1 else None
+    trainer = Trainer(model, tcfg, dp_group=group)
+    n_batches = 2
+    g = torch.Generator().manual_seed(1234 + rank)
+    host = [torch.randint(0, cfg.vocab_size, (per_gpu, args.seq), generator=g).pin_memory()
+            for _ in range(n_batches)]
+    dev = [h.cuda() for h in host]
+
+    for i in range(args.warmup):
+        trainer.train_step(dev[i % n_batches])
+    _barrier(world)
+    clocks = ClockSampler(gpu_index=torch.cuda.current_device()).start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        trainer.train_step(dev[i % n_batches])
+    end.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    clk = clocks.stop()
+    ms = _max_over_ranks(start.elapsed_time(end), world) / args.steps
+    tokens_per_step = world * per_gpu * args.seq
+    value = tokens_per_step / (ms / 1000.0)
+
+    e2e = None
+    if not args.no_e2e and args.e2e_steps > 0:
+        _barrier(world)
+        t0 = time.perf_counter()
+        loss = None
+        for i in range(args.e2e_steps):
+            loss = trainer.train_step(host[i % n_batches], sync_loss=True)   # H2D ids, D2H loss
+        torch.cuda.synchronize()
+        el = _max_over_ranks(time.perf_counter() - t0, world) / args.e2e_steps
+        e2e = {"value": tokens_per_step / el, "unit": "tokens/s",
+               "h2d_bytes_per_step": host[0].numel() * host[0].element_size(),
+               "d2h_bytes_per_step": 4, "last_loss": loss}
+
+    launches = all_kernels = None
+    if args.profile_launches:
+        ours, total = _count_launches(lambda: trainer.train_step(dev[0]))
+        launches = ours * args.steps
+        all_kernels = total * args.steps
+    mem = torch.cuda.max_memory_allocated() / 2 ** 30
+    out = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
+        "data": "synthetic uniform-random token ids, random-init weights",
+        "impl": "mamformer_b200",
+        "config": {"model": f"ultra-7b (configs/ultra-7b.yaml) depth-truncated to {args.layers} layers "
+                            f"({cfg.layout_string()}), same per-layer shapes",
+                   "global_batch": world * per_gpu, "seq_len": args.seq,
+                   "micro_batch": args.micro_batch, "grad_accum": args.grad_accum,
+                   "parallelism": f"dp{world}",
+                   "params_b": round(sum(p.numel() for p in model.parameters()) / 1e9, 3),
+                   "l2": "working set >> L2 (inputs larger than L2)"},
+        "clocks": clk, "e2e": e2e, "gpu_launches": launches, "all_kernel_launches": all_kernels,
+        "peak_mem_gib": round(mem, 1),
+    }
+    _emit(out, rank)
+
+
+def run_reference(args, rank, world):
+    """The unmodified reference (installed under baseline/_ref) through its public API: the
+    same model config, fp32 weights + bf16 autocast + AdamW, the loop of its scripts/train.py
+    (FSDP FULL_SHARD for N > 1, as that script does)."""
+    import torch
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "mamformer")):
+        _emit({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"}, rank)
+        return
+    sys.path.insert(0, ref_dir)
+    from mamformer.config import MamformerConfig as RefConfig
+    from mamformer.model import MamformerForCausalLM as RefModel
+    cfg = RefConfig.from_dict(bench_config(args.layers))
+    per_gpu = args.micro_batch * args.grad_accum
+    try:
+        torch.manual_seed(0)
+        model = RefModel(cfg).cuda()
+        if world > 1:
+            from torch.distributed.fsdp import FullyShardedDataParallel as FSDP, MixedPrecision, ShardingStrategy
+            from torch.distributed.fsdp.wrap import ModuleWrapPolicy
+            from mamformer.layers.hybrid import MamformerBlock
+            model = FSDP(model, sharding_strategy=ShardingStrategy.FULL_SHARD,
+                         auto_wrap_policy=ModuleWrapPolicy({MamformerBlock}),
+                         mixed_precision=MixedPrecision(param_dtype=torch.bfloat16, reduce_dtype=torch.bfloat16,
+                                                        buffer_dtype=torch.bfloat16),
+                         device_id=torch.cuda.current_device(), use_orig_params=True)
+        decay, no_decay = [], []
+        for n, p in model.named_parameters():
+            (no_decay if any(k in n for k in ("norm", "bias", "gate", "alpha", "lambda_log", "A_log")) else decay).append(p)
+        opt = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1}, {"params": no_decay, "weight_decay": 0.0}],
+                                lr=2e-4, betas=(0.9, 0.95), eps=1e-8)
+        model.train()
+        g = torch.Generator().manual_seed(1234 + rank)
+        batch = torch.randint(0, cfg.vocab_size, (per_gpu, args.seq), generator=g).cuda()
+
+        def step():
+            opt.zero_grad()
+            for i in range(args.grad_accum):
+                mb = batch[i * args.micro_batch:(i + 1) * args.micro_batch]
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    loss = model(mb, labels=mb)["loss"]
+                (loss / args.grad_accum).backward()
+            torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+            opt.step()
+
+        for _ in range(args.warmup):
+            step()
+        _barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        ms = _max_over_ranks(s.elapsed_time(e), world) / args.steps
+        value = world * per_gpu * args.seq / (ms / 1000.0)
+        _emit({"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+               "config": {"model": f"ultra-7b truncated to {args.layers} layers", "global_batch": world * per_gpu,
+                          "seq_len": args.seq, "parallelism": f"fsdp{world}" if world > 1 else "single"}}, rank)
+    except torch.cuda.OutOfMemoryError as exc:
+        msg = str(exc).split("\n")[0][:160]
+        _emit({"impl": "reference", "unavailable": f"CUDA out of memory on a 180 GB B200 at seq {args.seq}, "
+                                                   f"micro-batch {args.micro_batch}: {msg}"}, rank)
+    except Exception as exc:   # the reference's own Triton kernel fails to compile on this image
+        name = type(exc).__name__
+        msg = str(exc).strip().split("\n")[-1][:160]
+        _emit({"impl": "reference", "unavailable": f"reference forward fails on its stock GPU path "
+                                                   f"({name}: {msg})"}, rank)
+
+
+def main():
+    args = _args()
+    rank, world, _ = _dist_init()
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world)
+    finally:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

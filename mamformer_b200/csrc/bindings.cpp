@@ -1,0 +1,56 @@
+// Python bindings of the native sm_100a kernels (module mamformer_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace mamf {
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps);
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd);
+at::Tensor swiglu_fwd(at::Tensor g, at::Tensor u);
+std::vector<at::Tensor> swiglu_bwd(at::Tensor g, at::Tensor u, at::Tensor dy);
+at::Tensor rope_apply(at::Tensor x, at::Tensor cos, at::Tensor sin, bool inverse);
+at::Tensor conv_silu_fwd(at::Tensor x, at::Tensor w);
+std::vector<at::Tensor> conv_silu_bwd(at::Tensor x, at::Tensor w, at::Tensor dy);
+std::vector<at::Tensor> head_groupnorm_fwd(at::Tensor x, int64_t H, at::Tensor w, at::Tensor b, double eps);
+std::vector<at::Tensor> head_groupnorm_bwd(at::Tensor x, int64_t H, at::Tensor w, at::Tensor mr, at::Tensor dy);
+std::vector<at::Tensor> selective_scan_fwd(at::Tensor x, at::Tensor dt, at::Tensor A_log, at::Tensor Bm,
+                                           at::Tensor Cm, at::Tensor D, c10::optional<at::Tensor> z,
+                                           c10::optional<at::Tensor> h0, bool softplus, bool need_hs,
+                                           bool need_final);
+std::vector<at::Tensor> selective_scan_bwd(at::Tensor x, at::Tensor dt, at::Tensor A_log, at::Tensor Bm,
+                                           at::Tensor Cm, at::Tensor D, c10::optional<at::Tensor> z,
+                                           at::Tensor ckpt, at::Tensor dy, c10::optional<at::Tensor> dhs,
+                                           bool softplus);
+void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> out16,
+                double lr, double b1, double b2, double eps, double wd, int64_t step,
+                c10::optional<at::Tensor> gscale);
+void sq_norm_accumulate(at::Tensor g, at::Tensor out);
+void clip_scale(at::Tensor sq, at::Tensor scale, double max_norm, double inv_world, at::Tensor norm_out);
+void grad_accumulate(at::Tensor dst, at::Tensor src);
+void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, bool accumulate,
+             c10::optional<at::Tensor> seg, c10::optional<at::Tensor> tile_off, int64_t mode, double alpha);
+int64_t gemm_error();
+void gemm_clear_error();
+}  // namespace mamf
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "mamformer_b200 native kernels for sm_100a (B200)";
+  m.def("rmsnorm_fwd", &mamf::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &mamf::rmsnorm_bwd);
+  m.def("swiglu_fwd", &mamf::swiglu_fwd);
+  m.def("swiglu_bwd", &mamf::swiglu_bwd);
+  m.def("rope_apply", &mamf::rope_apply);
+  m.def("conv_silu_fwd", &mamf::conv_silu_fwd);
+  m.def("conv_silu_bwd", &mamf::conv_silu_bwd);
+  m.def("head_groupnorm_fwd", &mamf::head_groupnorm_fwd);
+  m.def("head_groupnorm_bwd", &mamf::head_groupnorm_bwd);
+  m.def("selective_scan_fwd", &mamf::selective_scan_fwd);
+  m.def("selective_scan_bwd", &mamf::selective_scan_bwd);
+  m.def("adamw_step", &mamf::adamw_step);
+  m.def("sq_norm_accumulate", &mamf::sq_norm_accumulate);
+  m.def("clip_scale", &mamf::clip_scale);
+  m.def("grad_accumulate", &mamf::grad_accumulate);
+  m.def("gemm_tn", &mamf::gemm_tn);
+  m.def("gemm_error", &mamf::gemm_error);
+  m.def("gemm_clear_error", &mamf::gemm_clear_error);
+}

@@ -1,0 +1,574 @@
+// Memory-bound kernels: RMSNorm, SwiGLU, RoPE, causal depthwise conv + SiLU, per-head
+// GroupNorm.  All are bandwidth-bound on B200 (HBM3e), so each does one pass over its data
+// with 16-byte vector accesses and fp32 math.
+//
+// Reference semantics: RMSNorm mamformer/layers/norm.py:34-43; RoPE rope.py:283-339
+// (half-split rotation); conv mamba2.py:370-405; GroupNorm kda_diff.py:345-348
+// (nn.GroupNorm(H, H*hd) over (hd x S) per sample); SwiGLU ffn.py:71-80.
+#include "common.cuh"
+
+namespace mamf {
+
+// ============================ RMSNorm ========================================================
+// One warp per row, the row is held in registers (up to 32*8*NV elements).
+template <typename T, int NV>
+__global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                   T* __restrict__ y, float* __restrict__ rstd_out, int64_t rows,
+                                   int d, float eps) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * d;
+  Vec16<T> buf[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int col = (i * 32 + lane) * V;
+    if (col < d) {
+      buf[i] = ld16(xr + col);
+#pragma unroll
+      for (int k = 0; k < V; ++k) { float f = to_f(buf[i].v[k]); ss += f * f; }
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / d + eps);
+  if (lane == 0 && rstd_out) rstd_out[row] = r;
+  T* yr = y + row * d;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int col = (i * 32 + lane) * V;
+    if (col < d) {
+      Vec16<T> o;
+#pragma unroll
+      for (int k = 0; k < V; ++k) o.v[k] = from_f<T>(to_f(buf[i].v[k]) * r * w[col + k]);
+      st16(yr + col, o);
+    }
+  }
+}
+
+// dx = r * (g - xhat * mean(g * xhat)),  g = dy * w,  xhat = x * r
+template <typename T, int NV>
+__global__ void rmsnorm_bwd_dx_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                      const T* __restrict__ dy, const float* __restrict__ rstd,
+                                      T* __restrict__ dx, int64_t rows, int d) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float r = rstd[row];
+  Vec16<T> xb[NV], gb[NV];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int col = (i * 32 + lane) * V;
+    if (col < d) {
+      xb[i] = ld16(x + row * d + col);
+      gb[i] = ld16(dy + row * d + col);
+#pragma unroll
+      for (int k = 0; k < V; ++k) dot += to_f(gb[i].v[k]) * w[col + k] * to_f(xb[i].v[k]);
+    }
+  }
+  dot = warp_sum(dot) * r / d;   // mean(g * xhat) = r * mean(g*x)
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int col = (i * 32 + lane) * V;
+    if (col < d) {
+      Vec16<T> o;
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float g = to_f(gb[i].v[k]) * w[col + k];
+        const float xh = to_f(xb[i].v[k]) * r;
+        o.v[k] = from_f<T>(r * (g - xh * dot));
+      }
+      st16(dx + row * d + col, o);
+    }
+  }
+}
+
+// dw partial sums: block (32 x 8 threads) covers 32 columns and a slab of rows.
+template <typename T>
+__global__ void rmsnorm_bwd_dw_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                      const float* __restrict__ rstd, float* __restrict__ part,
+                                      int64_t rows, int d, int rows_per_block) {
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+  const int64_t r1 = min(rows, r0 + rows_per_block);
+  float acc = 0.f;
+  if (col < d)
+    for (int64_t r = r0 + threadIdx.y; r < r1; r += blockDim.y)
+      acc += to_f(dy[r * d + col]) * to_f(x[r * d + col]) * rstd[r];
+  __shared__ float sm[8][33];
+  sm[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && col < d) {
+    float s = 0.f;
+    for (int i = 0; i < blockDim.y; ++i) s += sm[i][threadIdx.x];
+    part[(int64_t)blockIdx.y * d + col] = s;
+  }
+}
+
+template <typename T>
+static int rms_nv(int d) {
+  constexpr int V = 16 / sizeof(T);
+  return (d + 32 * V - 1) / (32 * V);
+}
+
+// Calls fn(std::integral_constant<int, NV>) for the smallest supported NV >= nv.
+template <typename F>
+static void with_nv(int nv, F&& fn) {
+  if (nv <= 1) fn(std::integral_constant<int, 1>{});
+  else if (nv <= 2) fn(std::integral_constant<int, 2>{});
+  else if (nv <= 4) fn(std::integral_constant<int, 4>{});
+  else if (nv <= 8) fn(std::integral_constant<int, 8>{});
+  else if (nv <= 16) fn(std::integral_constant<int, 16>{});
+  else if (nv <= 32) fn(std::integral_constant<int, 32>{});
+  else TORCH_CHECK(false, "rmsnorm: d too large");
+}
+
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.is_contiguous() && w.dtype() == at::kFloat, "rmsnorm: contiguous x, fp32 weight");
+  const int d = x.size(-1);
+  const int64_t rows = x.numel() / d;
+  at::Tensor y = at::empty_like(x);
+  at::Tensor rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  at::Tensor wc = w.contiguous();
+  MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "rmsnorm_fwd", [&] {
+    TORCH_CHECK((d * sizeof(scalar_t)) % 16 == 0 && aligned16(x.data_ptr()), "rmsnorm: d*elt must be a multiple of 16 bytes");
+    const int blocks = (int)((rows + 7) / 8);
+    with_nv(rms_nv<scalar_t>(d), [&](auto nvc) {
+      constexpr int NVV = decltype(nvc)::value;
+      rmsnorm_fwd_kernel<scalar_t, NVV><<<blocks, 256, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(),
+          rstd.data_ptr<float>(), rows, d, (float)eps);
+    });
+  });
+  MAMF_LAUNCH_CHECK();
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd) {
+  c10::cuda::CUDAGuard g(x.device());
+  dy = dy.contiguous();
+  const int d = x.size(-1);
+  const int64_t rows = x.numel() / d;
+  at::Tensor dx = at::empty_like(x);
+  at::Tensor wc = w.contiguous();
+  const int rpb = 256;
+  const int nrb = (int)((rows + rpb - 1) / rpb);
+  at::Tensor part = at::empty({nrb, d}, x.options().dtype(at::kFloat));
+  MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "rmsnorm_bwd", [&] {
+    const int blocks = (int)((rows + 7) / 8);
+    with_nv(rms_nv<scalar_t>(d), [&](auto nvc) {
+      constexpr int NVV = decltype(nvc)::value;
+      rmsnorm_bwd_dx_kernel<scalar_t, NVV><<<blocks, 256, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
+          rstd.data_ptr<float>(), (scalar_t*)dx.data_ptr(), rows, d);
+    });
+    dim3 grid((d + 31) / 32, nrb);
+    rmsnorm_bwd_dw_kernel<scalar_t><<<grid, dim3(32, 8), 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), rstd.data_ptr<float>(),
+        part.data_ptr<float>(), rows, d, rpb);
+  });
+  MAMF_LAUNCH_CHECK();
+  return {dx, part.sum(0)};
+}
+
+// ============================ SwiGLU =========================================================
+template <typename T>
+__global__ void swiglu_fwd_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y,
+                                  int64_t rows, int cols, int64_t gs, int64_t us) {
+  constexpr int V = 16 / sizeof(T);
+  const int cv = cols / V;
+  const int64_t total = rows * cv;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cv;
+    const int c = (int)(i - r * cv) * V;
+    Vec16<T> a = ld16(g + r * gs + c), b = ld16(u + r * us + c), o;
+#pragma unroll
+    for (int k = 0; k < V; ++k) o.v[k] = from_f<T>(silu_f(to_f(a.v[k])) * to_f(b.v[k]));
+    st16(y + r * cols + c, o);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_bwd_kernel(const T* __restrict__ g, const T* __restrict__ u, const T* __restrict__ dy,
+                                  T* __restrict__ dg, T* __restrict__ du, int64_t rows, int cols,
+                                  int64_t gs, int64_t us) {
+  constexpr int V = 16 / sizeof(T);
+  const int cv = cols / V;
+  const int64_t total = rows * cv;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cv;
+    const int c = (int)(i - r * cv) * V;
+    Vec16<T> a = ld16(g + r * gs + c), b = ld16(u + r * us + c), d = ld16(dy + r * cols + c), og, ou;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float gv = to_f(a.v[k]), uv = to_f(b.v[k]), dv = to_f(d.v[k]);
+      const float s = sigmoid_f(gv);
+      og.v[k] = from_f<T>(dv * uv * s * (1.f + gv * (1.f - s)));
+      ou.v[k] = from_f<T>(dv * gv * s);
+    }
+    st16(dg + r * cols + c, og);
+    st16(du + r * cols + c, ou);
+  }
+}
+
+static int ew_blocks(int64_t n) { return (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 16); }
+
+at::Tensor swiglu_fwd(at::Tensor g, at::Tensor u) {
+  c10::cuda::CUDAGuard guard(g.device());
+  const int cols = g.size(-1);
+  const int64_t rows = g.numel() / cols;
+  TORCH_CHECK(g.stride(-1) == 1 && u.stride(-1) == 1, "swiglu: unit inner stride");
+  auto g2 = g.reshape({rows, cols}), u2 = u.reshape({rows, cols});
+  at::Tensor y = at::empty({rows, cols}, g.options());
+  MAMF_DISPATCH_FLOAT_BF16(g.scalar_type(), "swiglu_fwd", [&] {
+    TORCH_CHECK((cols * sizeof(scalar_t)) % 16 == 0, "swiglu: cols*elt % 16");
+    const int64_t n = rows * cols / (16 / sizeof(scalar_t));
+    swiglu_fwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>(
+        (const scalar_t*)g2.data_ptr(), (const scalar_t*)u2.data_ptr(), (scalar_t*)y.data_ptr(), rows, cols,
+        g2.stride(0), u2.stride(0));
+  });
+  MAMF_LAUNCH_CHECK();
+  auto shape = g.sizes().vec();
+  return y.view(shape);
+}
+
+std::vector<at::Tensor> swiglu_bwd(at::Tensor g, at::Tensor u, at::Tensor dy) {
+  c10::cuda::CUDAGuard guard(g.device());
+  const int cols = g.size(-1);
+  const int64_t rows = g.numel() / cols;
+  auto g2 = g.reshape({rows, cols}), u2 = u.reshape({rows, cols});
+  auto dy2 = dy.reshape({rows, cols}).contiguous();
+  at::Tensor dg = at::empty({rows, cols}, g.options()), du = at::empty({rows, cols}, g.options());
+  MAMF_DISPATCH_FLOAT_BF16(g.scalar_type(), "swiglu_bwd", [&] {
+    const int64_t n = rows * cols / (16 / sizeof(scalar_t));
+    swiglu_bwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>(
+        (const scalar_t*)g2.data_ptr(), (const scalar_t*)u2.data_ptr(), (const scalar_t*)dy2.data_ptr(),
+        (scalar_t*)dg.data_ptr(), (scalar_t*)du.data_ptr(), rows, cols, g2.stride(0), u2.stride(0));
+  });
+  MAMF_LAUNCH_CHECK();
+  auto shape = g.sizes().vec();
+  return {dg.view(shape), du.view(shape)};
+}
+
+// ============================ RoPE ===========================================================
+// x: (B, S, H, hd) with row stride xs between (b,s) rows (heads contiguous); cos/sin (S, hd/2).
+// sign = +1 forward, -1 backward (rotation by -theta).
+template <typename T>
+__global__ void rope_kernel(const T* __restrict__ x, T* __restrict__ y, const float* __restrict__ cs,
+                            const float* __restrict__ sn, int64_t BS, int S, int H, int hd,
+                            int64_t xs, float sign) {
+  const int half = hd / 2;
+  const int64_t total = BS * H * half;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % half);
+    const int64_t rh = i / half;
+    const int h = (int)(rh % H);
+    const int64_t bs = rh / H;
+    const int s = (int)(bs % S);
+    const T* xp = x + bs * xs + (int64_t)h * hd;
+    T* yp = y + (bs * H + h) * hd;
+    const float c = cs[(int64_t)s * half + j], sv = sign * sn[(int64_t)s * half + j];
+    const float x1 = to_f(xp[j]), x2 = to_f(xp[j + half]);
+    yp[j] = from_f<T>(x1 * c - x2 * sv);
+    yp[j + half] = from_f<T>(x2 * c + x1 * sv);
+  }
+}
+
+at::Tensor rope_apply(at::Tensor x, at::Tensor cos, at::Tensor sin, bool inverse) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.dim() == 4, "rope: x must be (B, S, H, hd)");
+  const int B = x.size(0), S = x.size(1), H = x.size(2), hd = x.size(3);
+  TORCH_CHECK(x.stride(3) == 1 && x.stride(2) == hd && x.stride(0) == x.stride(1) * S,
+              "rope: heads must be contiguous within a token row");
+  at::Tensor cc = cos.to(at::kFloat).contiguous(), ss = sin.to(at::kFloat).contiguous();
+  TORCH_CHECK(cc.size(0) == S && cc.size(1) == hd / 2, "rope: table shape");
+  at::Tensor y = at::empty({B, S, H, hd}, x.options());
+  MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "rope", [&] {
+    const int64_t n = (int64_t)B * S * H * (hd / 2);
+    rope_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), (scalar_t*)y.data_ptr(), cc.data_ptr<float>(), ss.data_ptr<float>(),
+        (int64_t)B * S, S, H, hd, x.stride(1), inverse ? -1.f : 1.f);
+  });
+  MAMF_LAUNCH_CHECK();
+  return y;
+}
+
+// ============================ causal depthwise conv + SiLU ===================================
+// x (B, S, C) with row stride xs; w (C, K).  Thread = one channel x a TT-step time tile.
+constexpr int CONV_TT = 64;
+
+template <typename T, int K>
+__global__ void conv_silu_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                     T* __restrict__ y, int B, int S, int C, int64_t xs) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t0 = blockIdx.y * CONV_TT;
+  const int b = blockIdx.z;
+  if (c >= C) return;
+  float wk[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) wk[k] = w[c * K + k];
+  float hist[K];
+#pragma unroll
+  for (int k = 0; k < K - 1; ++k) {
+    const int t = t0 - (K - 1) + k;
+    hist[k] = t >= 0 ? to_f(x[((int64_t)b * S + t) * xs + c]) : 0.f;
+  }
+  const int t1 = min(S, t0 + CONV_TT);
+  for (int t = t0; t < t1; ++t) {
+    hist[K - 1] = to_f(x[((int64_t)b * S + t) * xs + c]);
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], hist[k], acc);
+    y[((int64_t)b * S + t) * C + c] = from_f<T>(silu_f(acc));
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) hist[k] = hist[k + 1];
+  }
+}
+
+// dpre[t] = dy[t] * silu'(pre[t]);  dx[t] = sum_k w[k] dpre[t + K-1-k];  dw[k] += dpre[t] x[t-K+1+k]
+template <typename T, int K>
+__global__ void conv_silu_bwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                     const T* __restrict__ dy, T* __restrict__ dx,
+                                     float* __restrict__ dw_part, int B, int S, int C, int64_t xs) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int tile = blockIdx.y;
+  const int t0 = tile * CONV_TT;
+  const int b = blockIdx.z;
+  if (c >= C) return;
+  float wk[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) wk[k] = w[c * K + k];
+  auto X = [&](int t) -> float { return (t >= 0 && t < S) ? to_f(x[((int64_t)b * S + t) * xs + c]) : 0.f; };
+  auto DPRE = [&](int t) -> float {
+    if (t < 0 || t >= S) return 0.f;
+    float pre = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) pre = fmaf(wk[k], X(t - (K - 1) + k), pre);
+    const float s = sigmoid_f(pre);
+    return to_f(dy[((int64_t)b * S + t) * C + c]) * s * (1.f + pre * (1.f - s));
+  };
+  float dp[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) dp[k] = DPRE(t0 + k);
+  float dwa[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) dwa[k] = 0.f;
+  const int t1 = min(S, t0 + CONV_TT);
+  for (int t = t0; t < t1; ++t) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc = fmaf(wk[k], dp[K - 1 - k], acc);
+    dx[((int64_t)b * S + t) * C + c] = from_f<T>(acc);
+    const float d0 = dp[0];
+#pragma unroll
+    for (int k = 0; k < K; ++k) dwa[k] = fmaf(d0, X(t - (K - 1) + k), dwa[k]);
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) dp[k] = dp[k + 1];
+    dp[K - 1] = DPRE(t + K);
+  }
+  const int64_t pidx = ((int64_t)b * gridDim.y + tile);
+#pragma unroll
+  for (int k = 0; k < K; ++k) dw_part[(pidx * C + c) * K + k] = dwa[k];
+}
+
+at::Tensor conv_silu_fwd(at::Tensor x, at::Tensor w) {
+  c10::cuda::CUDAGuard guard(x.device());
+  const int B = x.size(0), S = x.size(1), C = x.size(2), K = w.size(1);
+  TORCH_CHECK(x.stride(2) == 1 && x.stride(0) == x.stride(1) * S, "conv: x rows must be uniformly strided");
+  at::Tensor wc = w.to(at::kFloat).contiguous();
+  at::Tensor y = at::empty({B, S, C}, x.options());
+  dim3 grid((C + 127) / 128, (S + CONV_TT - 1) / CONV_TT, B);
+  MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "conv_silu_fwd", [&] {
+    TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
+    conv_silu_fwd_kernel<scalar_t, 4><<<grid, 128, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(), B, S, C, x.stride(1));
+  });
+  MAMF_LAUNCH_CHECK();
+  return y;
+}
+
+std::vector<at::Tensor> conv_silu_bwd(at::Tensor x, at::Tensor w, at::Tensor dy) {
+  c10::cuda::CUDAGuard guard(x.device());
+  const int B = x.size(0), S = x.size(1), C = x.size(2), K = w.size(1);
+  dy = dy.contiguous();
+  at::Tensor wc = w.to(at::kFloat).contiguous();
+  at::Tensor dx = at::empty({B, S, C}, x.options());
+  const int tiles = (S + CONV_TT - 1) / CONV_TT;
+  at::Tensor part = at::empty({(int64_t)B * tiles, C, K}, x.options().dtype(at::kFloat));
+  dim3 grid((C + 127) / 128, tiles, B);
+  MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "conv_silu_bwd", [&] {
+    TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
+    conv_silu_bwd_kernel<scalar_t, 4><<<grid, 128, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
+        (scalar_t*)dx.data_ptr(), part.data_ptr<float>(), B, S, C, x.stride(1));
+  });
+  MAMF_LAUNCH_CHECK();
+  return {dx, part.sum(0)};
+}
+
+// ============================ per-head GroupNorm =============================================
+// x (B, S, H*hd) contiguous.  Group (b, h) spans S x hd elements.  Pass 1: per (b, h, S-tile)
+// partial (count, mean, M2); finalize combines them (Chan) in double; pass 2 normalises.
+constexpr int GN_ROWS = 64;
+
+template <typename T>
+__global__ void gn_stats_kernel(const T* __restrict__ x, float* __restrict__ part, int S, int H, int hd) {
+  const int b = blockIdx.z, h = blockIdx.y, tile = blockIdx.x;
+  const int s0 = tile * GN_ROWS, s1 = min(S, s0 + GN_ROWS);
+  const int C = H * hd;
+  float sum = 0.f, sq = 0.f;
+  for (int s = s0 + threadIdx.y; s < s1; s += blockDim.y)
+    for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+      const float v = to_f(x[((int64_t)b * S + s) * C + (int64_t)h * hd + j]);
+      sum += v; sq += v * v;
+    }
+  __shared__ float sm[64];
+  const int lin = threadIdx.y * blockDim.x + threadIdx.x;
+  sum = block_sum(sum, sm);
+  sq = block_sum(sq, sm);
+  if (lin == 0) {
+    const int64_t o = (((int64_t)b * H + h) * gridDim.x + tile) * 3;
+    const float n = (float)((s1 - s0) * hd);
+    const float mean = sum / n;
+    part[o] = n; part[o + 1] = mean; part[o + 2] = fmaxf(sq - sum * mean, 0.f);
+  }
+}
+
+__global__ void gn_finalize_kernel(const float* __restrict__ part, float* __restrict__ mean_rstd,
+                                   int groups, int tiles, float eps) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  double n = 0, mean = 0, m2 = 0;
+  for (int t = 0; t < tiles; ++t) {
+    const float* q = part + ((int64_t)g * tiles + t) * 3;
+    const double nb = q[0], mb = q[1], m2b = q[2];
+    const double nt = n + nb;
+    const double delta = mb - mean;
+    mean += delta * nb / nt;
+    m2 += m2b + delta * delta * n * nb / nt;
+    n = nt;
+  }
+  mean_rstd[2 * g] = (float)mean;
+  mean_rstd[2 * g + 1] = (float)(1.0 / sqrt(m2 / n + (double)eps));
+}
+
+template <typename T>
+__global__ void gn_apply_kernel(const T* __restrict__ x, const float* __restrict__ mr,
+                                const float* __restrict__ w, const float* __restrict__ bias,
+                                T* __restrict__ y, int64_t rows, int S, int H, int hd) {
+  const int C = H * hd;
+  const int64_t total = rows * C;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const int64_t r = i / C;
+    const int b = (int)(r / S), h = c / hd;
+    const float m = mr[2 * (b * H + h)], rs = mr[2 * (b * H + h) + 1];
+    y[i] = from_f<T>((to_f(x[i]) - m) * rs * w[c] + bias[c]);
+  }
+}
+
+// backward pass 1: per (b, h, tile): sum(dy*w), sum(dy*w*xhat); per channel partial dw, db.
+template <typename T>
+__global__ void gn_bwd_reduce_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                     const float* __restrict__ mr, const float* __restrict__ w,
+                                     float* __restrict__ gpart, float* __restrict__ wpart,
+                                     int S, int H, int hd) {
+  const int b = blockIdx.z, h = blockIdx.y, tile = blockIdx.x;
+  const int s0 = tile * GN_ROWS, s1 = min(S, s0 + GN_ROWS);
+  const int C = H * hd;
+  const float m = mr[2 * (b * H + h)], rs = mr[2 * (b * H + h) + 1];
+  float a1 = 0.f, a2 = 0.f;
+  for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+    float dwj = 0.f, dbj = 0.f;
+    for (int s = s0 + threadIdx.y; s < s1; s += blockDim.y) {
+      const int64_t off = ((int64_t)b * S + s) * C + (int64_t)h * hd + j;
+      const float xh = (to_f(x[off]) - m) * rs;
+      const float d = to_f(dy[off]);
+      const float g = d * w[h * hd + j];
+      a1 += g; a2 += g * xh;
+      dwj += d * xh; dbj += d;
+    }
+    const int64_t wo = ((((int64_t)b * gridDim.x + tile) * blockDim.y + threadIdx.y) * C + (int64_t)h * hd + j) * 2;
+    wpart[wo] = dwj; wpart[wo + 1] = dbj;
+  }
+  __shared__ float sm[64];
+  a1 = block_sum(a1, sm);
+  a2 = block_sum(a2, sm);
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
+    const int64_t o = (((int64_t)b * H + h) * gridDim.x + tile) * 2;
+    gpart[o] = a1; gpart[o + 1] = a2;
+  }
+}
+
+template <typename T>
+__global__ void gn_bwd_dx_kernel(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ mr,
+                                 const float* __restrict__ w, const float* __restrict__ gsum,
+                                 T* __restrict__ dx, int64_t rows, int S, int H, int hd) {
+  const int C = H * hd;
+  const float inv_n = 1.f / ((float)S * hd);
+  const int64_t total = rows * C;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const int64_t r = i / C;
+    const int b = (int)(r / S), h = c / hd;
+    const int g = b * H + h;
+    const float m = mr[2 * g], rs = mr[2 * g + 1];
+    const float xh = (to_f(x[i]) - m) * rs;
+    const float gg = to_f(dy[i]) * w[c];
+    dx[i] = from_f<T>(rs * (gg - gsum[2 * g] * inv_n - xh * gsum[2 * g + 1] * inv_n));
+  }
+}
+
+std::vector<at::Tensor> head_groupnorm_fwd(at::Tensor x, int64_t H, at::Tensor w, at::Tensor bias, double eps) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 3, "groupnorm: contiguous (B, S, C)");
+  const int B = x.size(0), S = x.size(1), C = x.size(2), hd = C / H;
+  const int tiles = (S + GN_ROWS - 1) / GN_ROWS;
+  auto f32 = x.options().dtype(at::kFloat);
+  at::Tensor part = at::empty({(int64_t)B * H * tiles * 3}, f32);
+  at::Tensor mr = at::empty({(int64_t)B * H, 2}, f32);
+  at::Tensor y = at::empty_like(x);
+  at::Tensor wc = w.to(at::kFloat).contiguous(), bc = bias.to(at::kFloat).contiguous();
+  MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "gn_fwd", [&] {
+    gn_stats_kernel<scalar_t><<<dim3(tiles, H, B), dim3(std::min(hd, 128), 4), 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), part.data_ptr<float>(), S, H, hd);
+    gn_finalize_kernel<<<(B * H + 127) / 128, 128, 0, stream()>>>(part.data_ptr<float>(), mr.data_ptr<float>(),
+                                                                  B * H, tiles, (float)eps);
+    gn_apply_kernel<scalar_t><<<ew_blocks(x.numel()), 256, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(), bc.data_ptr<float>(),
+        (scalar_t*)y.data_ptr(), (int64_t)B * S, S, H, hd);
+  });
+  MAMF_LAUNCH_CHECK();
+  return {y, mr};
+}
+
+std::vector<at::Tensor> head_groupnorm_bwd(at::Tensor x, int64_t H, at::Tensor w, at::Tensor mr, at::Tensor dy) {
+  c10::cuda::CUDAGuard guard(x.device());
+  dy = dy.contiguous();
+  const int B = x.size(0), S = x.size(1), C = x.size(2), hd = C / H;
+  const int tiles = (S + GN_ROWS - 1) / GN_ROWS;
+  auto f32 = x.options().dtype(at::kFloat);
+  const int by = 4;
+  at::Tensor gpart = at::empty({(int64_t)B * H, tiles, 2}, f32);
+  at::Tensor wpart = at::empty({(int64_t)B * tiles * by, C, 2}, f32);
+  at::Tensor dx = at::empty_like(x);
+  at::Tensor wc = w.to(at::kFloat).contiguous();
+  MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "gn_bwd", [&] {
+    gn_bwd_reduce_kernel<scalar_t><<<dim3(tiles, H, B), dim3(std::min(hd, 128), by), 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(),
+        gpart.data_ptr<float>(), wpart.data_ptr<float>(), S, H, hd);
+    at::Tensor gsum = gpart.sum(1).contiguous();
+    gn_bwd_dx_kernel<scalar_t><<<ew_blocks(x.numel()), 256, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(),
+        gsum.data_ptr<float>(), (scalar_t*)dx.data_ptr(), (int64_t)B * S, S, H, hd);
+  });
+  MAMF_LAUNCH_CHECK();
+  at::Tensor wsum = wpart.sum(0);
+  return {dx, wsum.select(1, 0), wsum.select(1, 1)};
+}
+
+}  // namespace mamf

@@ -1,0 +1,532 @@
+// Diagonal selective scan (the reference's Mamba2Block recurrence), forward and backward.
+//
+//   h[t,c,n] = exp(-A[n] dt[t,c]) h[t-1,c,n] + B[t,n] dt[t,c] x[t,c]
+//   y[t,c]   = (sum_n C[t,n] h[t,c,n] + D[c] x[t,c]) * silu(z[t,c])        (GATE)
+//   hs[t,n]  = mean_c h[t,c,n]                                             (HS)
+// with A = exp(clamp(A_log, -5, 5)) and dt = softplus(dt_raw) (SOFTPLUS).
+// Reference semantics: mamformer/layers/mamba2.py:70-130 (scan), 249-368 (block).
+//
+// Work split (sm_100a, 148 SMs): one CTA per (batch, 32-channel block); warp w owns states
+// [32w, 32w+32) of all 32 channels; lane = channel.  Each thread keeps its 32 states in
+// registers, so the time recurrence is 32 independent FMA chains per thread (ILP) and the
+// decay exp2 runs on the MUFU pipe.  Inputs of a 32-step chunk are staged in shared memory
+// (B/C rows are broadcast reads).  Reductions over channels (h_states, dB, dC) use a 5-step
+// in-warp reduce-scatter after which lane l holds the 32-channel sum for state 32w+l; the
+// per-block partial rows are written to [batch, channel-block, S, N] and summed by the caller.
+//
+// Backward: the forward stores the state at every 32-step chunk start (fp32).  The backward
+// walks chunks in reverse: phase A recomputes the chunk forward (saving 4-step
+// sub-checkpoints to a per-CTA global scratch area and producing y, dz, dC); phase B walks
+// the 4-step sub-chunks in reverse: B1 runs the adjoint recurrence
+// G[t] = a[t+1] G[t+1] + C[t] dy'[t] + dhs[t]/Di (fp32 carry in registers, G copied to shared
+// memory as bf16), B2 recomputes h from the sub-checkpoint and forms the decay gradients
+// sum_n G a h[t-1] A[n] (-> ddt) and sum G a h[t-1] dt (-> dA).
+#include "common.cuh"
+
+namespace mamf {
+namespace scan {
+
+constexpr int CK = 32;      // checkpoint / staging chunk (time steps)
+constexpr int SUB = 4;      // backward sub-chunk (time steps between sub-checkpoints)
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// After the call lane l holds sum over the 32 lanes of v[l]; v is destroyed.
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const bool up = lane & 16;
+    float send = up ? v[j] : v[j + 16];
+    float keep = up ? v[j + 16] : v[j];
+    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const bool up = lane & 8;
+    float send = up ? v[j] : v[j + 8];
+    float keep = up ? v[j + 8] : v[j];
+    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const bool up = lane & 4;
+    float send = up ? v[j] : v[j + 4];
+    float keep = up ? v[j + 4] : v[j];
+    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const bool up = lane & 2;
+    float send = up ? v[j] : v[j + 2];
+    float keep = up ? v[j + 2] : v[j];
+    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  {
+    const bool up = lane & 1;
+    float send = up ? v[0] : v[1];
+    float keep = up ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+  }
+  return v[0];
+}
+
+struct Params {
+  int Bsz, S, Di, N, G, nck;
+  // inputs: [b, t, c] / [b, t, n] with unit inner stride
+  const void* x;  int64_t x_bs, x_ts;
+  const void* dt; int64_t dt_bs, dt_ts;
+  const void* Bm; int64_t B_bs, B_ts;
+  const void* Cm; int64_t C_bs, C_ts;
+  const void* z;  int64_t z_bs, z_ts;
+  const float* A_log;
+  const float* D;
+  const float* h0;          // [Bsz, Di, N] or null
+  // forward outputs
+  void* y; int64_t y_bs, y_ts;
+  float* hs_part;           // [Bsz, G, S, N]
+  float* ckpt;              // [Bsz, nck, Di, N]
+  float* final_state;       // [Bsz, Di, N] or null
+  // backward
+  const void* dy; int64_t dy_bs, dy_ts;
+  const float* dhs;         // [Bsz, S, N] or null
+  void* dx; void* ddt; void* dz;   // contiguous [b, t, c]
+  float* dB_part; float* dC_part;  // [Bsz, G, S, N]
+  float* dA;                // [N]   (d loss / d A[n])
+  float* dD;                // [Di]
+  float* scratch;           // per CTA: [CK/SUB][32][NT]
+};
+
+template <typename T>
+__device__ __forceinline__ float ldf(const void* base, int64_t off) {
+  return to_f<T>(reinterpret_cast<const T*>(base)[off]);
+}
+
+// ---------------------------------------------------------------------------------------------
+template <typename T, int NW, bool SOFTPLUS, bool GATE, bool HS>
+__global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
+  constexpr int NT = NW * 32;
+  const int N = NW * 32;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int b = blockIdx.y, cblk = blockIdx.x;
+  const int c = cblk * 32 + lane;
+  const bool cvalid = c < p.Di;
+
+  extern __shared__ float smem[];
+  float* sB = smem;                 // [CK][N]
+  float* sC = sB + CK * N;          // [CK][N]
+  float* sDt = sC + CK * N;         // [CK][32]
+  float* sDtx = sDt + CK * 32;      // [CK][32]
+  float* sY = sDtx + CK * 32;       // [CK][32]
+
+  float A2[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float al = fminf(fmaxf(p.A_log[w * 32 + j], -5.f), 5.f);
+    A2[j] = -__expf(al) * LOG2E;
+  }
+  float h[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    h[j] = (p.h0 && cvalid) ? p.h0[((int64_t)b * p.Di + c) * N + w * 32 + j] : 0.f;
+
+  for (int t0 = 0, ck = 0; t0 < p.S; t0 += CK, ++ck) {
+    const int L = min(CK, p.S - t0);
+    if (p.ckpt && cvalid) {
+      float4* dst = reinterpret_cast<float4*>(p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + c) * N + w * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < L * N; i += NT) {
+      const int tt = i / N, n = i - tt * N;
+      sB[i] = ldf<T>(p.Bm, (int64_t)b * p.B_bs + (int64_t)(t0 + tt) * p.B_ts + n);
+      sC[i] = ldf<T>(p.Cm, (int64_t)b * p.C_bs + (int64_t)(t0 + tt) * p.C_ts + n);
+    }
+    for (int i = threadIdx.x; i < L * 32; i += NT) {
+      const int tt = i >> 5, cc = cblk * 32 + (i & 31);
+      float d = 0.f, xv = 0.f;
+      if (cc < p.Di) {
+        d = ldf<T>(p.dt, (int64_t)b * p.dt_bs + (int64_t)(t0 + tt) * p.dt_ts + cc);
+        if (SOFTPLUS) d = softplus_f(d);
+        xv = ldf<T>(p.x, (int64_t)b * p.x_bs + (int64_t)(t0 + tt) * p.x_ts + cc);
+      }
+      sDt[i] = d;
+      sDtx[i] = d * xv;
+      sY[i] = 0.f;
+    }
+    __syncthreads();
+    for (int tt = 0; tt < L; ++tt) {
+      const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
+      const float4* Bt = reinterpret_cast<const float4*>(sB + tt * N + w * 32);
+      const float4* Ct = reinterpret_cast<const float4*>(sC + tt * N + w * 32);
+      float yp = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 bq = Bt[q], cq = Ct[q];
+        const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
+        const float cc[4] = {cq.x, cq.y, cq.z, cq.w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int j = 4 * q + r;
+          const float a = ex2(A2[j] * d);
+          h[j] = fmaf(a, h[j], bb[r] * dxv);
+          yp = fmaf(cc[r], h[j], yp);
+        }
+      }
+      atomicAdd(&sY[tt * 32 + lane], yp);
+      if (HS) {
+        float tmp[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tmp[j] = h[j];
+        const float r = reduce_scatter32(tmp, lane);
+        p.hs_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * 32 + lane] = r;
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < L * 32; i += NT) {
+      const int tt = i >> 5, cc = cblk * 32 + (i & 31);
+      if (cc >= p.Di) continue;
+      const float xv = ldf<T>(p.x, (int64_t)b * p.x_bs + (int64_t)(t0 + tt) * p.x_ts + cc);
+      float yv = sY[i] + p.D[cc] * xv;
+      if (GATE) yv *= silu_f(ldf<T>(p.z, (int64_t)b * p.z_bs + (int64_t)(t0 + tt) * p.z_ts + cc));
+      reinterpret_cast<T*>(p.y)[(int64_t)b * p.y_bs + (int64_t)(t0 + tt) * p.y_ts + cc] = from_f<T>(yv);
+    }
+  }
+  if (p.final_state && cvalid) {
+    float* dst = p.final_state + ((int64_t)b * p.Di + c) * N + w * 32;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) dst[j] = h[j];
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+template <typename T, int NW, bool SOFTPLUS, bool GATE, bool HS>
+__global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
+  constexpr int NT = NW * 32;
+  const int N = NW * 32;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int b = blockIdx.y, cblk = blockIdx.x;
+  const int c = cblk * 32 + lane;
+  const bool cvalid = c < p.Di;
+  const float inv_di = 1.f / (float)p.Di;
+
+  extern __shared__ float smem[];
+  float* sB = smem;                       // [CK][N]
+  float* sC = sB + CK * N;                // [CK][N]
+  float* sDhs = sC + CK * N;              // [CK][N]  (HS)
+  float* sDt = sDhs + (HS ? CK * N : 0);  // [CK][32]
+  float* sDtx = sDt + CK * 32;
+  float* sX = sDtx + CK * 32;
+  float* sDyp = sX + CK * 32;
+  float* sY = sDyp + CK * 32;
+  float* sDU = sY + CK * 32;
+  float* sDD = sDU + CK * 32;
+  float* sA2 = sDD + CK * 32;             // [N]
+  float* sDsum = sA2 + N;                 // [32]
+  __nv_bfloat16* sG = reinterpret_cast<__nv_bfloat16*>(sDsum + 32);   // [SUB][32][NT]
+
+  for (int i = tid; i < N; i += NT) {
+    float al = fminf(fmaxf(p.A_log[i], -5.f), 5.f);
+    sA2[i] = -__expf(al) * LOG2E;
+  }
+  if (tid < 32) sDsum[tid] = 0.f;
+  float* scratch = p.scratch + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * (CK / SUB) * 32 * NT;
+
+  float P[32], dAacc[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) { P[j] = 0.f; dAacc[j] = 0.f; }
+  __syncthreads();
+
+  for (int ck = p.nck - 1; ck >= 0; --ck) {
+    const int t0 = ck * CK;
+    const int L = min(CK, p.S - t0);
+    __syncthreads();
+    for (int i = tid; i < L * N; i += NT) {
+      const int tt = i / N, n = i - tt * N;
+      sB[i] = ldf<T>(p.Bm, (int64_t)b * p.B_bs + (int64_t)(t0 + tt) * p.B_ts + n);
+      sC[i] = ldf<T>(p.Cm, (int64_t)b * p.C_bs + (int64_t)(t0 + tt) * p.C_ts + n);
+      if (HS) sDhs[i] = p.dhs[((int64_t)b * p.S + t0 + tt) * N + n] * inv_di;
+    }
+    for (int i = tid; i < L * 32; i += NT) {
+      const int tt = i >> 5, cc = cblk * 32 + (i & 31);
+      float d = 0.f, xv = 0.f, dyp = 0.f;
+      if (cc < p.Di) {
+        d = ldf<T>(p.dt, (int64_t)b * p.dt_bs + (int64_t)(t0 + tt) * p.dt_ts + cc);
+        if (SOFTPLUS) d = softplus_f(d);
+        xv = ldf<T>(p.x, (int64_t)b * p.x_bs + (int64_t)(t0 + tt) * p.x_ts + cc);
+        dyp = ldf<T>(p.dy, (int64_t)b * p.dy_bs + (int64_t)(t0 + tt) * p.dy_ts + cc);
+        if (GATE) dyp *= silu_f(ldf<T>(p.z, (int64_t)b * p.z_bs + (int64_t)(t0 + tt) * p.z_ts + cc));
+      }
+      sDt[i] = d; sDtx[i] = d * xv; sX[i] = xv; sDyp[i] = dyp;
+      sY[i] = 0.f; sDU[i] = 0.f; sDD[i] = 0.f;
+    }
+    __syncthreads();
+
+    // ---- phase A: recompute the chunk forward --------------------------------------------
+    {
+      float h[32];
+      const float* src = p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + (cvalid ? c : 0)) * N + w * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) h[j] = cvalid ? src[j] : 0.f;
+      for (int tt = 0; tt < L; ++tt) {
+        if ((tt % SUB) == 0) {
+          float* dst = scratch + (int64_t)(tt / SUB) * 32 * NT;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) dst[j * NT + tid] = h[j];
+        }
+        const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
+        const float* Bt = sB + tt * N + w * 32;
+        const float* Ct = sC + tt * N + w * 32;
+        float yp = 0.f;
+        float tmp[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float a = ex2(sA2[w * 32 + j] * d);
+          h[j] = fmaf(a, h[j], Bt[j] * dxv);
+          yp = fmaf(Ct[j], h[j], yp);
+          tmp[j] = h[j] * dyp;
+        }
+        atomicAdd(&sY[tt * 32 + lane], yp);
+        const float r = reduce_scatter32(tmp, lane);
+        p.dC_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * 32 + lane] = r;
+      }
+    }
+    __syncthreads();
+    // epilogue A: dz and dD
+    for (int i = tid; i < L * 32; i += NT) {
+      const int tt = i >> 5, cl = i & 31, cc = cblk * 32 + cl;
+      if (cc >= p.Di) continue;
+      const float xv = sX[i];
+      atomicAdd(&sDsum[cl], sDyp[i] * xv);
+      if (GATE) {
+        const int64_t off = (int64_t)b * p.z_bs + (int64_t)(t0 + tt) * p.z_ts + cc;
+        const float zv = ldf<T>(p.z, off);
+        const float sg = sigmoid_f(zv);
+        const float yfull = sY[i] + p.D[cc] * xv;
+        const float dyg = ldf<T>(p.dy, (int64_t)b * p.dy_bs + (int64_t)(t0 + tt) * p.dy_ts + cc);
+        const float dz = dyg * yfull * (sg * (1.f + zv * (1.f - sg)));
+        reinterpret_cast<T*>(p.dz)[((int64_t)b * p.S + t0 + tt) * p.Di + cc] = from_f<T>(dz);
+      }
+    }
+
+    // ---- phase B: adjoint over sub-chunks in reverse ---------------------------------------
+    const int nsub = (L + SUB - 1) / SUB;
+    for (int sub = nsub - 1; sub >= 0; --sub) {
+      const int s0 = sub * SUB, s1 = min(s0 + SUB, L);
+      // B1: G recurrence (reverse)
+      for (int tt = s1 - 1; tt >= s0; --tt) {
+        const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
+        const float* Bt = sB + tt * N + w * 32;
+        const float* Ct = sC + tt * N + w * 32;
+        const float* Ht = sDhs + tt * N + w * 32;
+        float du = 0.f;
+        float gb[32];
+        __nv_bfloat16* gdst = sG + (int64_t)(tt - s0) * 32 * NT + tid;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float G = fmaf(Ct[j], dyp, P[j]);
+          if (HS) G += Ht[j];
+          gdst[j * NT] = __float2bfloat16(G);
+          du = fmaf(G, Bt[j], du);
+          gb[j] = G * dxv;
+          P[j] = ex2(sA2[w * 32 + j] * d) * G;
+        }
+        atomicAdd(&sDU[tt * 32 + lane], du);
+        const float r = reduce_scatter32(gb, lane);
+        p.dB_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * 32 + lane] = r;
+      }
+      // B2: recompute h over the sub-chunk and form the decay gradients
+      {
+        float h[32];
+        const float* src = scratch + (int64_t)sub * 32 * NT;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) h[j] = src[j * NT + tid];
+        for (int tt = s0; tt < s1; ++tt) {
+          const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
+          const float* Bt = sB + tt * N + w * 32;
+          const __nv_bfloat16* gsrc = sG + (int64_t)(tt - s0) * 32 * NT + tid;
+          float dd = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float A2j = sA2[w * 32 + j];
+            const float a = ex2(A2j * d);
+            const float v = a * h[j];
+            h[j] = fmaf(Bt[j], dxv, v);
+            const float gv = __bfloat162float(gsrc[j * NT]) * v;
+            dd = fmaf(gv, A2j, dd);
+            dAacc[j] = fmaf(gv, -d, dAacc[j]);
+          }
+          atomicAdd(&sDD[tt * 32 + lane], dd);
+        }
+      }
+    }
+    __syncthreads();
+    // epilogue B: dx, ddt
+    for (int i = tid; i < L * 32; i += NT) {
+      const int tt = i >> 5, cc = cblk * 32 + (i & 31);
+      if (cc >= p.Di) continue;
+      const float d = sDt[i], xv = sX[i], du = sDU[i];
+      float ddt = sDD[i] * LN2 + xv * du;       // decay part uses A2 = -A*log2(e)
+      const float dxo = d * du + p.D[cc] * sDyp[i];
+      if (SOFTPLUS) {
+        const float raw = ldf<T>(p.dt, (int64_t)b * p.dt_bs + (int64_t)(t0 + tt) * p.dt_ts + cc);
+        ddt *= (raw > 20.f) ? 1.f : sigmoid_f(raw);
+      }
+      const int64_t off = ((int64_t)b * p.S + t0 + tt) * p.Di + cc;
+      reinterpret_cast<T*>(p.dx)[off] = from_f<T>(dxo);
+      reinterpret_cast<T*>(p.ddt)[off] = from_f<T>(ddt);
+    }
+  }
+  __syncthreads();
+  {
+    const float r = reduce_scatter32(dAacc, lane);
+    atomicAdd(&p.dA[w * 32 + lane], r);
+  }
+  if (tid < 32 && cvalid) atomicAdd(&p.dD[c], sDsum[tid]);
+}
+
+// ---------------------------------------------------------------------------------------------
+inline size_t fwd_smem(int N) { return (size_t)(2 * CK * N + 3 * CK * 32) * sizeof(float); }
+inline size_t bwd_smem(int N, bool hs) {
+  size_t f = (size_t)(2 * CK * N + (hs ? CK * N : 0) + 7 * CK * 32 + N + 32) * sizeof(float);
+  return f + (size_t)SUB * 32 * N * sizeof(__nv_bfloat16);
+}
+
+template <typename T, int NW, bool SP, bool GATE, bool HS>
+void launch_fwd(const Params& p) {
+  auto k = scan_fwd_kernel<T, NW, SP, GATE, HS>;
+  size_t sm = fwd_smem(NW * 32);
+  MAMF_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  dim3 grid((p.Di + 31) / 32, p.Bsz);
+  k<<<grid, NW * 32, sm, stream()>>>(p);
+  MAMF_LAUNCH_CHECK();
+}
+
+template <typename T, int NW, bool SP, bool GATE, bool HS>
+void launch_bwd(const Params& p) {
+  auto k = scan_bwd_kernel<T, NW, SP, GATE, HS>;
+  size_t sm = bwd_smem(NW * 32, HS);
+  MAMF_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  dim3 grid((p.Di + 31) / 32, p.Bsz);
+  k<<<grid, NW * 32, sm, stream()>>>(p);
+  MAMF_LAUNCH_CHECK();
+}
+
+template <bool FWD, typename T, int NW>
+void dispatch_flags(const Params& p, bool sp, bool gate, bool hs) {
+#define MAMF_SCAN_CASE(SP, GT, H)                                               \
+  if (sp == SP && gate == GT && hs == H) {                                      \
+    if (FWD) launch_fwd<T, NW, SP, GT, H>(p); else launch_bwd<T, NW, SP, GT, H>(p); \
+    return;                                                                     \
+  }
+  MAMF_SCAN_CASE(true, true, true) MAMF_SCAN_CASE(true, true, false)
+  MAMF_SCAN_CASE(false, false, true) MAMF_SCAN_CASE(false, false, false)
+#undef MAMF_SCAN_CASE
+  TORCH_CHECK(false, "selective scan: unsupported flag combination (softplus and gate go together)");
+}
+
+template <bool FWD, typename T>
+void dispatch_nw(const Params& p, bool sp, bool gate, bool hs) {
+  switch (p.N) {
+    case 32: dispatch_flags<FWD, T, 1>(p, sp, gate, hs); break;
+    case 64: dispatch_flags<FWD, T, 2>(p, sp, gate, hs); break;
+    case 128: dispatch_flags<FWD, T, 4>(p, sp, gate, hs); break;
+    default: TORCH_CHECK(false, "selective scan: d_state must be 32, 64 or 128, got ", p.N);
+  }
+}
+
+}  // namespace scan
+
+// Python-facing entry points --------------------------------------------------------------------
+using scan::Params;
+
+static void fill_common(Params& p, const at::Tensor& x, const at::Tensor& dt, const at::Tensor& Bm,
+                        const at::Tensor& Cm, const c10::optional<at::Tensor>& z,
+                        const at::Tensor& A_log, const at::Tensor& D) {
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && dt.stride(2) == 1 && Bm.stride(2) == 1 && Cm.stride(2) == 1,
+              "selective scan: inputs must be (B, S, C) with unit inner stride");
+  p.Bsz = x.size(0); p.S = x.size(1); p.Di = x.size(2); p.N = Bm.size(2);
+  TORCH_CHECK(A_log.numel() == p.N && D.numel() == p.Di && A_log.dtype() == at::kFloat && D.dtype() == at::kFloat,
+              "selective scan: A_log (N,) and D (Di,) must be fp32");
+  p.G = (p.Di + 31) / 32;
+  p.nck = (p.S + scan::CK - 1) / scan::CK;
+  p.x = x.data_ptr(); p.x_bs = x.stride(0); p.x_ts = x.stride(1);
+  p.dt = dt.data_ptr(); p.dt_bs = dt.stride(0); p.dt_ts = dt.stride(1);
+  p.Bm = Bm.data_ptr(); p.B_bs = Bm.stride(0); p.B_ts = Bm.stride(1);
+  p.Cm = Cm.data_ptr(); p.C_bs = Cm.stride(0); p.C_ts = Cm.stride(1);
+  if (z.has_value()) {
+    TORCH_CHECK(z->stride(2) == 1, "selective scan: z needs unit inner stride");
+    p.z = z->data_ptr(); p.z_bs = z->stride(0); p.z_ts = z->stride(1);
+  } else {
+    p.z = nullptr; p.z_bs = p.z_ts = 0;
+  }
+  p.A_log = A_log.data_ptr<float>();
+  p.D = D.data_ptr<float>();
+}
+
+// Returns (y, hs or empty, ckpt, final or empty)
+std::vector<at::Tensor> selective_scan_fwd(at::Tensor x, at::Tensor dt, at::Tensor A_log, at::Tensor Bm,
+                                           at::Tensor Cm, at::Tensor D, c10::optional<at::Tensor> z,
+                                           c10::optional<at::Tensor> h0, bool softplus, bool need_hs,
+                                           bool need_final) {
+  c10::cuda::CUDAGuard g(x.device());
+  Params p{};
+  fill_common(p, x, dt, Bm, Cm, z, A_log, D);
+  auto f32 = x.options().dtype(at::kFloat);
+  at::Tensor y = at::empty({p.Bsz, p.S, p.Di}, x.options());
+  at::Tensor ckpt = at::empty({p.Bsz, p.nck, p.Di, p.N}, f32);
+  at::Tensor part, fin;
+  p.y = y.data_ptr(); p.y_bs = y.stride(0); p.y_ts = y.stride(1);
+  p.ckpt = ckpt.data_ptr<float>();
+  if (need_hs) { part = at::empty({p.Bsz, p.G, p.S, p.N}, f32); p.hs_part = part.data_ptr<float>(); }
+  if (need_final) { fin = at::empty({p.Bsz, p.Di, p.N}, f32); p.final_state = fin.data_ptr<float>(); }
+  at::Tensor h0c;
+  if (h0.has_value()) { h0c = h0->to(at::kFloat).contiguous(); p.h0 = h0c.data_ptr<float>(); }
+  if (x.scalar_type() == at::kBFloat16) scan::dispatch_nw<true, __nv_bfloat16>(p, softplus, z.has_value(), need_hs);
+  else if (x.scalar_type() == at::kFloat) scan::dispatch_nw<true, float>(p, softplus, z.has_value(), need_hs);
+  else TORCH_CHECK(false, "selective scan: bf16 or fp32 inputs");
+  at::Tensor hs;
+  if (need_hs) hs = part.sum(1).div_((double)p.Di);
+  return {y, hs, ckpt, fin};
+}
+
+// Returns (dx, ddt, dB, dC, dz or empty, dA (N,), dD (Di,))
+std::vector<at::Tensor> selective_scan_bwd(at::Tensor x, at::Tensor dt, at::Tensor A_log, at::Tensor Bm,
+                                           at::Tensor Cm, at::Tensor D, c10::optional<at::Tensor> z,
+                                           at::Tensor ckpt, at::Tensor dy, c10::optional<at::Tensor> dhs,
+                                           bool softplus) {
+  c10::cuda::CUDAGuard g(x.device());
+  Params p{};
+  fill_common(p, x, dt, Bm, Cm, z, A_log, D);
+  TORCH_CHECK(dy.stride(2) == 1, "selective scan bwd: dy needs unit inner stride");
+  auto f32 = x.options().dtype(at::kFloat);
+  p.ckpt = ckpt.data_ptr<float>();
+  p.dy = dy.data_ptr(); p.dy_bs = dy.stride(0); p.dy_ts = dy.stride(1);
+  at::Tensor dhs_c;
+  if (dhs.has_value()) { dhs_c = dhs->to(at::kFloat).contiguous(); p.dhs = dhs_c.data_ptr<float>(); }
+  at::Tensor dx = at::empty({p.Bsz, p.S, p.Di}, x.options());
+  at::Tensor ddt = at::empty({p.Bsz, p.S, p.Di}, x.options());
+  at::Tensor dz;
+  if (z.has_value()) { dz = at::empty({p.Bsz, p.S, p.Di}, x.options()); p.dz = dz.data_ptr(); }
+  at::Tensor dBp = at::empty({p.Bsz, p.G, p.S, p.N}, f32);
+  at::Tensor dCp = at::empty({p.Bsz, p.G, p.S, p.N}, f32);
+  at::Tensor dA = at::zeros({p.N}, f32);
+  at::Tensor dD = at::zeros({p.Di}, f32);
+  at::Tensor scratch = at::empty({(int64_t)p.Bsz * p.G * (scan::CK / scan::SUB) * 32 * p.N}, f32);
+  p.dx = dx.data_ptr(); p.ddt = ddt.data_ptr();
+  p.dB_part = dBp.data_ptr<float>(); p.dC_part = dCp.data_ptr<float>();
+  p.dA = dA.data_ptr<float>(); p.dD = dD.data_ptr<float>();
+  p.scratch = scratch.data_ptr<float>();
+  if (x.scalar_type() == at::kBFloat16) scan::dispatch_nw<false, __nv_bfloat16>(p, softplus, z.has_value(), dhs.has_value());
+  else if (x.scalar_type() == at::kFloat) scan::dispatch_nw<false, float>(p, softplus, z.has_value(), dhs.has_value());
+  else TORCH_CHECK(false, "selective scan: bf16 or fp32 inputs");
+  return {dx, ddt, dBp.sum(1), dCp.sum(1), dz, dA, dD};
+}
+
+}  // namespace mamf

@@ -1,0 +1,106 @@
+"""Training engine: one optimizer step over gradient-accumulated micro-batches.
+
+Reference loop: ``scripts/train.py:363-462`` (micro-batch forward, loss / grad_accum backward,
+NaN/Inf skip, clip 1.0, AdamW step, scheduler step).  Here:
+
+* the model runs in the bf16 compute layout with fp32 masters in ``MixedPrecisionAdamW``;
+* ``return_logits=False`` so the main and MTP losses use the fused linear-cross-entropy path;
+* the step never synchronises with the host unless asked (``sync_loss=True``): the loss is
+  accumulated on the device and the clip factor is computed on the device;
+* with ``sync_loss=True`` the step reads the loss back and, like the reference, skips the
+  update when it is not finite.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from mamformer_b200.models.model import MamformerForCausalLM
+from mamformer_b200.optim import MixedPrecisionAdamW, create_lr_scheduler, param_groups
+from mamformer_b200.utils.precision import to_compute_dtype
+
+
+@dataclass
+class TrainConfig:
+    learning_rate: float = 3e-4
+    weight_decay: float = 0.1
+    adam_beta1: float = 0.9
+    adam_beta2: float = 0.95
+    adam_epsilon: float = 1e-8
+    warmup_steps: int = 2000
+    max_steps: int = 100000
+    min_lr_ratio: float = 0.1
+    max_grad_norm: float = 1.0
+    micro_batch: int = 1
+    grad_accum: int = 1
+    compute_dtype: torch.dtype = torch.bfloat16
+    gradient_checkpointing: bool = False
+
+
+class Trainer:
+    """Owns model + optimizer + schedule; ``train_step`` is the public per-step API."""
+
+    def __init__(self, model: MamformerForCausalLM, cfg: TrainConfig,
+                 dp_group: Optional[dist.ProcessGroup] = None, expert_params=None):
+        self.cfg = cfg
+        self.model = model
+        if cfg.compute_dtype != torch.float32:
+            to_compute_dtype(model, cfg.compute_dtype)
+        model.return_logits = False
+        model.train()
+        if cfg.gradient_checkpointing:
+            model.model.enable_gradient_checkpointing()
+        self.optimizer = MixedPrecisionAdamW(
+            param_groups(model, cfg.weight_decay), lr=cfg.learning_rate,
+            betas=(cfg.adam_beta1, cfg.adam_beta2), eps=cfg.adam_epsilon,
+            weight_decay=cfg.weight_decay, max_grad_norm=cfg.max_grad_norm, dp_group=dp_group,
+            no_dp_reduce=expert_params)
+        self.scheduler = create_lr_scheduler(self.optimizer, cfg.warmup_steps, cfg.max_steps,
+                                             cfg.learning_rate, cfg.min_lr_ratio)
+        dev = next(model.parameters()).device
+        self.device = dev
+        self._loss_acc = torch.zeros((), device=dev)
+        self.step_count = 0
+        self.skipped_steps = 0
+
+    def train_step(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
+                   sync_loss: bool = False):
+        """One optimizer step.  ``input_ids`` (micro_batch*grad_accum, S) on the device or in
+        (pinned) host memory.  Returns the mean loss (device tensor, or float if sync_loss)."""
+        cfg = self.cfg
+        if not input_ids.is_cuda and self.device.type == "cuda":
+            input_ids = input_ids.to(self.device, non_blocking=True)
+            if labels is not None:
+                labels = labels.to(self.device, non_blocking=True)
+        labels = input_ids if labels is None else labels
+        n_micro = max(1, input_ids.shape[0] // cfg.micro_batch)
+        self.optimizer.zero_grad()
+        self._loss_acc.zero_()
+        for i in range(n_micro):
+            sl = slice(i * cfg.micro_batch, (i + 1) * cfg.micro_batch)
+            out = self.model(input_ids[sl], labels=labels[sl])
+            loss = out["loss"]
+            (loss / n_micro).backward()
+            self._loss_acc += loss.detach().float() / n_micro
+        loss_val = None
+        if sync_loss:
+            loss_val = float(self._loss_acc)
+            if loss_val != loss_val or loss_val in (float("inf"), float("-inf")):
+                # non-finite loss: skip the update (reference train.py:406-432)
+                self.skipped_steps += 1
+                self.optimizer.zero_grad()
+                return loss_val
+        self.optimizer.step()
+        self.scheduler.step()
+        self.step_count += 1
+        return loss_val if sync_loss else self._loss_acc
+
+
+def build_trainer(config, train_cfg: TrainConfig, device="cuda", seed: int = 0, dp_group=None):
+    torch.manual_seed(seed)
+    model = MamformerForCausalLM(config).to(device)
+    return Trainer(model, train_cfg, dp_group=dp_group)

@@ -1,0 +1,186 @@
+"""Autograd wrappers around the native kernels in ``mamformer_b200._C``.
+
+Importing this module registers the covered op names in ``ops.NATIVE``.  Each wrapper keeps
+the tensors its backward kernel needs and nothing else (e.g. the scan saves chunk-start
+states, not per-step states).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from mamformer_b200.ops import NATIVE
+from mamformer_b200.ops._ext import require_native
+
+_C = require_native()
+
+
+def _register(name: str, source: str):
+    def deco(fn):
+        NATIVE[name] = source
+        return fn
+    return deco
+
+
+# ---------------------------------------------------------------------------------------------
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        shape = x.shape
+        x2 = x.contiguous()
+        y, rstd = _C.rmsnorm_fwd(x2, w.float().contiguous(), float(eps))
+        ctx.save_for_backward(x2, w, rstd)
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dx, dw = _C.rmsnorm_bwd(x, w.float().contiguous(), dy.contiguous(), rstd)
+        return dx.view(dy.shape), dw.to(w.dtype), None
+
+
+@_register("rms_norm", "csrc/elementwise.cu")
+def rms_norm(x, weight, eps):
+    return _RMSNorm.apply(x, weight, eps)
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, g, u):
+        ctx.save_for_backward(g, u)
+        return _C.swiglu_fwd(g, u)
+
+    @staticmethod
+    def backward(ctx, dy):
+        g, u = ctx.saved_tensors
+        dg, du = _C.swiglu_bwd(g, u, dy)
+        return dg, du
+
+
+@_register("swiglu", "csrc/elementwise.cu")
+def swiglu(gate, up):
+    if gate.shape[-1] * gate.element_size() % 16 or up.stride(-1) != 1 or gate.stride(-1) != 1:
+        from mamformer_b200.ops import reference
+        return reference.swiglu(gate, up)
+    return _SwiGLU.apply(gate, up)
+
+
+class _Rope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, cos, sin):
+        ctx.save_for_backward(cos, sin)
+        return _C.rope_apply(x, cos, sin, False)
+
+    @staticmethod
+    def backward(ctx, dy):
+        cos, sin = ctx.saved_tensors
+        return _C.rope_apply(dy.contiguous(), cos, sin, True), None, None
+
+
+@_register("rope", "csrc/elementwise.cu")
+def rope(x, cos, sin):
+    if x.stride(-1) != 1 or x.stride(-2) != x.shape[-1] or x.stride(0) != x.stride(1) * x.shape[1]:
+        x = x.contiguous()
+    return _Rope.apply(x, cos, sin)
+
+
+class _ConvSiLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w):
+        ctx.save_for_backward(x, w)
+        return _C.conv_silu_fwd(x, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dx, dw = _C.conv_silu_bwd(x, w, dy)
+        return dx, dw.to(w.dtype)
+
+
+@_register("causal_conv1d_silu", "csrc/elementwise.cu")
+def causal_conv1d_silu(x, weight):
+    return _ConvSiLU.apply(x, weight)
+
+
+class _HeadGroupNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, H, w, b, eps):
+        x = x.contiguous()
+        y, mr = _C.head_groupnorm_fwd(x, int(H), w, b, float(eps))
+        ctx.save_for_backward(x, w, mr)
+        ctx.H = int(H)
+        ctx.wdt = (w.dtype, b.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, mr = ctx.saved_tensors
+        dx, dw, db = _C.head_groupnorm_bwd(x, ctx.H, w, mr, dy.contiguous())
+        return dx, None, dw.to(ctx.wdt[0]), db.to(ctx.wdt[1]), None
+
+
+@_register("head_group_norm", "csrc/elementwise.cu")
+def head_group_norm(x, n_heads, weight, bias, eps):
+    return _HeadGroupNorm.apply(x, n_heads, weight, bias, eps)
+
+
+# ---------------------------------------------------------------------------------------------
+class _Scan(torch.autograd.Function):
+    """Outputs (y, h_states-or-None, final-or-None); gradients for x, dt, A_log, B, C, D, z."""
+
+    @staticmethod
+    def forward(ctx, x, dt, A_log, Bm, Cm, D, z, softplus, need_hs, need_final):
+        A32 = A_log.float().contiguous()
+        D32 = D.float().contiguous()
+        y, hs, ckpt, fin = _C.selective_scan_fwd(x, dt, A32, Bm, Cm, D32, z, None, softplus,
+                                                 need_hs, need_final)
+        ctx.save_for_backward(x, dt, A_log, Bm, Cm, D, z if z is not None else x.new_empty(0), ckpt)
+        ctx.has_z = z is not None
+        ctx.softplus = softplus
+        ctx.need_hs = need_hs
+        if need_final:
+            ctx.mark_non_differentiable(fin)
+        return y, (hs if need_hs else None), (fin if need_final else None)
+
+    @staticmethod
+    def backward(ctx, dy, dhs, dfin):
+        x, dt, A_log, Bm, Cm, D, z, ckpt = ctx.saved_tensors
+        z = z if ctx.has_z else None
+        if dy is None:
+            dy = torch.zeros_like(x)
+        dhs_in = dhs if (ctx.need_hs and dhs is not None) else None
+        dx, ddt, dB, dC, dz, dA, dD = _C.selective_scan_bwd(
+            x, dt, A_log.float().contiguous(), Bm, Cm, D.float().contiguous(), z, ckpt,
+            dy.contiguous(), dhs_in, ctx.softplus)
+        al = A_log.float()
+        dA_log = dA * torch.exp(al.clamp(-5.0, 5.0)) * ((al > -5.0) & (al < 5.0)).float()
+        return (dx, ddt, dA_log.to(A_log.dtype), dB.to(Bm.dtype), dC.to(Cm.dtype), dD.to(D.dtype),
+                dz if ctx.has_z else None, None, None, None)
+
+
+def _scan_ok(x, N):
+    return N in (32, 64, 128) and x.dtype in (torch.float32, torch.bfloat16)
+
+
+@_register("mamba_inner", "csrc/selective_scan.cu")
+def mamba_inner(x_act, dt_raw, A_log, Bm, Cm, D, z, need_h_states, return_final=False):
+    if not _scan_ok(x_act, Bm.shape[-1]):
+        from mamformer_b200.ops import reference
+        return reference.mamba_inner(x_act, dt_raw, A_log, Bm, Cm, D, z, need_h_states, return_final=return_final)
+    dt_raw = dt_raw if dt_raw.stride(-1) == 1 else dt_raw.contiguous()
+    y, hs, fin = _Scan.apply(x_act, dt_raw, A_log, Bm, Cm, D, z, True, need_h_states, return_final)
+    return y, hs, fin
+
+
+@_register("selective_scan", "csrc/selective_scan.cu")
+def selective_scan(x, dt, A_log, B, C, D, return_h_states=False, return_final_state=False):
+    if not _scan_ok(x, B.shape[-1]):
+        from mamformer_b200.ops import reference
+        return reference.selective_scan(x, dt, A_log, B, C, D, return_h_states, return_final_state)
+    y, hs, fin = _Scan.apply(x, dt, A_log, B, C, D, None, False, return_h_states, return_final_state)
+    out = [y]
+    if return_h_states:
+        out.append(hs)
+    if return_final_state:
+        out.append(fin)
+    return out[0] if len(out) == 1 else tuple(out)

@@ -1,0 +1,227 @@
+"""Mixed-precision AdamW over flat buffers, parameter groups and the LR schedule.
+
+Reference behaviour kept (``scripts/train.py:134-164, 255-277``):
+
+* AdamW, betas (0.9, 0.95), eps 1e-8, weight decay 0.1 except for parameters whose name
+  contains ``norm``, ``bias``, ``gate``, ``alpha``, ``lambda_log`` or ``A_log`` (GRPO also
+  exempts ``comm_strength``).  ``gate`` also matches every ``gate_proj``, so those get no decay,
+  exactly as in the reference;
+* LinearLR warm-up from 0.01x, then cosine decay to ``min_lr_ratio`` x peak, stepped once
+  per optimizer step; gradient clipping at 1.0.
+
+B200 design:
+
+* model matrices live in flat bf16 buffers (parameters are views into them); fp32 master
+  weights, fp32 gradients and the two moments live in flat fp32 buffers, segmented by
+  (master kind, weight decay, data-parallel reduction) - one fused kernel launch per segment
+  updates master, moments and the bf16 copy in a single pass;
+* every gradient is added into the fp32 gradient buffer by a post-accumulate hook
+  (micro-batch accumulation in fp32) and the autograd copy is released;
+* the gradient norm is reduced on the device and the clip factor is read by the update
+  kernel from device memory: no host synchronisation in ``step``;
+* data parallelism: gradient segments that are replicated across the data-parallel group are
+  all-reduced (NCCL) before the norm; expert-parallel segments are not (each rank owns its
+  experts and already holds the sum over every rank's tokens).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+from torch.optim.lr_scheduler import CosineAnnealingLR, LinearLR, SequentialLR
+
+NO_DECAY_KEYS = ("norm", "bias", "gate", "alpha", "lambda_log", "A_log")
+_ALIGN = 64   # elements; keeps every parameter 256-byte aligned in fp32
+
+
+def is_no_decay(name: str, extra: Tuple[str, ...] = ()) -> bool:
+    return any(k in name for k in NO_DECAY_KEYS + tuple(extra))
+
+
+def param_groups(model: torch.nn.Module, weight_decay: float = 0.1,
+                 extra_no_decay: Tuple[str, ...] = ()) -> List[dict]:
+    decay, no_decay = [], []
+    for name, p in model.named_parameters():
+        if not p.requires_grad:
+            continue
+        (no_decay if is_no_decay(name, extra_no_decay) else decay).append(p)
+    return [{"params": decay, "weight_decay": weight_decay},
+            {"params": no_decay, "weight_decay": 0.0}]
+
+
+def create_lr_scheduler(optimizer, warmup_steps: int = 2000, max_steps: int = 100000,
+                        learning_rate: float = 3e-4, min_lr_ratio: float = 0.1):
+    warmup_steps = max(1, int(warmup_steps))
+    warm = LinearLR(optimizer, start_factor=0.01, end_factor=1.0, total_iters=warmup_steps)
+    cos = CosineAnnealingLR(optimizer, T_max=max(1, max_steps - warmup_steps),
+                            eta_min=learning_rate * min_lr_ratio)
+    return SequentialLR(optimizer, schedulers=[warm, cos], milestones=[warmup_steps])
+
+
+def _native():
+    from mamformer_b200.ops._ext import ext
+    return ext()
+
+
+class _Segment:
+    """One flat run of parameters sharing (master kind, decay, dp reduction)."""
+
+    def __init__(self, params: List[torch.nn.Parameter], wd: float, dp_reduce: bool, device,
+                 world: int):
+        self.params = params
+        self.wd = wd
+        self.dp_reduce = dp_reduce
+        self.low = params[0].dtype != torch.float32
+        self.offsets = []
+        off = 0
+        for p in params:
+            self.offsets.append(off)
+            off += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
+        pad = _ALIGN * max(1, world)
+        self.numel = max(pad, (off + pad - 1) // pad * pad)
+        f32 = dict(device=device, dtype=torch.float32)
+        self.master = torch.zeros(self.numel, **f32)
+        self.grad = torch.zeros(self.numel, **f32)
+        self.m = torch.zeros(self.numel, **f32)
+        self.v = torch.zeros(self.numel, **f32)
+        self.low_flat = torch.zeros(self.numel, device=device, dtype=params[0].dtype) if self.low else None
+        with torch.no_grad():
+            for p, o in zip(params, self.offsets):
+                n = p.numel()
+                self.master[o:o + n].copy_(p.detach().reshape(-1).float())
+                if self.low:
+                    self.low_flat[o:o + n].copy_(p.detach().reshape(-1))
+                    p.data = self.low_flat[o:o + n].view_as(p)
+                else:
+                    p.data = self.master[o:o + n].view_as(p)
+                p.main_grad = self.grad[o:o + n].view_as(p)
+
+
+class MixedPrecisionAdamW(torch.optim.Optimizer):
+    def __init__(self, params, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
+                 weight_decay: float = 0.1, max_grad_norm: float = 1.0,
+                 dp_group: Optional[dist.ProcessGroup] = None, no_dp_reduce=None):
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        self.max_grad_norm = max_grad_norm
+        self.dp_group = dp_group
+        self.world = dist.get_world_size(dp_group) if (dp_group is not None and dist.is_initialized()) else 1
+        skip = set(id(p) for p in (no_dp_reduce or []))
+        dev = self.param_groups[0]["params"][0].device
+        self.segments: List[Tuple[int, _Segment]] = []
+        for gi, g in enumerate(self.param_groups):
+            buckets: Dict[tuple, list] = {}
+            for p in g["params"]:
+                buckets.setdefault((p.dtype, id(p) not in skip), []).append(p)
+            for (dt, red), ps in buckets.items():
+                self.segments.append((gi, _Segment(ps, g["weight_decay"], red and self.world > 1, dev, self.world)))
+        self._hooks = [p.register_post_accumulate_grad_hook(_accumulate_grad)
+                       for _, seg in self.segments for p in seg.params]
+        self._sq = torch.zeros(1, device=dev)
+        self._scale = torch.ones(1, device=dev)
+        self.last_grad_norm = torch.zeros(1, device=dev)
+        self._step = 0
+
+    # -- gradients -------------------------------------------------------------------------
+    def zero_grad(self, set_to_none: bool = True):
+        for _, seg in self.segments:
+            seg.grad.zero_()
+            for p in seg.params:
+                p.grad = None
+
+    def reduce_gradients(self, async_op: bool = False):
+        """Sum replicated-gradient segments over the data-parallel group."""
+        works = []
+        for _, seg in self.segments:
+            if seg.dp_reduce:
+                works.append(dist.all_reduce(seg.grad, group=self.dp_group, async_op=async_op))
+        return works
+
+    @torch.no_grad()
+    def step(self, closure=None, reduce: bool = True):
+        if reduce and self.world > 1:
+            self.reduce_gradients()
+        C = _native()
+        self._step += 1
+        self._sq.zero_()
+        use_native = C is not None and self._sq.is_cuda
+        # Both kinds of segment hold sum_r dL_r/dtheta (replicated ones after the all-reduce,
+        # expert-parallel ones because dispatch brought every rank's tokens to the owner), so
+        # both are scaled by 1/world.  Replicated segments are identical on every rank; the
+        # expert-parallel part of the squared norm is summed over ranks.
+        sq_ep = torch.zeros_like(self._sq) if self.world > 1 else None
+        for _, seg in self.segments:
+            acc = sq_ep if (sq_ep is not None and not seg.dp_reduce) else self._sq
+            if use_native:
+                C.sq_norm_accumulate(seg.grad, acc)
+            else:
+                acc += seg.grad.pow(2).sum()
+        if sq_ep is not None:
+            dist.all_reduce(sq_ep, group=self.dp_group)
+            self._sq += sq_ep
+        if use_native:
+            C.clip_scale(self._sq, self._scale, float(self.max_grad_norm or 0.0), 1.0 / self.world,
+                         self.last_grad_norm)
+        else:
+            nrm = self._sq.sqrt() / self.world
+            s = 1.0 / self.world
+            if self.max_grad_norm and float(nrm) > self.max_grad_norm:
+                s *= self.max_grad_norm / (float(nrm) + 1e-6)
+            self._scale.fill_(s)
+            self.last_grad_norm.copy_(nrm)
+        for gi, seg in self.segments:
+            grp = self.param_groups[gi]
+            b1, b2 = grp["betas"]
+            if use_native:
+                C.adamw_step(seg.master, seg.grad, seg.m, seg.v, seg.low_flat, float(grp["lr"]), b1, b2,
+                             grp["eps"], seg.wd, self._step, self._scale)
+            else:
+                _adamw_torch(seg, grp["lr"], b1, b2, grp["eps"], seg.wd, self._step, self._scale)
+        return None
+
+    def grad_norm(self) -> torch.Tensor:
+        return self.last_grad_norm
+
+    # -- checkpointing ---------------------------------------------------------------------
+    def state_dict(self):
+        return {"step": self._step,
+                "segments": [{"master": s.master.cpu(), "m": s.m.cpu(), "v": s.v.cpu()} for _, s in self.segments],
+                "param_groups": [{k: v for k, v in g.items() if k != "params"} for g in self.param_groups]}
+
+    def load_state_dict(self, state):
+        self._step = int(state["step"])
+        for (_, seg), st in zip(self.segments, state["segments"]):
+            seg.master.copy_(st["master"])
+            seg.m.copy_(st["m"])
+            seg.v.copy_(st["v"])
+            if seg.low:
+                seg.low_flat.copy_(seg.master)
+        for g, sg in zip(self.param_groups, state["param_groups"]):
+            g.update({k: v for k, v in sg.items() if k in ("lr", "betas", "eps", "weight_decay", "initial_lr")})
+
+
+def _accumulate_grad(p: torch.Tensor) -> None:
+    g = p.grad
+    if g is None:
+        return
+    C = _native()
+    if C is not None and g.is_cuda:
+        C.grad_accumulate(p.main_grad, g.contiguous())
+    else:
+        p.main_grad.add_(g.float())
+    p.grad = None
+
+
+def _adamw_torch(seg: _Segment, lr, b1, b2, eps, wd, step, scale):
+    g = seg.grad * scale
+    seg.m.mul_(b1).add_(g, alpha=1 - b1)
+    seg.v.mul_(b2).addcmul_(g, g, value=1 - b2)
+    bc1 = 1 - b1 ** step
+    bc2 = 1 - b2 ** step
+    seg.master.mul_(1 - lr * wd)
+    seg.master.addcdiv_(seg.m, (seg.v.sqrt() / math.sqrt(bc2)).add_(eps), value=-lr / bc1)
+    if seg.low:
+        seg.low_flat.copy_(seg.master)

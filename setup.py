@@ -1,0 +1,43 @@
+"""Build the native sm_100a extension in-tree:  python setup.py build_ext --inplace
+
+Every .cu/.cpp under mamformer_b200/csrc is compiled for sm_100a only
+(-gencode arch=compute_100a,code=sm_100a); the resulting mamformer_b200/_C*.so is loaded by
+mamformer_b200.ops.
+"""
+
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("mamformer_b200", "csrc")
+
+NVCC_FLAGS = [
+    "-O3", "-lineinfo", "-std=c++17",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "--expt-relaxed-constexpr", "--expt-extended-lambda",
+    "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_BFLOAT16_OPERATORS__",
+    "-DNDEBUG",
+]
+if os.environ.get("MAMF_BOUNDS_CHECK") == "1":
+    NVCC_FLAGS.append("-DMAMF_BOUNDS_CHECK=1")
+
+sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
+
+setup(
+    name="mamformer_b200",
+    version="0.1.0",
+    packages=["mamformer_b200"],
+    ext_modules=[
+        CUDAExtension(
+            name="mamformer_b200._C",
+            sources=sources,
+            include_dirs=[os.path.join(HERE, CSRC)],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)
