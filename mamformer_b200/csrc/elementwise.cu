@@ -572,3 +572,89 @@ std::vector<at::Tensor> head_groupnorm_bwd(at::Tensor x, int64_t H, at::Tensor w
 }
 
 }  // namespace mamf
+
+// ============================ allocation-free GroupNorm forward ==============================
+// See noalloc.h: same kernels as head_groupnorm_fwd, scratch in a fixed device array.
+#include <mutex>
+#include <stdio.h>
+
+#include "noalloc.h"
+
+namespace mamf {
+namespace noalloc {
+
+static __device__ __align__(256) float g_scratch[MAMF_NOALLOC_SCRATCH_FLOATS];
+
+constexpr int kMaxDevices = 64;
+static float* g_scratch_addr[kMaxDevices];    // device address of g_scratch, per device
+static std::mutex g_setup_mutex;
+static thread_local char g_msg[256] = "";
+
+static int fail(int code, const char* msg) {
+  snprintf(g_msg, sizeof(g_msg), "%s", msg);
+  return code;
+}
+
+// Device address of the scratch array on the current device (looked up once per device).
+static int scratch_address(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(3, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(1, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_scratch);
+    if (e != cudaSuccess) return fail(3, cudaGetErrorString(e));
+    g_scratch_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return 0;
+}
+
+}  // namespace noalloc
+}  // namespace mamf
+
+extern "C" __attribute__((visibility("default")))
+const char* mamf_noalloc_last_error(void) { return mamf::noalloc::g_msg; }
+
+extern "C" __attribute__((visibility("default")))
+int mamf_head_groupnorm_fwd_noalloc(const void* x, const float* w, const float* b, void* y,
+                                    float* mean_rstd_out, int64_t B, int64_t S, int64_t H, int64_t hd,
+                                    float eps, int dtype, void* stream_ptr) {
+  using namespace mamf;
+  if (!x || !w || !b || !y || B <= 0 || S <= 0 || H <= 0 || hd <= 0 || (dtype != 0 && dtype != 1))
+    return noalloc::fail(1, "invalid arguments");
+  const int64_t tiles = (S + GN_ROWS - 1) / GN_ROWS;
+  const int64_t part_floats = B * H * tiles * 3;
+  const int64_t mr_floats = mean_rstd_out ? 0 : 2 * B * H;
+  if (part_floats + mr_floats > MAMF_NOALLOC_SCRATCH_FLOATS) {
+    char buf[200];
+    snprintf(buf, sizeof(buf), "problem needs %lld scratch floats, the fixed array holds %d",
+             (long long)(part_floats + mr_floats), MAMF_NOALLOC_SCRATCH_FLOATS);
+    return noalloc::fail(2, buf);
+  }
+  float* scratch = nullptr;
+  if (int rc = noalloc::scratch_address(&scratch)) return rc;
+  float* part = scratch;
+  float* mr = mean_rstd_out ? mean_rstd_out : scratch + part_floats;
+  cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
+  const int Bi = (int)B, Si = (int)S, Hi = (int)H, hdi = (int)hd;
+  const int64_t numel = B * S * H * hd;
+  dim3 sgrid((unsigned)tiles, (unsigned)H, (unsigned)B), sblock((unsigned)std::min<int64_t>(hd, 128), 4);
+  if (dtype == 1) {
+    gn_stats_kernel<__nv_bfloat16><<<sgrid, sblock, 0, st>>>((const __nv_bfloat16*)x, part, Si, Hi, hdi);
+  } else {
+    gn_stats_kernel<float><<<sgrid, sblock, 0, st>>>((const float*)x, part, Si, Hi, hdi);
+  }
+  gn_finalize_kernel<<<(unsigned)((B * H + 127) / 128), 128, 0, st>>>(part, mr, Bi * Hi, (int)tiles, eps);
+  if (dtype == 1) {
+    gn_apply_kernel<__nv_bfloat16><<<ew_blocks(numel), 256, 0, st>>>(
+        (const __nv_bfloat16*)x, mr, w, b, (__nv_bfloat16*)y, B * S, Si, Hi, hdi);
+  } else {
+    gn_apply_kernel<float><<<ew_blocks(numel), 256, 0, st>>>((const float*)x, mr, w, b, (float*)y, B * S, Si, Hi, hdi);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return noalloc::fail(3, cudaGetErrorString(e));
+  return 0;
+}
