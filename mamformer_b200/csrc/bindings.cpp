@@ -31,6 +31,9 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
              c10::optional<at::Tensor> seg, c10::optional<at::Tensor> tile_off, int64_t mode, double alpha);
 int64_t gemm_error();
 void gemm_clear_error();
+void ce_stats(at::Tensor logits, at::Tensor labels, int64_t ignore_index, at::Tensor loss, at::Tensor lse);
+void ce_grad_inplace(at::Tensor logits, at::Tensor labels, int64_t ignore_index, at::Tensor lse,
+                     at::Tensor scale, at::Tensor n_valid);
 }  // namespace mamf
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -53,4 +56,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn", &mamf::gemm_tn);
   m.def("gemm_error", &mamf::gemm_error);
   m.def("gemm_clear_error", &mamf::gemm_clear_error);
+  m.def("ce_stats", &mamf::ce_stats);
+  m.def("ce_grad_inplace", &mamf::ce_grad_inplace);
 }

@@ -476,11 +476,16 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
     p.d_gstride = D.stride(0);
   }
   p.M = M; p.N = N; p.K = K;
-  TORCH_CHECK(K % 8 == 0 && N % 8 == 0 && M % 8 == 0, "gemm: M, N and K must be multiples of 8");
+  // TMA needs the contiguous (innermost) dimension of every operand to be 16-byte aligned
+  TORCH_CHECK((a_mn && b_mn) || K % 8 == 0, "gemm: K must be a multiple of 8 for K-major operands");
+  TORCH_CHECK(!a_mn || M % 8 == 0, "gemm: M must be a multiple of 8 for an MN-major A");
+  TORCH_CHECK(!b_mn || N % 8 == 0, "gemm: N must be a multiple of 8 for an MN-major B");
   const int64_t esz_d = D.element_size();
   TORCH_CHECK(aligned16(D.data_ptr()) && (p.ldd * esz_d) % 16 == 0 && (p.d_gstride * esz_d) % 16 == 0,
               "gemm: D must be 16-byte aligned with 16-byte-multiple row strides");
-  const int bn = (N >= 256 && mode != 2) ? 256 : 128;
+  // tile width: the one that pads N least (ties -> 256); grouped-K keeps 128 (more tiles per group)
+  const int pad128 = (N + 127) / 128 * 128, pad256 = (N + 255) / 256 * 256;
+  const int bn = (mode != 2 && N >= 256 && pad256 <= pad128) ? 256 : 128;
   p.n_tiles_n = (N + bn - 1) / bn;
   if (!a_mn) {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, st[1] = {(uint64_t)A.stride(0) * esz};

@@ -179,13 +179,7 @@ def moe_expert_outputs(x, idx, w_gate, w_up, w_down):
     """Unweighted per-slot expert outputs (T, k, d)."""
     if _native(x) and "moe_expert_outputs" in NATIVE:
         return _nat().moe_expert_outputs(x, idx, w_gate, w_up, w_down)
-    T, k = idx.shape
-    outs = torch.zeros(T, k, x.shape[1], dtype=x.dtype, device=x.device)
-    for slot in range(k):
-        one = torch.zeros(T, k, dtype=x.dtype, device=x.device)
-        one[:, slot] = 1.0
-        outs[:, slot] = ref.moe_routed(x, idx, one, w_gate, w_up, w_down)
-    return outs
+    return ref.moe_expert_outputs(x, idx, w_gate, w_up, w_down)
 
 
 def fused_ce_available(h: torch.Tensor) -> bool:

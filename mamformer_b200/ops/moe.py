@@ -1,0 +1,132 @@
+"""Routed-expert computation on the tensor cores (single device; the expert-parallel engine
+reuses the same pieces on each rank's local experts).
+
+Forward for T tokens with top-k assignments (reference semantics ``moe.py:310-332``):
+
+1. counting sort of the T*k assignments by expert: each expert's rows start at a 64-aligned
+   offset ``seg[e]`` of a permuted buffer whose size is a fixed upper bound (T*k + 64*E rows),
+   so nothing here waits for the host; pad rows are zero;
+2. ``H_g = X_e W_gate_e^T``, ``H_u = X_e W_up_e^T`` (tcgen05 grouped GEMM, one launch each);
+3. ``A = silu(H_g) * H_u`` (native SwiGLU);
+4. ``Y_e = A_e W_down_e^T`` (grouped GEMM);
+5. ``out[t] = sum_j gate[t, j] * Y[pos[t, j]]``.
+
+Backward: ``dY`` rows = gate * dout, ``dgate = <dout, Y>``; ``dA = dY W_down`` and
+``dX = dH_g W_gate + dH_u W_up`` (grouped GEMMs with MN-major weights); weight gradients
+``dW_e += dY_e^T A_e`` etc. (grouped-K GEMMs) are accumulated by the GEMM epilogue straight into
+the optimizer's fp32 gradient buffer (``param.main_grad``) when it exists, so no bf16 gradient
+is materialised for the 128 experts.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from mamformer_b200.ops import gemm
+
+ALIGN = 64
+
+
+def plan(idx: torch.Tensor, n_experts: int):
+    """Counting-sort plan for the (T, k) expert indices.
+
+    Returns (pos (T*k,) int64 row of each assignment in the permuted buffer, seg (E+1,) int32,
+    tile_off (E+1,) int32, counts (E,) int64, rows (int, upper bound of the buffer size))."""
+    flat = idx.reshape(-1).long()
+    counts = torch.bincount(flat, minlength=n_experts)
+    padded = (counts + ALIGN - 1) // ALIGN * ALIGN
+    seg = torch.zeros(n_experts + 1, dtype=torch.int64, device=idx.device)
+    seg[1:] = torch.cumsum(padded, 0)
+    start = torch.zeros(n_experts, dtype=torch.int64, device=idx.device)
+    start[1:] = torch.cumsum(counts, 0)[:-1]
+    order = torch.sort(flat, stable=True).indices
+    sorted_e = flat[order]
+    rank = torch.arange(flat.numel(), device=idx.device) - start[sorted_e]
+    pos = torch.empty_like(flat)
+    pos[order] = seg[sorted_e] + rank
+    seg32 = seg.to(torch.int32)
+    rows = (flat.numel() + ALIGN * n_experts + ALIGN - 1) // ALIGN * ALIGN
+    return pos, seg32, gemm.tile_offsets(seg32), counts, rows
+
+
+def _grad_sink(w: torch.Tensor):
+    """fp32 buffer the weight gradient is accumulated into (the optimizer's, if attached)."""
+    mg = getattr(w, "main_grad", None)
+    if mg is not None:
+        return mg, True
+    return torch.zeros(w.shape, device=w.device, dtype=torch.float32), False
+
+
+class _RoutedExperts(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, gates, idx, w_gate, w_up, w_down, combine):
+        T, d = x.shape
+        k = idx.shape[1]
+        E = w_gate.shape[0]
+        pos, seg, tile_off, _, rows = plan(idx, E)
+        tok = torch.arange(T, device=x.device).repeat_interleave(k)
+        xp = torch.zeros(rows, d, device=x.device, dtype=x.dtype)
+        xp[pos] = x[tok]
+        hg = gemm.grouped_mm(xp, w_gate, seg, tile_off)
+        hu = gemm.grouped_mm(xp, w_up, seg, tile_off)
+        from mamformer_b200.ops.native import _C
+        act = _C.swiglu_fwd(hg, hu)
+        yp = gemm.grouped_mm(act, w_down, seg, tile_off)
+        y_rows = yp[pos].view(T, k, d)
+        ctx.save_for_backward(xp, hg, hu, act, yp, pos, seg, tile_off, gates, w_gate, w_up, w_down)
+        ctx.combine = combine
+        ctx.shape = (T, k, d)
+        if combine:
+            return (y_rows.float() * gates.float().unsqueeze(-1)).sum(1).to(x.dtype)
+        return y_rows
+
+    @staticmethod
+    def backward(ctx, dout):
+        xp, hg, hu, act, yp, pos, seg, tile_off, gates, w_gate, w_up, w_down = ctx.saved_tensors
+        T, k, d = ctx.shape
+        rows = xp.shape[0]
+        from mamformer_b200.ops.native import _C
+        if ctx.combine:
+            dout = dout.contiguous()
+            dgates = (yp[pos].view(T, k, d).float() * dout.float().unsqueeze(1)).sum(-1).to(gates.dtype)
+            dy_rows = (gates.float().unsqueeze(-1) * dout.float().unsqueeze(1)).to(xp.dtype).reshape(T * k, d)
+        else:
+            dgates = None
+            dy_rows = dout.reshape(T * k, d).to(xp.dtype)
+        dyp = torch.zeros(rows, d, device=xp.device, dtype=xp.dtype)
+        dyp[pos] = dy_rows
+        # down projection
+        dact = gemm.grouped_mm_nn(dyp, w_down, seg, tile_off)
+        gd, own_d = _grad_sink(w_down)
+        gemm.grouped_wgrad(dyp, act, seg, gd, accumulate=True)
+        dhg, dhu = _C.swiglu_bwd(hg, hu, dact)
+        # gate / up projections
+        dxp = gemm.grouped_mm_nn(dhg, w_gate, seg, tile_off, out_dtype=torch.float32)
+        _C.gemm_tn(dhu, False, w_up, True, dxp, True, seg, tile_off, 1, 1.0)
+        gg, own_g = _grad_sink(w_gate)
+        gemm.grouped_wgrad(dhg, xp, seg, gg, accumulate=True)
+        gu, own_u = _grad_sink(w_up)
+        gemm.grouped_wgrad(dhu, xp, seg, gu, accumulate=True)
+        dx = dxp[pos].view(T, k, d).sum(1).to(xp.dtype)
+        # weights with an optimizer buffer were accumulated in place -> no autograd gradient
+        ret_g = None if own_g else gg.to(w_gate.dtype)
+        ret_u = None if own_u else gu.to(w_up.dtype)
+        ret_d = None if own_d else gd.to(w_down.dtype)
+        return dx, dgates, None, ret_g, ret_u, ret_d, None
+
+
+def supported(x: torch.Tensor, w_gate: torch.Tensor) -> bool:
+    d, I = x.shape[1], w_gate.shape[1]
+    return (x.is_cuda and x.dtype == torch.bfloat16 and w_gate.dtype == torch.bfloat16
+            and d % 64 == 0 and I % 64 == 0)
+
+
+def routed(x, idx, gates, w_gate, w_up, w_down):
+    return _RoutedExperts.apply(x.contiguous(), gates, idx, w_gate, w_up, w_down, True)
+
+
+def expert_outputs(x, idx, w_gate, w_up, w_down):
+    dummy = torch.ones(idx.shape, device=x.device, dtype=torch.float32)
+    return _RoutedExperts.apply(x.contiguous(), dummy, idx, w_gate, w_up, w_down, False)

@@ -184,3 +184,31 @@ def selective_scan(x, dt, A_log, B, C, D, return_h_states=False, return_final_st
     if return_final_state:
         out.append(fin)
     return out[0] if len(out) == 1 else tuple(out)
+
+
+# ---------------------------------------------------------------------------------------------
+@_register("moe_routed", "csrc/gemm_tcgen05.cu (grouped) + ops/moe.py")
+def moe_routed(x, idx, gates, w_gate, w_up, w_down):
+    from mamformer_b200.ops import moe
+    if not moe.supported(x, w_gate):
+        from mamformer_b200.ops import reference
+        return reference.moe_routed(x, idx, gates, w_gate, w_up, w_down)
+    return moe.routed(x, idx, gates, w_gate, w_up, w_down)
+
+
+@_register("linear_cross_entropy", "csrc/cross_entropy.cu + csrc/gemm_tcgen05.cu")
+def linear_cross_entropy(h, weight, labels, ignore_index=-100):
+    from mamformer_b200.ops import linear_ce
+    if not linear_ce.supported(h, weight):
+        from mamformer_b200.ops import reference
+        return reference.linear_cross_entropy(h, weight, labels, ignore_index)
+    return linear_ce.linear_cross_entropy(h, weight, labels, ignore_index)
+
+
+@_register("moe_expert_outputs", "csrc/gemm_tcgen05.cu (grouped) + ops/moe.py")
+def moe_expert_outputs(x, idx, w_gate, w_up, w_down):
+    from mamformer_b200.ops import moe
+    if not moe.supported(x, w_gate):
+        from mamformer_b200.ops import reference
+        return reference.moe_expert_outputs(x, idx, w_gate, w_up, w_down)
+    return moe.expert_outputs(x, idx, w_gate, w_up, w_down)

@@ -305,6 +305,20 @@ def moe_routed(x, idx, gates, w_gate, w_up, w_down):
     return out
 
 
+def moe_expert_outputs(x, idx, w_gate, w_up, w_down):
+    """Unweighted per-slot expert outputs (T, k, d) (reference ``communicative_moe.py:341-391``)."""
+    T, k = idx.shape
+    out = torch.zeros(T, k, x.shape[1], dtype=x.dtype, device=x.device)
+    for e in range(w_gate.shape[0]):
+        tok, slot = (idx == e).nonzero(as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        xe = x[tok]
+        h = F.silu(xe @ w_gate[e].t().to(x.dtype)) * (xe @ w_up[e].t().to(x.dtype))
+        out[tok, slot] = h @ w_down[e].t().to(x.dtype)
+    return out
+
+
 # ---------------------------------------------------------------------------------------------
 # loss
 # ---------------------------------------------------------------------------------------------
