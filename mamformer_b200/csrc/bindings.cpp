@@ -34,6 +34,16 @@ void gemm_clear_error();
 void ce_stats(at::Tensor logits, at::Tensor labels, int64_t ignore_index, at::Tensor loss, at::Tensor lse);
 void ce_grad_inplace(at::Tensor logits, at::Tensor labels, int64_t ignore_index, at::Tensor lse,
                      at::Tensor scale, at::Tensor n_valid);
+void moe_scatter_rows(at::Tensor dst, at::Tensor dst_idx, at::Tensor src, int64_t k);
+void moe_combine(at::Tensor out, std::vector<int64_t> table, int64_t ld_src, at::ScalarType src_dtype,
+                 c10::optional<at::Tensor> owner, at::Tensor pos, c10::optional<at::Tensor> w, int64_t k,
+                 c10::optional<at::Tensor> rows_out);
+void moe_combine_bwd(at::Tensor dout, at::Tensor y, c10::optional<at::Tensor> y_idx, at::Tensor gate,
+                     at::Tensor dgate, at::Tensor dy, c10::optional<at::Tensor> dy_idx, int64_t k);
+void ep_pull_runs(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor runs, int64_t max_len);
+void ep_barrier(std::vector<int64_t> signal, int64_t me, int64_t epoch, int64_t slot0);
+int64_t comm_error();
+void comm_clear_error();
 }  // namespace mamf
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -58,4 +68,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_clear_error", &mamf::gemm_clear_error);
   m.def("ce_stats", &mamf::ce_stats);
   m.def("ce_grad_inplace", &mamf::ce_grad_inplace);
+  m.def("moe_scatter_rows", &mamf::moe_scatter_rows);
+  m.def("moe_combine", &mamf::moe_combine);
+  m.def("moe_combine_bwd", &mamf::moe_combine_bwd);
+  m.def("ep_pull_runs", &mamf::ep_pull_runs);
+  m.def("ep_barrier", &mamf::ep_barrier);
+  m.def("comm_error", &mamf::comm_error);
+  m.def("comm_clear_error", &mamf::comm_clear_error);
 }

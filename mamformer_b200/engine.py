@@ -45,7 +45,9 @@ class Trainer:
     """Owns model + optimizer + schedule; ``train_step`` is the public per-step API."""
 
     def __init__(self, model: MamformerForCausalLM, cfg: TrainConfig,
-                 dp_group: Optional[dist.ProcessGroup] = None, expert_params=None):
+                 dp_group: Optional[dist.ProcessGroup] = None, expert_params=None,
+                 expert_dp_group: Optional[dist.ProcessGroup] = None,
+                 ep_group: Optional[dist.ProcessGroup] = None, bucket_mb: float = 64.0):
         self.cfg = cfg
         self.model = model
         if cfg.compute_dtype != torch.float32:
@@ -54,11 +56,15 @@ class Trainer:
         model.train()
         if cfg.gradient_checkpointing:
             model.model.enable_gradient_checkpointing()
+        if expert_params is None:
+            expert_params = [p for p in model.parameters() if getattr(p, "_mamf_expert", False)] or None
+        self.dp_group = dp_group
         self.optimizer = MixedPrecisionAdamW(
             param_groups(model, cfg.weight_decay), lr=cfg.learning_rate,
             betas=(cfg.adam_beta1, cfg.adam_beta2), eps=cfg.adam_epsilon,
             weight_decay=cfg.weight_decay, max_grad_norm=cfg.max_grad_norm, dp_group=dp_group,
-            no_dp_reduce=expert_params)
+            no_dp_reduce=expert_params, expert_dp_group=expert_dp_group, ep_group=ep_group,
+            bucket_mb=bucket_mb, param_order={id(p): i for i, p in enumerate(model.parameters())})
         self.scheduler = create_lr_scheduler(self.optimizer, cfg.warmup_steps, cfg.max_steps,
                                              cfg.learning_rate, cfg.min_lr_ratio)
         dev = next(model.parameters()).device
@@ -84,10 +90,19 @@ class Trainer:
             sl = slice(i * cfg.micro_batch, (i + 1) * cfg.micro_batch)
             out = self.model(input_ids[sl], labels=labels[sl])
             loss = out["loss"]
+            if i == n_micro - 1:
+                self.optimizer.reducer.arm()      # overlap the gradient all-reduce with this backward
             (loss / n_micro).backward()
             self._loss_acc += loss.detach().float() / n_micro
         loss_val = None
         if sync_loss:
+            self.optimizer.reduce_gradients()
+            if self.dp_group is not None and dist.is_initialized() and dist.get_world_size(self.dp_group) > 1:
+                dist.all_reduce(self._loss_acc, group=self.dp_group)   # same skip decision on all ranks
+                self._loss_acc /= dist.get_world_size(self.dp_group)
+            eng = getattr(self.model, "_mamf_ep_engine", None)
+            if eng is not None:
+                eng.check_error()
             loss_val = float(self._loss_acc)
             if loss_val != loss_val or loss_val in (float("inf"), float("-inf")):
                 # non-finite loss: skip the update (reference train.py:406-432)

@@ -90,8 +90,11 @@ class CommunicativeMoE(nn.Module):
         if base.router_temperature != 1.0:
             logits = logits / base.router_temperature
         gates, idx = base._select(logits)
-        outs = ops.moe_expert_outputs(xf, idx, base.routed_gate_proj, base.routed_up_proj,
-                                      base.routed_down_proj)            # (T, k, d)
+        if base.ep_engine is not None:
+            outs = base.ep_engine.expert_outputs(base, xf, idx)         # (T, k, d)
+        else:
+            outs = ops.moe_expert_outputs(xf, idx, base.routed_gate_proj, base.routed_up_proj,
+                                          base.routed_down_proj)        # (T, k, d)
         comm = self.comm_layer(outs)
         mix = torch.sigmoid(self.comm_strength)
         outs = (1.0 - mix) * outs + mix * comm

@@ -96,6 +96,9 @@ class Mamba2Block(nn.Module):
             y, h_states, final = ops.mamba_inner(x_act, dt_raw, self.A_log, Bm, Cm, self.D, z,
                                                  need_h_states=return_h_states,
                                                  return_final=use_cache)
+            if h_states is not None and getattr(self, "tp_group", None) is not None:
+                from mamformer_b200.parallel.tensor_parallel import mean_from_tp
+                h_states = mean_from_tp(h_states, self.tp_group)   # channel mean over all TP shards
         out = self.out_proj(y)
         new_cache = None
         if use_cache:

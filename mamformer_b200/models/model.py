@@ -154,11 +154,28 @@ class MamformerModel(nn.Module):
         if attention_mask is not None and attention_mask.dim() == 2:
             m = attention_mask[:, None, None, :].to(h.dtype)
             attention_mask = (1.0 - m) * torch.finfo(h.dtype).min
+        h, _, new_caches, aux_list = self.run_layers(h, attention_mask, 0, len(self.layers), None,
+                                                     use_cache, cache, rope_offset)
+        h = self.norm(h)
+        out = {"last_hidden_state": h}
+        if use_cache:
+            out["cache"] = new_caches
+        if aux_list:
+            out["moe_aux_info"] = aux_list
+        return out
+
+    def run_layers(self, h: torch.Tensor, attention_mask: Optional[torch.Tensor], start: int, end: int,
+                   pending: Optional[torch.Tensor] = None, use_cache: bool = False,
+                   cache: Optional[List[dict]] = None, rope_offset: int = 0):
+        """Layers [start, end) with cross-layer SSM-state passing (``model.py:237-297``): an
+        SSM-only layer's per-step state is handed to the next attention-only layer.  Returns
+        (hidden, pending state, caches, MoE aux list); the pipeline stages call this on their
+        slice and ship ``pending`` with the activations."""
         per_layer = cache if cache is not None else [None] * len(self.layers)
         new_caches: List[dict] = []
         aux_list: List[dict] = []
-        pending: Optional[torch.Tensor] = None
-        for idx, layer in enumerate(self.layers):
+        for idx in range(start, end):
+            layer = self.layers[idx]
             lc = per_layer[idx] if idx < len(per_layer) else None
             kw: dict = {}
             attn_only = layer.has_attention and not layer.has_ssm
@@ -182,13 +199,7 @@ class MamformerModel(nn.Module):
                 new_caches.append(entry)
             if entry is not None and "moe_aux_info" in entry:
                 aux_list.append(entry["moe_aux_info"])
-        h = self.norm(h)
-        out = {"last_hidden_state": h}
-        if use_cache:
-            out["cache"] = new_caches
-        if aux_list:
-            out["moe_aux_info"] = aux_list
-        return out
+        return h, pending, new_caches, aux_list
 
     def enable_gradient_checkpointing(self) -> None:
         self.gradient_checkpointing = True
@@ -301,6 +312,12 @@ class MamformerForCausalLM(GenerationMixin, nn.Module):
             result["cache"] = out.get("cache")
         if "moe_aux_info" in out:
             result["moe_aux_info"] = out["moe_aux_info"]
+        return self.compute_head(h, input_ids, labels, attention_mask, want_logits, result)
+
+    def compute_head(self, h: torch.Tensor, input_ids: torch.Tensor, labels: Optional[torch.Tensor],
+                     attention_mask: Optional[torch.Tensor], want_logits: bool, result: dict) -> dict:
+        """Tied LM head, shifted CE and the MTP loss on the final hidden state (also the last
+        pipeline stage's head)."""
         fused = (labels is not None and not want_logits and ops.fused_ce_available(h))
         main_loss = None
         if fused:

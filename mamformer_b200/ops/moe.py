@@ -59,62 +59,81 @@ def _grad_sink(w: torch.Tensor):
     return torch.zeros(w.shape, device=w.device, dtype=torch.float32), False
 
 
+def mlp_forward(xp, seg, tile_off, w_gate, w_up, w_down, y_out=None):
+    """Grouped SwiGLU experts on expert-grouped rows: returns (hg, hu, act, yp)."""
+    from mamformer_b200.ops.native import _C
+    hg = gemm.grouped_mm(xp, w_gate, seg, tile_off)
+    hu = gemm.grouped_mm(xp, w_up, seg, tile_off)
+    act = _C.swiglu_fwd(hg, hu)
+    yp = gemm.grouped_mm(act, w_down, seg, tile_off, out=y_out)
+    return hg, hu, act, yp
+
+
+def mlp_backward(dyp, xp, hg, hu, act, seg, tile_off, w_gate, w_up, w_down, dx_out=None):
+    """Backward of :func:`mlp_forward`.  Returns (dxp fp32, grads) where grads holds the bf16
+    weight gradients of the weights without an optimizer buffer (None for the others, whose
+    gradient was accumulated in place)."""
+    from mamformer_b200.ops.native import _C
+    dact = gemm.grouped_mm_nn(dyp, w_down, seg, tile_off)
+    gd, own_d = _grad_sink(w_down)
+    gemm.grouped_wgrad(dyp, act, seg, gd, accumulate=True)
+    dhg, dhu = _C.swiglu_bwd(hg, hu, dact)
+    dxp = gemm.grouped_mm_nn(dhg, w_gate, seg, tile_off, out=dx_out, out_dtype=torch.float32)
+    _C.gemm_tn(dhu, False, w_up, True, dxp, True, seg, tile_off, 1, 1.0)
+    gg, own_g = _grad_sink(w_gate)
+    gemm.grouped_wgrad(dhg, xp, seg, gg, accumulate=True)
+    gu, own_u = _grad_sink(w_up)
+    gemm.grouped_wgrad(dhu, xp, seg, gu, accumulate=True)
+    from mamformer_b200.optim import mark_grad_ready
+    for w, own in ((w_gate, own_g), (w_up, own_u), (w_down, own_d)):
+        if own:
+            mark_grad_ready(w)
+    grads = (None if own_g else gg.to(w_gate.dtype), None if own_u else gu.to(w_up.dtype),
+             None if own_d else gd.to(w_down.dtype))
+    return dxp, grads
+
+
 class _RoutedExperts(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, gates, idx, w_gate, w_up, w_down, combine):
+        from mamformer_b200.ops.native import _C
         T, d = x.shape
         k = idx.shape[1]
         E = w_gate.shape[0]
         pos, seg, tile_off, _, rows = plan(idx, E)
-        tok = torch.arange(T, device=x.device).repeat_interleave(k)
         xp = torch.zeros(rows, d, device=x.device, dtype=x.dtype)
-        xp[pos] = x[tok]
-        hg = gemm.grouped_mm(xp, w_gate, seg, tile_off)
-        hu = gemm.grouped_mm(xp, w_up, seg, tile_off)
-        from mamformer_b200.ops.native import _C
-        act = _C.swiglu_fwd(hg, hu)
-        yp = gemm.grouped_mm(act, w_down, seg, tile_off)
-        y_rows = yp[pos].view(T, k, d)
-        ctx.save_for_backward(xp, hg, hu, act, yp, pos, seg, tile_off, gates, w_gate, w_up, w_down)
+        _C.moe_scatter_rows(xp, pos, x, k)
+        hg, hu, act, yp = mlp_forward(xp, seg, tile_off, w_gate, w_up, w_down)
+        g32 = gates.float().reshape(-1).contiguous()
+        ctx.save_for_backward(xp, hg, hu, act, yp, pos, seg, tile_off, g32, w_gate, w_up, w_down)
         ctx.combine = combine
         ctx.shape = (T, k, d)
+        ctx.gdtype = gates.dtype
         if combine:
-            return (y_rows.float() * gates.float().unsqueeze(-1)).sum(1).to(x.dtype)
-        return y_rows
+            out = torch.empty(T, d, device=x.device, dtype=x.dtype)
+            _C.moe_combine(out, [yp.data_ptr()], yp.stride(0), yp.dtype, None, pos, g32, k, None)
+            return out
+        return yp[pos].view(T, k, d)
 
     @staticmethod
     def backward(ctx, dout):
-        xp, hg, hu, act, yp, pos, seg, tile_off, gates, w_gate, w_up, w_down = ctx.saved_tensors
+        from mamformer_b200.ops.native import _C
+        xp, hg, hu, act, yp, pos, seg, tile_off, g32, w_gate, w_up, w_down = ctx.saved_tensors
         T, k, d = ctx.shape
         rows = xp.shape[0]
-        from mamformer_b200.ops.native import _C
+        dyp = torch.zeros(rows, d, device=xp.device, dtype=xp.dtype)
+        dout = dout.to(xp.dtype).contiguous()
         if ctx.combine:
-            dout = dout.contiguous()
-            dgates = (yp[pos].view(T, k, d).float() * dout.float().unsqueeze(1)).sum(-1).to(gates.dtype)
-            dy_rows = (gates.float().unsqueeze(-1) * dout.float().unsqueeze(1)).to(xp.dtype).reshape(T * k, d)
+            dg = torch.empty(T * k, device=xp.device, dtype=torch.float32)
+            _C.moe_combine_bwd(dout, yp, pos, g32, dg, dyp, pos, k)
+            dgates = dg.view(T, k).to(ctx.gdtype)
         else:
             dgates = None
-            dy_rows = dout.reshape(T * k, d).to(xp.dtype)
-        dyp = torch.zeros(rows, d, device=xp.device, dtype=xp.dtype)
-        dyp[pos] = dy_rows
-        # down projection
-        dact = gemm.grouped_mm_nn(dyp, w_down, seg, tile_off)
-        gd, own_d = _grad_sink(w_down)
-        gemm.grouped_wgrad(dyp, act, seg, gd, accumulate=True)
-        dhg, dhu = _C.swiglu_bwd(hg, hu, dact)
-        # gate / up projections
-        dxp = gemm.grouped_mm_nn(dhg, w_gate, seg, tile_off, out_dtype=torch.float32)
-        _C.gemm_tn(dhu, False, w_up, True, dxp, True, seg, tile_off, 1, 1.0)
-        gg, own_g = _grad_sink(w_gate)
-        gemm.grouped_wgrad(dhg, xp, seg, gg, accumulate=True)
-        gu, own_u = _grad_sink(w_up)
-        gemm.grouped_wgrad(dhu, xp, seg, gu, accumulate=True)
-        dx = dxp[pos].view(T, k, d).sum(1).to(xp.dtype)
-        # weights with an optimizer buffer were accumulated in place -> no autograd gradient
-        ret_g = None if own_g else gg.to(w_gate.dtype)
-        ret_u = None if own_u else gu.to(w_up.dtype)
-        ret_d = None if own_d else gd.to(w_down.dtype)
-        return dx, dgates, None, ret_g, ret_u, ret_d, None
+            _C.moe_scatter_rows(dyp, pos, dout.reshape(T * k, d), 1)
+        dxp, (gw_g, gw_u, gw_d) = mlp_backward(dyp, xp, hg, hu, act, seg, tile_off, w_gate, w_up, w_down)
+        dx = torch.empty(T, d, device=xp.device, dtype=xp.dtype)
+        _C.moe_combine(dx, [dxp.data_ptr()], dxp.stride(0), dxp.dtype, None, pos, None, k, None)
+        return dx, dgates, None, gw_g, gw_u, gw_d, None
 
 
 def supported(x: torch.Tensor, w_gate: torch.Tensor) -> bool:

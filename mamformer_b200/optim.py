@@ -19,9 +19,13 @@ B200 design:
   (micro-batch accumulation in fp32) and the autograd copy is released;
 * the gradient norm is reduced on the device and the clip factor is read by the update
   kernel from device memory: no host synchronisation in ``step``;
-* data parallelism: gradient segments that are replicated across the data-parallel group are
-  all-reduced (NCCL) before the norm; expert-parallel segments are not (each rank owns its
-  experts and already holds the sum over every rank's tokens).
+* data parallelism: replicated gradient segments are summed over the dense data-parallel group
+  (every rank that holds the same non-expert weights), expert-parallel segments over the
+  expert data-parallel group (ranks that hold the same expert shard; each owner already holds
+  the sum over its EP group's tokens).  The sums run as bucketed NCCL all-reduces launched from
+  the gradient hooks of the last micro-batch, so they overlap the rest of the backward pass;
+  buckets are launched in one fixed order on every rank (a bucket waits for its predecessors),
+  and whatever did not become ready during the backward is launched by ``step``.
 """
 
 from __future__ import annotations
@@ -100,24 +104,134 @@ class _Segment:
                 p.main_grad = self.grad[o:o + n].view_as(p)
 
 
+def _group_size(g) -> int:
+    return dist.get_world_size(g) if (g is not None and dist.is_available() and dist.is_initialized()) else 1
+
+
+class _Bucket:
+    __slots__ = ("seg", "lo", "hi", "params", "group", "pending", "work")
+
+    def __init__(self, seg, lo, hi, params, group):
+        self.seg, self.lo, self.hi, self.params, self.group = seg, lo, hi, params, group
+        self.pending = 0
+        self.work = None
+
+
+class GradReducer:
+    """Bucketed all-reduce of the fp32 gradient segments, overlapped with the backward pass.
+
+    ``arm()`` before the backward of the last micro-batch; gradient hooks then count each
+    bucket down and launch ready buckets (in the fixed launch order) as async all-reduces;
+    ``finish()`` launches the rest and waits."""
+
+    def __init__(self, segments, dense_group, expert_group, bucket_mb: float = 64.0, order=None):
+        self.buckets: List[_Bucket] = []
+        cap = max(1, int(bucket_mb * (1 << 20) / 4))
+        pidx = order or {}
+        for _, seg in segments:
+            if not seg.dp_reduce:
+                continue
+            group = expert_group if seg.expert else dense_group
+            hi = lo = seg.numel
+            cur = []
+            for p, o in reversed(list(zip(seg.params, seg.offsets))):   # backward order ~ reverse
+                if cur and hi - o > cap:
+                    self.buckets.append(_Bucket(seg, lo, hi, cur, group))
+                    hi, cur = lo, []
+                lo = o
+                cur.append(p)
+            if cur:
+                self.buckets.append(_Bucket(seg, 0, hi, cur, group))
+        # launch order: the bucket whose earliest parameter comes last in the model first
+        self.buckets.sort(key=lambda b: -min(pidx.get(id(p), 0) for p in b.params))
+        self._of = {}
+        for i, b in enumerate(self.buckets):
+            for p in b.params:
+                self._of[id(p)] = i
+        self.armed = False
+        self._next = 0
+
+    def arm(self) -> None:
+        self.armed = True
+        self._next = 0
+        for b in self.buckets:
+            b.pending = len(b.params)
+            b.work = None
+
+    def ready(self, p) -> None:
+        if not self.armed:
+            return
+        i = self._of.get(id(p))
+        if i is None:
+            return
+        b = self.buckets[i]
+        if b.pending > 0:
+            b.pending -= 1
+        self._launch_ready()
+
+    def _launch(self, b: _Bucket) -> None:
+        b.work = dist.all_reduce(b.seg.grad[b.lo:b.hi], group=b.group, async_op=True)
+
+    def _launch_ready(self) -> None:
+        while self._next < len(self.buckets) and self.buckets[self._next].pending == 0:
+            self._launch(self.buckets[self._next])
+            self._next += 1
+
+    def finish(self) -> None:
+        while self._next < len(self.buckets):
+            self._launch(self.buckets[self._next])
+            self._next += 1
+        for b in self.buckets:
+            if b.work is not None:
+                b.work.wait()
+                b.work = None
+        self.armed = False
+
+
+def mark_grad_ready(p: torch.Tensor) -> None:
+    """Tell the data-parallel reducer that ``p.main_grad`` is final for this backward (for
+    gradients accumulated in place by a kernel instead of through autograd)."""
+    red = getattr(p, "_mamf_reducer", None)
+    if red is not None:
+        red.ready(p)
+
+
 class MixedPrecisionAdamW(torch.optim.Optimizer):
+    """``dp_group``: dense data-parallel group (all replicas of the non-expert weights; also
+    the 1/world gradient scale).  ``expert_dp_group``: replicas of this rank's expert shard
+    (None: none).  ``ep_group``: the expert-parallel group, over which the squared norm of the
+    expert shards is summed (None: ``dp_group``, i.e. every rank owns a distinct shard)."""
+
     def __init__(self, params, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.1, max_grad_norm: float = 1.0,
-                 dp_group: Optional[dist.ProcessGroup] = None, no_dp_reduce=None):
+                 dp_group: Optional[dist.ProcessGroup] = None, no_dp_reduce=None,
+                 expert_dp_group: Optional[dist.ProcessGroup] = None,
+                 ep_group: Optional[dist.ProcessGroup] = None, bucket_mb: float = 64.0,
+                 param_order=None):
         defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         super().__init__(params, defaults)
         self.max_grad_norm = max_grad_norm
         self.dp_group = dp_group
-        self.world = dist.get_world_size(dp_group) if (dp_group is not None and dist.is_initialized()) else 1
+        self.expert_dp_group = expert_dp_group
+        self.ep_group = ep_group if ep_group is not None else (dp_group if no_dp_reduce else None)
+        self.world = _group_size(dp_group)
+        expert_world = _group_size(expert_dp_group)
         skip = set(id(p) for p in (no_dp_reduce or []))
         dev = self.param_groups[0]["params"][0].device
         self.segments: List[Tuple[int, _Segment]] = []
         for gi, g in enumerate(self.param_groups):
             buckets: Dict[tuple, list] = {}
             for p in g["params"]:
-                buckets.setdefault((p.dtype, id(p) not in skip), []).append(p)
-            for (dt, red), ps in buckets.items():
-                self.segments.append((gi, _Segment(ps, g["weight_decay"], red and self.world > 1, dev, self.world)))
+                buckets.setdefault((p.dtype, id(p) in skip), []).append(p)
+            for (dt, is_exp), ps in buckets.items():
+                red = (expert_world > 1) if is_exp else (self.world > 1)
+                seg = _Segment(ps, g["weight_decay"], red, dev, self.world)
+                seg.expert = is_exp
+                self.segments.append((gi, seg))
+        self.reducer = GradReducer(self.segments, dp_group, expert_dp_group, bucket_mb, param_order)
+        for _, seg in self.segments:
+            for p in seg.params:
+                p._mamf_reducer = self.reducer
         self._hooks = [p.register_post_accumulate_grad_hook(_accumulate_grad)
                        for _, seg in self.segments for p in seg.params]
         self._sq = torch.zeros(1, device=dev)
@@ -132,17 +246,13 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
             for p in seg.params:
                 p.grad = None
 
-    def reduce_gradients(self, async_op: bool = False):
-        """Sum replicated-gradient segments over the data-parallel group."""
-        works = []
-        for _, seg in self.segments:
-            if seg.dp_reduce:
-                works.append(dist.all_reduce(seg.grad, group=self.dp_group, async_op=async_op))
-        return works
+    def reduce_gradients(self) -> None:
+        """Finish the data-parallel gradient sums (launching buckets not launched yet)."""
+        self.reducer.finish()
 
     @torch.no_grad()
     def step(self, closure=None, reduce: bool = True):
-        if reduce and self.world > 1:
+        if reduce:
             self.reduce_gradients()
         C = _native()
         self._step += 1
@@ -152,15 +262,15 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
         # expert-parallel ones because dispatch brought every rank's tokens to the owner), so
         # both are scaled by 1/world.  Replicated segments are identical on every rank; the
         # expert-parallel part of the squared norm is summed over ranks.
-        sq_ep = torch.zeros_like(self._sq) if self.world > 1 else None
+        sq_ep = torch.zeros_like(self._sq) if _group_size(self.ep_group) > 1 else None
         for _, seg in self.segments:
-            acc = sq_ep if (sq_ep is not None and not seg.dp_reduce) else self._sq
+            acc = sq_ep if (sq_ep is not None and seg.expert) else self._sq
             if use_native:
                 C.sq_norm_accumulate(seg.grad, acc)
             else:
                 acc += seg.grad.pow(2).sum()
         if sq_ep is not None:
-            dist.all_reduce(sq_ep, group=self.dp_group)
+            dist.all_reduce(sq_ep, group=self.ep_group)
             self._sq += sq_ep
         if use_native:
             C.clip_scale(self._sq, self._scale, float(self.max_grad_norm or 0.0), 1.0 / self.world,
@@ -213,6 +323,9 @@ def _accumulate_grad(p: torch.Tensor) -> None:
     else:
         p.main_grad.add_(g.float())
     p.grad = None
+    red = getattr(p, "_mamf_reducer", None)
+    if red is not None and red.armed:
+        red.ready(p)
 
 
 def _adamw_torch(seg: _Segment, lr, b1, b2, eps, wd, step, scale):

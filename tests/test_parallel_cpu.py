@@ -1,0 +1,86 @@
+"""Parallel runtime on CPU: gloo ranks in child processes, each checking its shard of the
+gradients (and the loss) against the unsharded single-process model."""
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import _dist_workers as W
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _spawn(fn, world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=W._run, args=(fn, r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, msg = q.get(timeout=600)
+        res[r] = msg
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    bad = {r: m for r, m in res.items() if m != "ok"}
+    assert not bad, "\n".join(f"rank {r}:\n{m}" for r, m in bad.items())
+
+
+def test_parallel_config_layout():
+    from mamformer_b200.parallel import ParallelConfig
+    pc = ParallelConfig(dp_size=2, tp_size=2, pp_size=1, ep_size=2)
+    assert pc.world_size == 8
+    for r in range(8):
+        assert pc.get_global_rank(*pc.get_4d_rank(r)) == r
+    assert pc.get_4d_rank(5) == (1, 0, 0, 1)
+    assert pc.group_members(("ep",))[0] == [0, 1]
+    assert pc.group_members(("tp",))[0] == [0, 2]
+    assert pc.group_members(("dp", "ep"))[0] == [0, 1, 4, 5]
+    with pytest.raises(ValueError):
+        ParallelConfig(tp_size=3).validate(3)
+
+
+def test_pipeline_split_and_bubble():
+    from mamformer_b200.parallel.pipeline_parallel import bubble_fraction, split_layers
+    assert split_layers(10, 4) == [(0, 3), (3, 6), (6, 8), (8, 10)]
+    assert bubble_fraction(4, 12) == pytest.approx(3 / 15)
+
+
+def test_data_parallel_matches_single_process():
+    _spawn(W.dp_worker, 2)
+
+
+def test_expert_parallel_matches_single_process():
+    _spawn(W.ep_worker, 2)
+
+
+def test_tensor_parallel_matches_single_process():
+    _spawn(W.tp_worker, 2)
+
+
+def test_pipeline_parallel_matches_single_process():
+    _spawn(W.pp_worker, 2)
+
+
+def test_diagnostics_cpu():
+    from mamformer_b200.parallel import LoadBalanceAnalyzer, ParallelismMonitor
+    lb = LoadBalanceAnalyzer(1, 4)
+    lb.update(0, torch.tensor([100, 0, 0, 0]))
+    assert any("COLLAPSE" in w for w in lb.get_warnings())
+    mon = ParallelismMonitor(n_layers=1, n_experts=4, use_cuda=False)
+    mon.start_step()
+    mon.comm_start("all_reduce", 1 << 20)
+    mon.comm_end("all_reduce")
+    st = mon.end_step(1, 2.0, 1000)
+    assert st.loss == 2.0 and "communication" in mon.get_full_report()
+    mon.reset()
