@@ -50,6 +50,9 @@ def _args():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-launches", type=int, default=1)
+    ap.add_argument("--parallel", default="ep", choices=["ep", "dp"],
+                    help="N > 1: ep = routed experts sharded over all N GPUs (EP=N x dense DP=N, the "
+                         "BASELINE ultra-7b layout); dp = every GPU holds every expert")
     return ap.parse_args()
 
 
@@ -132,8 +135,17 @@ def run_ours(args, rank, world):
                        grad_accum=args.grad_accum)
     torch.manual_seed(0)
     model = MamformerForCausalLM(cfg).cuda()
-    group = dist.group.WORLD if world > 1 else None
-    trainer = Trainer(model, tcfg, dp_group=group)
+    if world > 1 and args.parallel == "ep":
+        from mamformer_b200.parallel import DistributedCoordinator, ParallelConfig
+        coord = DistributedCoordinator(ParallelConfig(ep_size=world)).initialize()
+        model = coord.shard_model(model)
+        torch.cuda.empty_cache()
+        trainer = Trainer(model, tcfg, dp_group=coord.get_group("dense_dp"),
+                          expert_dp_group=coord.get_group("expert_dp"), ep_group=coord.get_group("ep"))
+        parallelism = f"ep{world} (routed experts sharded over {world} GPUs; dense weights data-parallel)"
+    else:
+        trainer = Trainer(model, tcfg, dp_group=dist.group.WORLD if world > 1 else None)
+        parallelism = f"dp{world}"
     n_batches = 2
     g = torch.Generator().manual_seed(1234 + rank)
     host = [torch.randint(0, cfg.vocab_size, (per_gpu, args.seq), generator=g).pin_memory()
@@ -185,7 +197,7 @@ def run_ours(args, rank, world):
                             f"({cfg.layout_string()}), same per-layer shapes",
                    "global_batch": world * per_gpu, "seq_len": args.seq,
                    "micro_batch": args.micro_batch, "grad_accum": args.grad_accum,
-                   "parallelism": f"dp{world}",
+                   "parallelism": parallelism,
                    "params_b": round(sum(p.numel() for p in model.parameters()) / 1e9, 3),
                    "l2": "working set >> L2 (inputs larger than L2)"},
         "clocks": clk, "e2e": e2e, "gpu_launches": launches, "all_kernel_launches": all_kernels,

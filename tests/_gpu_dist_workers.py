@@ -1,0 +1,85 @@
+"""Worker bodies for the multi-GPU tests (NCCL, one process per GPU)."""
+import copy
+import os
+import traceback
+
+import torch
+import torch.distributed as dist
+
+
+def _run(fn, rank, world, port, out):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        import datetime
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                                timeout=datetime.timedelta(seconds=120))
+        fn(rank, world)
+        out.put((rank, "ok"))
+    except Exception:
+        out.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+def ep_moe_worker(rank, world):
+    """Expert-parallel MoE layer (both transports) against the unsharded layer on one GPU."""
+    from mamformer_b200.models.moe import DeepSeekMoE
+    from mamformer_b200.parallel.expert_parallel import ExpertParallelGroup, shard_experts_ep
+    torch.manual_seed(0)
+    base = DeepSeekMoE(128, n_shared_experts=1, shared_expert_dim=128, n_routed_experts=8, top_k=2,
+                       routed_expert_dim=64).cuda().bfloat16().eval()
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    x = torch.randn(2, 192, 128, device="cuda", generator=g).bfloat16()
+    ref = copy.deepcopy(base)
+    xr = x.clone().requires_grad_()
+    yr, _ = ref(xr)
+    dy = torch.randn(yr.shape, device="cuda", generator=g).bfloat16()
+    yr.backward(dy)
+    ref_w = {n: p.grad.float().clone() for n, p in ref.named_parameters() if n.startswith("routed_")}
+    for n in ref_w:
+        dist.all_reduce(ref_w[n])                      # owners see every rank's tokens
+    epg = ExpertParallelGroup(group=dist.group.WORLD)
+    for backend in ("p2p", "nccl"):
+        m = copy.deepcopy(base)
+        shard_experts_ep(m, epg, backend=backend)
+        xe = x.clone().requires_grad_()
+        ye, _ = m(xe)
+        assert _rel(ye, yr) < 2e-2, (backend, "out", _rel(ye, yr))
+        ye.backward(dy)
+        assert _rel(xe.grad, xr.grad) < 3e-2, (backend, "dx", _rel(xe.grad, xr.grad))
+        s, e = epg.get_expert_range(8)
+        for n, p in m.named_parameters():
+            if n in ref_w:
+                assert _rel(p.grad, ref_w[n][s:e]) < 3e-2, (backend, n, _rel(p.grad, ref_w[n][s:e]))
+        m.ep_engine.check_error()
+    torch.cuda.synchronize()
+
+
+def dp_trainer_worker(rank, world):
+    """Bucketed, overlapped data-parallel gradient sums on NCCL: every rank ends with the same
+    parameters, equal to a single-GPU step on the concatenated batch."""
+    from mamformer_b200 import MamformerConfig, MamformerForCausalLM
+    from mamformer_b200.engine import Trainer, TrainConfig
+    cfg = MamformerConfig.from_preset("debug")
+    tc = TrainConfig(learning_rate=1e-3, warmup_steps=1, micro_batch=1)
+    torch.manual_seed(0)
+    ref = Trainer(MamformerForCausalLM(cfg).cuda(), tc)
+    ids = torch.randint(0, cfg.vocab_size, (world, 128), generator=torch.Generator().manual_seed(5)).cuda()
+    ref.cfg.micro_batch = 1
+    ref.train_step(ids, sync_loss=True)
+    torch.manual_seed(0)
+    tr = Trainer(MamformerForCausalLM(cfg).cuda(), tc, dp_group=dist.group.WORLD, bucket_mb=1.0)
+    tr.train_step(ids[rank:rank + 1], sync_loss=True)
+    for (n, p), (_, q) in zip(tr.model.named_parameters(), ref.model.named_parameters()):
+        assert _rel(p.detach(), q.detach()) < 1e-2, (n, _rel(p.detach(), q.detach()))
+        other = p.detach().clone()
+        dist.broadcast(other, 0)
+        assert torch.equal(other, p.detach()), n
