@@ -44,6 +44,10 @@ void ep_pull_runs(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at
 void ep_barrier(std::vector<int64_t> signal, int64_t me, int64_t epoch, int64_t slot0);
 int64_t comm_error();
 void comm_clear_error();
+std::vector<at::Tensor> linear_attn_fwd(at::Tensor q1, at::Tensor q2, at::Tensor k, at::Tensor v, at::Tensor lam,
+                                        int64_t kernel_dim);
+std::vector<at::Tensor> linear_attn_bwd(at::Tensor q1, at::Tensor q2, at::Tensor k, at::Tensor v, at::Tensor lam,
+                                        int64_t kernel_dim, at::Tensor Sst, at::Tensor zst, at::Tensor dout);
 }  // namespace mamf
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -75,4 +79,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_barrier", &mamf::ep_barrier);
   m.def("comm_error", &mamf::comm_error);
   m.def("comm_clear_error", &mamf::comm_clear_error);
+  m.def("linear_attn_fwd", &mamf::linear_attn_fwd);
+  m.def("linear_attn_bwd", &mamf::linear_attn_bwd);
 }

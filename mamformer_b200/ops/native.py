@@ -212,3 +212,36 @@ def moe_expert_outputs(x, idx, w_gate, w_up, w_down):
         from mamformer_b200.ops import reference
         return reference.moe_expert_outputs(x, idx, w_gate, w_up, w_down)
     return moe.expert_outputs(x, idx, w_gate, w_up, w_down)
+
+
+# ---------------------------------------------------------------------------------------------
+class _LinearDiffAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q1, q2, k, v, lam, kernel_dim):
+        out, S, z = _C.linear_attn_fwd(q1, q2, k, v, lam, int(kernel_dim))
+        ctx.save_for_backward(q1, q2, k, v, lam, S, z)
+        ctx.kernel_dim = int(kernel_dim)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q1, q2, k, v, lam, S, z = ctx.saved_tensors
+        dq1, dq2, dk, dv, dlam = _C.linear_attn_bwd(q1, q2, k, v, lam, ctx.kernel_dim, S, z,
+                                                    dout.to(q1.dtype).contiguous())
+        return dq1, dq2, dk, dv, dlam.to(lam.dtype), None
+
+
+def _la_ok(q1, k, kernel_dim):
+    hd = q1.shape[-1]
+    return (q1.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and q1.dim() == 4
+            and (kernel_dim, hd) in ((128, 128), (64, 128), (64, 64)) and q1.shape[2] % k.shape[2] == 0)
+
+
+@_register("linear_diff_attention", "csrc/linear_attn.cu")
+def linear_diff_attention(q1, q2, k, v, lam, kernel_dim, chunk=256, state=None, return_state=False):
+    if state is not None or return_state or not _la_ok(q1, k, kernel_dim):
+        from mamformer_b200.ops import reference
+        return reference.linear_diff_attention(q1, q2, k, v, lam, kernel_dim, chunk, state=state,
+                                               return_state=return_state)
+    return _LinearDiffAttn.apply(q1.contiguous(), q2.contiguous(), k.contiguous(), v.contiguous(), lam,
+                                 kernel_dim)

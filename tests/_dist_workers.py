@@ -53,6 +53,24 @@ def _check(name, got, want, tol=2e-5):
     assert err <= tol * max(1.0, scale), f"{name}: max err {err:.3e} (scale {scale:.3e})"
 
 
+def _check_consolidation(tag, model, optimizer, ref_model):
+    """Every rank writes its shard; rank 0 consolidates and compares with the unsharded state."""
+    import tempfile
+    from mamformer_b200.checkpoint import consolidate, model_state_dict, save_sharded
+    d = os.path.join(tempfile.gettempdir(), f"mamf_ckpt_{os.getppid()}_{tag}")
+    save_sharded(d, model, optimizer)
+    dist.barrier()
+    if dist.get_rank() == 0:
+        full = consolidate(d)
+        want = model_state_dict(ref_model)
+        missing = set(want) - set(full)
+        assert not missing, sorted(missing)[:5]
+        for k, v in want.items():
+            assert full[k].shape == v.shape, (k, full[k].shape, v.shape)
+            assert torch.equal(full[k].float(), v.float()), k
+    dist.barrier()
+
+
 def _run(fn, rank, world, port, out):
     try:
         _init(rank, world, port)
@@ -96,6 +114,7 @@ def ep_worker(rank, world):
     assert len(expert_parameters(model)) == 3 * len(_moe_modules(model)) > 0
     tr = _trainer(model, mb=1, dp_group=coord.get_group("dense_dp"), expert_dp_group=coord.get_group("expert_dp"),
                   ep_group=coord.get_group("ep"))
+    _check_consolidation("ep", tr.model, tr.optimizer, _build(cfg))
     loss = tr.train_step(ids[rank:rank + 1], sync_loss=True)
     assert abs(loss - ref_loss) < 1e-5, (loss, ref_loss)
     for n, p in tr.model.named_parameters():
@@ -122,6 +141,7 @@ def tp_worker(rank, world):
     coord = DistributedCoordinator(ParallelConfig(tp_size=world)).initialize()
     model = coord.shard_model(_build(cfg))
     tr = _trainer(model, mb=2)
+    _check_consolidation("tp", tr.model, tr.optimizer, _build(cfg))
     loss = tr.train_step(ids, sync_loss=True)
     assert abs(loss - ref_loss) < 1e-5, (loss, ref_loss)
     n_sliced = 0
@@ -154,6 +174,7 @@ def pp_worker(rank, world):
         assert stage.send_state, "the layout puts an SSM state on the stage boundary"
     stage.model.train()
     opt = MixedPrecisionAdamW([p for p in stage.parameters()], lr=0.0)
+    _check_consolidation("pp", stage.model, opt, _build(cfg))
     sched = PipelineScheduler1F1B(stage, m, cfg.d_model, dtype=torch.float32)
     opt.zero_grad()
     loss = sched.run_forward_backward(ids)

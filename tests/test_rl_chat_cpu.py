@@ -129,3 +129,59 @@ def test_chat_stream(tiny):
     s.add_user_message("hello")
     chunks = list(s.generate_stream())
     assert 1 <= len(chunks) <= 3
+
+
+def test_checkpoint_roundtrip_and_resume(tmp_path):
+    from mamformer_b200.checkpoint import latest_checkpoint, load_checkpoint, save_checkpoint
+    from mamformer_b200.engine import TrainConfig, Trainer
+    cfg = MamformerConfig.from_preset("debug")
+    torch.manual_seed(0)
+    tr = Trainer(MamformerForCausalLM(cfg), TrainConfig(learning_rate=1e-3, warmup_steps=1, micro_batch=2,
+                                                        compute_dtype=torch.float32))
+    ids = torch.randint(0, 1000, (2, 16))
+    tr.train_step(ids)
+    path = save_checkpoint(str(tmp_path / "checkpoint_step_1.pt"), tr.model, tr.optimizer, tr.scheduler, step=1)
+    ck = torch.load(path, weights_only=False)
+    assert ck["step"] == 1 and all(v.dtype in (torch.float32, torch.int64) for v in ck["model"].values())
+    masters = {}
+    for _, seg in tr.optimizer.segments:
+        for p, o in zip(seg.params, seg.offsets):
+            masters[id(p)] = seg.master[o:o + p.numel()].view(p.shape).clone()
+    ref = {n: masters[id(p)] for n, p in tr.model.named_parameters()}
+    torch.manual_seed(1)
+    tr2 = Trainer(MamformerForCausalLM(cfg), TrainConfig(learning_rate=1e-3, warmup_steps=1, micro_batch=2,
+                                                         compute_dtype=torch.float32))
+    step = load_checkpoint(path, tr2.model, tr2.optimizer, tr2.scheduler)
+    assert step == 1 and latest_checkpoint(str(tmp_path)) == path
+    got = {}
+    for _, seg in tr2.optimizer.segments:
+        for p, o in zip(seg.params, seg.offsets):
+            got[id(p)] = seg.master[o:o + p.numel()].view(p.shape)
+    for n, p in tr2.model.named_parameters():
+        assert torch.equal(got[id(p)], ref[n]), n
+        assert torch.equal(p.detach().float(), ref[n].to(p.dtype).float()), n
+    l1 = float(tr.train_step(ids, sync_loss=True))
+    l2 = float(tr2.train_step(ids, sync_loss=True))
+    assert abs(l1 - l2) < 1e-6
+
+
+def test_grpo_step_cpu():
+    from mamformer_b200.grpo import (GRPOConfig, GRPOTrainer, PromptDataset, collate_prompts, compute_grpo_loss,
+                                     group_advantages, rollout_temperatures)
+    from mamformer_b200.sgrpo import StochasticGRPOConfig
+    a = group_advantages(torch.tensor([[1.0, 0.0, 1.0, 0.0]]))
+    assert torch.allclose(a.mean(), torch.tensor(0.0)) and a[0, 0] > 0
+    assert rollout_temperatures(1.0, 3) == [0.9, 1.0, 1.1]
+    loss, m = compute_grpo_loss(torch.tensor([[-1.0, -2.0]]), torch.tensor([[-1.0, -1.0]]), torch.tensor([[1.0, -1.0]]))
+    assert float(loss) == pytest.approx(-0.5 + 0.04 * 0.5)
+    tok = MamformerTokenizer()
+    ds = PromptDataset("/nonexistent.jsonl", tok)
+    batch = collate_prompts([ds[0], ds[1]])
+    torch.manual_seed(0)
+    policy = MamformerForCausalLM(MamformerConfig.from_preset("debug"))
+    tr = GRPOTrainer(policy, tok, GRPOConfig(group_size=2, gen_max_tokens=4, learning_rate=1e-4,
+                                             sgrpo=StochasticGRPOConfig(enabled=True, p=0.5, seed=0)))
+    before = [p.detach().clone() for p in tr.policy.parameters()]
+    m = tr.step(batch)
+    assert torch.isfinite(m["loss"]) and tr.global_step == 1
+    assert any(not torch.equal(b, p.detach()) for b, p in zip(before, tr.policy.parameters()))
