@@ -33,20 +33,17 @@ import torch.distributed as dist
 
 
 def _masters(optimizer):
-    """param id -> fp32 master view (None when there is no mixed-precision optimizer)."""
-    out = {}
-    if optimizer is None or not hasattr(optimizer, "segments"):
-        return out
-    for _, seg in optimizer.segments:
-        for p, o in zip(seg.params, seg.offsets):
-            out[id(p)] = seg.master[o:o + p.numel()].view(p.shape)
-    return out
+    """param id -> fp32 weight (a temporary full copy for ZeRO-sharded segments, gathered
+    collectively); empty without a mixed-precision optimizer."""
+    if optimizer is None or not hasattr(optimizer, "master_views"):
+        return {}
+    return optimizer.master_views()
 
 
 @contextlib.contextmanager
-def fp32_parameters(model, optimizer):
+def fp32_parameters(model, optimizer, ms=None):
     """Temporarily point every parameter at its fp32 master weight."""
-    ms = _masters(optimizer)
+    ms = _masters(optimizer) if ms is None else ms
     saved = []
     for p in model.parameters():
         m = ms.get(id(p))
@@ -80,21 +77,38 @@ def load_model_state(model, state: Dict[str, torch.Tensor], optimizer=None, stri
         p = named.get(k)
         sl = getattr(p, "_mamf_tp_slice", None) if p is not None else None
         local[k] = v.index_select(sl[0], sl[1].to(v.device)) if (sl is not None and v.shape != p.shape) else v
-    with fp32_parameters(model, optimizer):
+    ms = _masters(optimizer)
+    with fp32_parameters(model, optimizer, ms):
         res = model.load_state_dict(local, strict=strict)
     if optimizer is not None and hasattr(optimizer, "segments"):
         with torch.no_grad():
             for _, seg in optimizer.segments:
-                if seg.low:
+                if not seg.low:
+                    continue
+                if seg.sharded:          # the loaded values sit in the gathered temporary
+                    p0, o0 = seg.params[0], seg.offsets[0]
+                    full = ms[id(p0)].reshape(-1).view(-1)
+                    flat = torch.empty(0, device=full.device, dtype=torch.float32).set_(
+                        full.untyped_storage(), full.storage_offset() - o0, (seg.numel,))
+                    seg.master.copy_(flat[seg.lo:seg.hi])
+                    seg.low_flat.copy_(flat)
+                else:
                     seg.low_flat.copy_(seg.master)
     return res
 
 
-def save_checkpoint(path: str, model, optimizer=None, scheduler=None, step: int = 0, extra: Optional[dict] = None):
-    """Single-process checkpoint in the reference format."""
+def save_checkpoint(path: str, model, optimizer=None, scheduler=None, step: int = 0, extra: Optional[dict] = None,
+                    write: bool = True):
+    """Checkpoint in the reference format.  With a ZeRO-sharded optimizer every rank must call
+    this (the fp32 weights are gathered); only ranks with ``write`` touch the file."""
+    state = model_state_dict(model, optimizer)
+    if not write:
+        return path
     os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
-    ck = {"model": model_state_dict(model, optimizer), "step": int(step),
-          "optimizer": optimizer.state_dict() if optimizer is not None else None,
+    # a ZeRO-sharded optimizer state belongs in per-rank shards (save_sharded), not in one file
+    keep_opt = optimizer is not None and not getattr(optimizer, "sharded", False)
+    ck = {"model": state, "step": int(step),
+          "optimizer": optimizer.state_dict() if keep_opt else None,
           "scheduler": scheduler.state_dict() if scheduler is not None else None}
     if extra:
         ck.update(extra)

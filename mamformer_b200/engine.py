@@ -47,7 +47,8 @@ class Trainer:
     def __init__(self, model: MamformerForCausalLM, cfg: TrainConfig,
                  dp_group: Optional[dist.ProcessGroup] = None, expert_params=None,
                  expert_dp_group: Optional[dist.ProcessGroup] = None,
-                 ep_group: Optional[dist.ProcessGroup] = None, bucket_mb: float = 64.0):
+                 ep_group: Optional[dist.ProcessGroup] = None, bucket_mb: float = 64.0,
+                 zero_stage: int = 0):
         self.cfg = cfg
         self.model = model
         if cfg.compute_dtype != torch.float32:
@@ -64,7 +65,8 @@ class Trainer:
             betas=(cfg.adam_beta1, cfg.adam_beta2), eps=cfg.adam_epsilon,
             weight_decay=cfg.weight_decay, max_grad_norm=cfg.max_grad_norm, dp_group=dp_group,
             no_dp_reduce=expert_params, expert_dp_group=expert_dp_group, ep_group=ep_group,
-            bucket_mb=bucket_mb, param_order={id(p): i for i, p in enumerate(model.parameters())})
+            bucket_mb=bucket_mb, param_order={id(p): i for i, p in enumerate(model.parameters())},
+            zero_stage=zero_stage)
         self.scheduler = create_lr_scheduler(self.optimizer, cfg.warmup_steps, cfg.max_steps,
                                              cfg.learning_rate, cfg.min_lr_ratio)
         dev = next(model.parameters()).device

@@ -71,10 +71,15 @@ def _native():
 
 
 class _Segment:
-    """One flat run of parameters sharing (master kind, decay, dp reduction)."""
+    """One flat run of parameters sharing (master kind, decay, dp reduction).
+
+    With ``shard_group`` (ZeRO-1) the fp32 master weights and both moments cover only this
+    rank's 1/n slice [lo, hi) of the segment; gradients stay full (micro-batch accumulation),
+    the update runs on the slice and the updated weights are all-gathered back into the flat
+    parameter buffer."""
 
     def __init__(self, params: List[torch.nn.Parameter], wd: float, dp_reduce: bool, device,
-                 world: int):
+                 world: int, shard_group=None):
         self.params = params
         self.wd = wd
         self.dp_reduce = dp_reduce
@@ -84,24 +89,57 @@ class _Segment:
         for p in params:
             self.offsets.append(off)
             off += (p.numel() + _ALIGN - 1) // _ALIGN * _ALIGN
-        pad = _ALIGN * max(1, world)
+        sw = _group_size(shard_group)
+        self.shard_group = shard_group if sw > 1 else None
+        pad = _ALIGN * math.lcm(max(1, world), sw)
         self.numel = max(pad, (off + pad - 1) // pad * pad)
+        sr = dist.get_rank(shard_group) if self.shard_group is not None else 0
+        self.lo, self.hi = sr * self.numel // sw, (sr + 1) * self.numel // sw
         f32 = dict(device=device, dtype=torch.float32)
-        self.master = torch.zeros(self.numel, **f32)
+        n_local = self.hi - self.lo
         self.grad = torch.zeros(self.numel, **f32)
-        self.m = torch.zeros(self.numel, **f32)
-        self.v = torch.zeros(self.numel, **f32)
+        self.m = torch.zeros(n_local, **f32)
+        self.v = torch.zeros(n_local, **f32)
         self.low_flat = torch.zeros(self.numel, device=device, dtype=params[0].dtype) if self.low else None
+        # full fp32 values (the parameters of an fp32 segment view this buffer)
+        full = torch.zeros(self.numel, **f32)
         with torch.no_grad():
             for p, o in zip(params, self.offsets):
                 n = p.numel()
-                self.master[o:o + n].copy_(p.detach().reshape(-1).float())
+                full[o:o + n].copy_(p.detach().reshape(-1).float())
                 if self.low:
                     self.low_flat[o:o + n].copy_(p.detach().reshape(-1))
                     p.data = self.low_flat[o:o + n].view_as(p)
                 else:
-                    p.data = self.master[o:o + n].view_as(p)
+                    p.data = full[o:o + n].view_as(p)
                 p.main_grad = self.grad[o:o + n].view_as(p)
+        if self.low:
+            self.master = full[self.lo:self.hi].clone() if self.shard_group is not None else full
+            self.full32 = None
+        else:
+            self.full32 = full
+            self.master = full[self.lo:self.hi]
+
+    @property
+    def sharded(self) -> bool:
+        return self.shard_group is not None
+
+    def gather_params(self) -> None:
+        """All-gather the updated slice into the full flat parameter buffer."""
+        if not self.sharded:
+            return
+        buf = self.low_flat if self.low else self.full32
+        dist.all_gather_into_tensor(buf, buf[self.lo:self.hi].clone(), group=self.shard_group)
+
+    def full_master(self) -> torch.Tensor:
+        """fp32 values of the whole segment (collective over the shard group when sharded)."""
+        if not self.sharded:
+            return self.master if self.low else self.full32
+        if not self.low:
+            return self.full32
+        out = torch.empty(self.numel, device=self.master.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(out, self.master, group=self.shard_group)
+        return out
 
 
 def _group_size(g) -> int:
@@ -207,7 +245,7 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
                  dp_group: Optional[dist.ProcessGroup] = None, no_dp_reduce=None,
                  expert_dp_group: Optional[dist.ProcessGroup] = None,
                  ep_group: Optional[dist.ProcessGroup] = None, bucket_mb: float = 64.0,
-                 param_order=None):
+                 param_order=None, zero_stage: int = 0):
         defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         super().__init__(params, defaults)
         self.max_grad_norm = max_grad_norm
@@ -225,7 +263,8 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
                 buckets.setdefault((p.dtype, id(p) in skip), []).append(p)
             for (dt, is_exp), ps in buckets.items():
                 red = (expert_world > 1) if is_exp else (self.world > 1)
-                seg = _Segment(ps, g["weight_decay"], red, dev, self.world)
+                shard = dp_group if (zero_stage >= 1 and not is_exp and self.world > 1) else None
+                seg = _Segment(ps, g["weight_decay"], red, dev, self.world, shard_group=shard)
                 seg.expert = is_exp
                 self.segments.append((gi, seg))
         self.reducer = GradReducer(self.segments, dp_group, expert_dp_group, bucket_mb, param_order)
@@ -263,15 +302,20 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
         # both are scaled by 1/world.  Replicated segments are identical on every rank; the
         # expert-parallel part of the squared norm is summed over ranks.
         sq_ep = torch.zeros_like(self._sq) if _group_size(self.ep_group) > 1 else None
+        sq_sh = torch.zeros_like(self._sq) if any(seg.sharded for _, seg in self.segments) else None
         for _, seg in self.segments:
-            acc = sq_ep if (sq_ep is not None and seg.expert) else self._sq
+            acc = sq_ep if (sq_ep is not None and seg.expert) else (sq_sh if seg.sharded else self._sq)
+            g = seg.grad[seg.lo:seg.hi] if seg.sharded else seg.grad
             if use_native:
-                C.sq_norm_accumulate(seg.grad, acc)
+                C.sq_norm_accumulate(g, acc)
             else:
-                acc += seg.grad.pow(2).sum()
+                acc += g.pow(2).sum()
         if sq_ep is not None:
             dist.all_reduce(sq_ep, group=self.ep_group)
             self._sq += sq_ep
+        if sq_sh is not None:
+            dist.all_reduce(sq_sh, group=self.dp_group)
+            self._sq += sq_sh
         if use_native:
             C.clip_scale(self._sq, self._scale, float(self.max_grad_norm or 0.0), 1.0 / self.world,
                          self.last_grad_norm)
@@ -285,30 +329,53 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
         for gi, seg in self.segments:
             grp = self.param_groups[gi]
             b1, b2 = grp["betas"]
+            g = seg.grad[seg.lo:seg.hi] if seg.sharded else seg.grad
+            low = seg.low_flat[seg.lo:seg.hi] if (seg.low and seg.sharded) else seg.low_flat
             if use_native:
-                C.adamw_step(seg.master, seg.grad, seg.m, seg.v, seg.low_flat, float(grp["lr"]), b1, b2,
+                C.adamw_step(seg.master, g, seg.m, seg.v, low, float(grp["lr"]), b1, b2,
                              grp["eps"], seg.wd, self._step, self._scale)
             else:
-                _adamw_torch(seg, grp["lr"], b1, b2, grp["eps"], seg.wd, self._step, self._scale)
+                _adamw_torch(seg.master, g, seg.m, seg.v, low, grp["lr"], b1, b2, grp["eps"], seg.wd,
+                             self._step, self._scale)
+            seg.gather_params()
         return None
 
     def grad_norm(self) -> torch.Tensor:
         return self.last_grad_norm
 
+    def master_views(self) -> Dict[int, torch.Tensor]:
+        """param id -> fp32 weight (collective over the shard groups when ZeRO is on)."""
+        out = {}
+        for _, seg in self.segments:
+            full = seg.full_master()
+            for p, o in zip(seg.params, seg.offsets):
+                out[id(p)] = full[o:o + p.numel()].view(p.shape)
+        return out
+
     # -- checkpointing ---------------------------------------------------------------------
     def state_dict(self):
         return {"step": self._step,
-                "segments": [{"master": s.master.cpu(), "m": s.m.cpu(), "v": s.v.cpu()} for _, s in self.segments],
+                "segments": [{"master": s.master.cpu(), "m": s.m.cpu(), "v": s.v.cpu(),
+                              "shard": (s.lo, s.hi, s.numel)} for _, s in self.segments],
                 "param_groups": [{k: v for k, v in g.items() if k != "params"} for g in self.param_groups]}
 
+    @property
+    def sharded(self) -> bool:
+        return any(seg.sharded for _, seg in self.segments)
+
     def load_state_dict(self, state):
+        segs = state["segments"]
+        for (_, seg), st in zip(self.segments, segs):
+            if tuple(st.get("shard", (0, seg.numel, seg.numel))) != (seg.lo, seg.hi, seg.numel):
+                raise ValueError("optimizer state was saved with another sharding layout")
         self._step = int(state["step"])
-        for (_, seg), st in zip(self.segments, state["segments"]):
+        for (_, seg), st in zip(self.segments, segs):
             seg.master.copy_(st["master"])
             seg.m.copy_(st["m"])
             seg.v.copy_(st["v"])
             if seg.low:
-                seg.low_flat.copy_(seg.master)
+                (seg.low_flat[seg.lo:seg.hi] if seg.sharded else seg.low_flat).copy_(seg.master)
+            seg.gather_params()
         for g, sg in zip(self.param_groups, state["param_groups"]):
             g.update({k: v for k, v in sg.items() if k in ("lr", "betas", "eps", "weight_decay", "initial_lr")})
 
@@ -328,13 +395,13 @@ def _accumulate_grad(p: torch.Tensor) -> None:
         red.ready(p)
 
 
-def _adamw_torch(seg: _Segment, lr, b1, b2, eps, wd, step, scale):
-    g = seg.grad * scale
-    seg.m.mul_(b1).add_(g, alpha=1 - b1)
-    seg.v.mul_(b2).addcmul_(g, g, value=1 - b2)
+def _adamw_torch(master, grad, m, v, low, lr, b1, b2, eps, wd, step, scale):
+    g = grad * scale
+    m.mul_(b1).add_(g, alpha=1 - b1)
+    v.mul_(b2).addcmul_(g, g, value=1 - b2)
     bc1 = 1 - b1 ** step
     bc2 = 1 - b2 ** step
-    seg.master.mul_(1 - lr * wd)
-    seg.master.addcdiv_(seg.m, (seg.v.sqrt() / math.sqrt(bc2)).add_(eps), value=-lr / bc1)
-    if seg.low:
-        seg.low_flat.copy_(seg.master)
+    master.mul_(1 - lr * wd)
+    master.addcdiv_(m, (v.sqrt() / math.sqrt(bc2)).add_(eps), value=-lr / bc1)
+    if low is not None:
+        low.copy_(master)

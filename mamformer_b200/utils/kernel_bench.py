@@ -1,0 +1,177 @@
+"""Micro-benchmarks of the native kernels at the shapes of the ultra-7b bench workload.
+
+    python -m mamformer_b200.utils.kernel_bench --op gemm [--iters 20]
+    python -m mamformer_b200.utils.kernel_bench --op scan --once     # one launch (profiler capture)
+
+Each case builds its inputs once on the GPU, warms up, and times ``--iters`` launches with CUDA
+events on the launching stream (synchronised on both sides).  Inputs are larger than the 126 MB
+L2 where the kernel is memory-bound; for the GEMMs the operands are re-read from L2 by design.
+The report gives the achieved rate and its fraction of the measured peaks
+(``MEASURED_PEAKS.json``: copy bandwidth, cuBLAS bf16 GEMM throughput).  ``--once`` runs one
+warm-up and exactly one launch of the case, for a profiler that captures a single kernel.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"]
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0
+
+
+def case_gemm(d=4096, V=128000, T=4096):
+    """CE logits GEMM: (T, d) x (V, d)^T -> (T, V) bf16."""
+    from mamformer_b200.ops import gemm
+    h = torch.randn(T, d, device="cuda").bfloat16()
+    W = torch.randn(V, d, device="cuda").bfloat16() * 0.02
+    out = torch.empty(T, V, device="cuda", dtype=torch.bfloat16)
+    return (lambda: gemm.mm(h, W, out=out)), 2.0 * T * V * d, (T * d + V * d + T * V) * 2
+
+
+def case_grouped(E=128, k=8, T=4096, d=4096, I=576):
+    """MoE up-projection: grouped-M GEMM over 128 experts (balanced)."""
+    from mamformer_b200.ops import gemm
+    from mamformer_b200.ops.moe import plan
+    idx = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)])
+    pos, seg, tile_off, _, rows = plan(idx, E)
+    x = torch.randn(rows, d, device="cuda").bfloat16()
+    w = torch.randn(E, I, d, device="cuda").bfloat16() * 0.02
+    out = torch.empty(rows, I, device="cuda", dtype=torch.bfloat16)
+    return (lambda: gemm.grouped_mm(x, w, seg, tile_off, out=out)), 2.0 * T * k * I * d, (rows * d + E * I * d + rows * I) * 2
+
+
+def case_scan(B=1, S=4096, D=8192, N=128, backward=False):
+    """Selective scan (Mamba block of ultra-7b: d_inner 8192, d_state 128), fused gate."""
+    from mamformer_b200.ops.native import _C
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(B, S, D, device="cuda", generator=g).bfloat16()
+    dt = (torch.randn(B, S, D, device="cuda", generator=g) * 0.5 - 2).bfloat16()
+    A = torch.log(torch.linspace(0.5, 8, N, device="cuda"))
+    Bm = torch.randn(B, S, N, device="cuda", generator=g).bfloat16()
+    Cm = torch.randn(B, S, N, device="cuda", generator=g).bfloat16()
+    Dv = torch.ones(D, device="cuda")
+    z = torch.randn(B, S, D, device="cuda", generator=g).bfloat16()
+    y, hs, ck, fin = _C.selective_scan_fwd(x, dt, A, Bm, Cm, Dv, z, None, True, True, False)
+    io = (4 * B * S * D + 2 * B * S * N) * 2
+    if not backward:
+        return (lambda: _C.selective_scan_fwd(x, dt, A, Bm, Cm, Dv, z, None, True, True, False)), 0.0, io
+    dy = torch.randn_like(x)
+    dhs = torch.randn_like(hs) if hs is not None else None
+    return (lambda: _C.selective_scan_bwd(x, dt, A, Bm, Cm, Dv, z, ck, dy, dhs, True)), 0.0, 2 * io
+
+
+def case_linear_attn(B=1, S=4096, H=32, G=8, hd=128, backward=False):
+    from mamformer_b200.ops.native import _C
+    mk = lambda h: (torch.randn(B, S, h, hd, device="cuda") * 0.5).bfloat16()
+    q1, q2, k, v = mk(H), mk(H), mk(G), mk(G)
+    lam = torch.full((H,), 0.5, device="cuda")
+    out, Sst, zst = _C.linear_attn_fwd(q1, q2, k, v, lam, hd)
+    C = 64
+    flops = 2.0 * B * H * S * (2 * C * hd + 2 * C * hd + 2 * hd * hd) * 2
+    io = (3 * B * S * H * hd + 2 * B * S * G * hd) * 2
+    if not backward:
+        return (lambda: _C.linear_attn_fwd(q1, q2, k, v, lam, hd)), flops, io
+    dout = torch.randn_like(out)
+    return (lambda: _C.linear_attn_bwd(q1, q2, k, v, lam, hd, Sst, zst, dout)), 2.5 * flops, 2 * io
+
+
+def case_ce(T=4096, d=4096, V=128000):
+    """Fused linear + cross-entropy forward and backward (recompute), tied embedding."""
+    from mamformer_b200.ops import linear_ce
+    h = (torch.randn(T, d, device="cuda") * 0.5).bfloat16().requires_grad_()
+    W = (torch.randn(V, d, device="cuda") * 0.02).bfloat16().requires_grad_()
+    W.main_grad = torch.zeros(V, d, device="cuda")
+    lab = torch.randint(0, V, (T,), device="cuda")
+
+    def run():
+        loss = linear_ce.linear_cross_entropy(h, W, lab)
+        loss.backward()
+    return run, 4 * 2.0 * T * V * d, 0
+
+
+def case_moe(T=4096, d=4096, E=128, k=8, I=576):
+    """Routed experts forward + backward on one GPU (dispatch, 3 grouped GEMMs, combine)."""
+    from mamformer_b200.ops import moe
+    x = (torch.randn(T, d, device="cuda") * 0.5).bfloat16().requires_grad_()
+    idx = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)])
+    gates = torch.softmax(torch.randn(T, k, device="cuda"), -1).requires_grad_()
+    ws = [(torch.randn(*s, device="cuda") * 0.02).bfloat16().requires_grad_() for s in ((E, I, d), (E, I, d), (E, d, I))]
+    for w in ws:
+        w.main_grad = torch.zeros(w.shape, device="cuda")
+
+    def run():
+        out = moe.routed(x, idx, gates, *ws)
+        out.backward(torch.ones_like(out))
+    return run, 3 * 3 * 2.0 * T * k * d * I, 0
+
+
+def case_adamw(n=1 << 28):
+    """Fused AdamW over a 2^28-element fp32 segment with a bf16 copy (the optimizer step)."""
+    from mamformer_b200.ops.native import _C
+    p, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    v.abs_()
+    low = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    scale = torch.ones(1, device="cuda")
+    return (lambda: _C.adamw_step(p, g, m, v, low, 1e-4, 0.9, 0.95, 1e-8, 0.1, 1, scale)), 0.0, n * (4 * 7 + 2)
+
+
+CASES = {"gemm": case_gemm, "grouped": case_grouped, "scan": case_scan,
+         "scan_bwd": lambda: case_scan(backward=True), "linear_attn": case_linear_attn,
+         "linear_attn_bwd": lambda: case_linear_attn(backward=True), "ce": case_ce, "moe": case_moe,
+         "adamw": case_adamw}
+
+
+def run(op: str, iters: int = 20, once: bool = False) -> dict:
+    fn, flops, nbytes = CASES[op]()
+    fn()
+    torch.cuda.synchronize()
+    if once:
+        fn()
+        torch.cuda.synchronize()
+        return {"op": op, "launched": 1}
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    hbm, tf = _peaks()
+    out = {"op": op, "ms": round(ms, 4)}
+    if flops:
+        out["tflops"] = round(flops / ms / 1e9, 1)
+        out["frac_of_measured_bf16"] = round(flops / ms / 1e9 / tf, 3)
+    if nbytes:
+        out["gbs"] = round(nbytes / ms / 1e6, 1)
+        out["frac_of_measured_hbm"] = round(nbytes / ms / 1e6 / hbm, 3)
+    return out
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--op", default="all", choices=["all"] + list(CASES))
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--once", action="store_true")
+    a = ap.parse_args(argv)
+    for op in (CASES if a.op == "all" else [a.op]):
+        print(json.dumps(run(op, a.iters, a.once)), flush=True)
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()

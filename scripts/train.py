@@ -45,6 +45,8 @@ def build_parser():
     p.add_argument("--thinking_format", action="store_true", help="accepted for compatibility")
     p.add_argument("--ep", type=int, default=1, help="expert-parallel size (routed experts sharded)")
     p.add_argument("--seed", type=int, default=42)
+    p.add_argument("--zero", type=int, default=0, choices=[0, 1],
+                   help="1: shard fp32 master weights and Adam moments over the data-parallel ranks")
     return p
 
 
@@ -75,7 +77,8 @@ def train(args, parallel=None):
                        grad_accum=args.gradient_accumulation_steps, compute_dtype=dtype,
                        gradient_checkpointing=args.gradient_checkpointing)
     trainer = Trainer(model, tcfg, dp_group=coord.get_group("dense_dp") if world > 1 else None,
-                      expert_dp_group=coord.get_group("expert_dp"), ep_group=coord.get_group("ep"))
+                      expert_dp_group=coord.get_group("expert_dp"), ep_group=coord.get_group("ep"),
+                      zero_stage=args.zero)
     start = 0
     if args.resume:
         start = load_checkpoint(args.resume, trainer.model, trainer.optimizer, trainer.scheduler)
@@ -112,9 +115,9 @@ def _save(args, trainer, step, sharded, rank, final=False):
     name = "checkpoint_final" if final else f"checkpoint_step_{step}"
     if sharded:
         save_sharded(os.path.join(args.output_dir, name), trainer.model, trainer.optimizer, trainer.scheduler, step)
-    elif rank == 0:
+    else:   # every rank takes part (ZeRO gathers the fp32 weights); rank 0 writes
         save_checkpoint(os.path.join(args.output_dir, name + ".pt"), trainer.model, trainer.optimizer,
-                        trainer.scheduler, step)
+                        trainer.scheduler, step, write=rank == 0)
 
 
 def main(argv=None):

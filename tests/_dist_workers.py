@@ -100,6 +100,30 @@ def dp_worker(rank, world):
         _check("param " + n, p.detach(), q.detach(), 1e-6)
 
 
+def dp_zero_worker(rank, world):
+    """ZeRO-1: sharded masters/moments give the same parameters as the unsharded optimizer."""
+    import tempfile
+    from mamformer_b200.checkpoint import load_checkpoint, save_checkpoint
+    cfg = tiny_config(moe=False)
+    ids = torch.randint(0, 256, (world, 32), generator=torch.Generator().manual_seed(1))
+    ref = _trainer(_build(cfg), mb=1, dp_group=dist.group.WORLD)
+    tr = _trainer(_build(cfg), mb=1, dp_group=dist.group.WORLD, zero_stage=1)
+    assert any(seg.sharded for _, seg in tr.optimizer.segments)
+    for step in range(2):
+        ref.train_step(ids[rank:rank + 1], sync_loss=True)
+        tr.train_step(ids[rank:rank + 1], sync_loss=True)
+    for (n, p), (_, q) in zip(tr.model.named_parameters(), ref.model.named_parameters()):
+        _check("param " + n, p.detach(), q.detach(), 1e-6)
+    _check("grad norm", tr.optimizer.last_grad_norm, ref.optimizer.last_grad_norm, 1e-5)
+    path = os.path.join(tempfile.gettempdir(), f"mamf_zero_{os.getppid()}.pt")
+    save_checkpoint(path, tr.model, tr.optimizer, step=2, write=rank == 0)
+    dist.barrier()
+    tr2 = _trainer(_build(cfg), mb=1, dp_group=dist.group.WORLD, zero_stage=1)
+    load_checkpoint(path, tr2.model, tr2.optimizer)
+    for (n, p), (_, q) in zip(tr2.model.named_parameters(), tr.model.named_parameters()):
+        _check("reloaded " + n, p.detach(), q.detach(), 0.0)
+
+
 # ---- expert parallel ------------------------------------------------------------------------------
 def ep_worker(rank, world):
     from mamformer_b200.parallel import (DistributedCoordinator, ParallelConfig, expert_parameters)

@@ -60,6 +60,10 @@ def test_data_parallel_matches_single_process():
     _spawn(W.dp_worker, 2)
 
 
+def test_zero1_sharded_optimizer_matches_unsharded():
+    _spawn(W.dp_zero_worker, 2)
+
+
 def test_expert_parallel_matches_single_process():
     _spawn(W.ep_worker, 2)
 
