@@ -75,3 +75,29 @@ def test_validation_errors():
         MamformerConfig(d_model=100, n_heads=3)
     with pytest.raises(ValueError):
         MamformerConfig(d_model=256, n_heads=4, n_kv_heads=3, head_dim=64)
+
+
+def test_kernels_namespace_cpu():
+    """Reference-named kernel API on the CPU path (``mamformer.kernels`` names)."""
+    import torch
+    from mamformer_b200 import kernels
+    from mamformer_b200.ops import reference as ref
+    torch.manual_seed(0)
+    B, H, S, hd = 1, 2, 16, 8
+    q1, q2, k, v = (torch.randn(B, H, S, hd) for _ in range(4))
+    o1, o2 = kernels.triton_linear_attn_scan(q1, q2, k, v, hd)
+    assert o1.shape == (B, H, S, hd) and o2.shape == (B, H, S, hd)
+    lam = torch.tensor([0.3, 0.5])
+    want = ref.linear_diff_attention_fp32(q1.transpose(1, 2), q2.transpose(1, 2), k.transpose(1, 2),
+                                          v.transpose(1, 2), lam, hd).transpose(1, 2)
+    got = (o1 - lam.view(1, -1, 1, 1) * o2) / (1 - lam.view(1, -1, 1, 1) + 1e-8)
+    assert torch.allclose(got, want, atol=3e-2, rtol=3e-2)
+    a = kernels.flash_attn_gqa(q1, k, v, sliding_window=4)
+    assert a.shape == q1.shape
+    d = kernels.flash_attn_dsa(q1, q2, k, v, 0.2)
+    assert d.shape == q1.shape
+    x = torch.randn(1, 8, 4)
+    y = kernels.triton_ssd_scan(x, torch.rand(1, 8, 4), torch.zeros(3), torch.randn(1, 8, 3), torch.randn(1, 8, 3),
+                                torch.ones(4))
+    assert y.shape == x.shape
+    assert isinstance(kernels.is_triton_available(), bool)
