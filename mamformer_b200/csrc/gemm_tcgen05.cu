@@ -47,6 +47,7 @@ struct Params {
   const int* tile_off;  // [G+1] cumulative m-tile counts (grouped-M)
   int n_tiles_n;
   int total_tiles;
+  int group_m;          // dense: tile raster walks group_m m-tiles before the next n-tile
   void* D;
   int64_t ldd;          // row stride of D (elements)
   int64_t d_gstride;    // grouped-K: stride between D[g] (elements)
@@ -161,10 +162,23 @@ __device__ __forceinline__ Tile tile_of(const Params& p, int t) {
     r.m0 = p.seg[lo] + (tm - p.tile_off[lo]) * BM;
     r.m_end = p.seg[lo + 1];
     r.n0 = tn;
+  } else if (MODE == 0) {
+    // grouped raster: the CTAs running at one time share a panel of group_m m-tiles (A rows stay
+    // in L2) and a few n-tiles, so each B tile is fetched from DRAM about once per panel
+    const int m_tiles = (p.M + BM - 1) / BM;
+    const int span = p.group_m * p.n_tiles_n;
+    const int grp = t / span, first = grp * p.group_m;
+    const int gm = min(p.group_m, m_tiles - first);
+    const int local = t - grp * span;
+    const int tm = first + local % gm, tn = local / gm;
+    r.g = 0;
+    r.m0 = tm * BM;
+    r.m_end = p.M;
+    r.n0 = tn;
   } else {
     const int per_g = ((p.M + BM - 1) / BM) * p.n_tiles_n;
-    r.g = (MODE == 2) ? t / per_g : 0;
-    const int tt = (MODE == 2) ? t - r.g * per_g : t;
+    r.g = t / per_g;
+    const int tt = t - r.g * per_g;
     const int tm = tt / p.n_tiles_n, tn = tt - tm * p.n_tiles_n;
     r.m0 = tm * BM;
     r.m_end = p.M;
@@ -525,6 +539,9 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
     p.total_tiles = p.G * ((M + BM - 1) / BM) * p.n_tiles_n;
   } else {
     p.total_tiles = ((M + BM - 1) / BM) * p.n_tiles_n;
+    const int64_t panel_bytes = (int64_t)BM * K * 2;           // one m-tile of A
+    const int m_tiles = (M + BM - 1) / BM;
+    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>({(int64_t)m_tiles, 32, (48ll << 20) / std::max<int64_t>(1, panel_bytes)}));
   }
   if (p.total_tiles == 0) return;
   const auto out = D.scalar_type();

@@ -23,7 +23,8 @@
 //   la_rprefix    reverse exclusive prefix over chunks, summing the group's query heads
 //   la_bwd_dqkv   per (b, g, c): loop over the group's heads and both queries: dq_m, and the
 //                 chunk's dk, dv (intra + reverse-state terms)
-// The per-thread work is a 4 x (cols/16) register tile of each 64 x cols product.
+// The per-thread work is a 4 x (cols/16) register tile of each 64 x cols product (rows and
+// columns strided by 16 over the threads; shared-memory rows padded by one word).
 #include "common.cuh"
 
 namespace mamf {
@@ -50,19 +51,26 @@ struct Params {
   int B, S, H, G, NC;
 };
 
-// Load `rows` rows (<= C) of an (B,S,heads,HD) tensor at (b, s0, head) into smem [C][ld] as fp32,
-// applying phi to the first K columns when PHI (columns >= K are dropped when ld == K).
-template <int K, int LD, bool PHI>
+// Shared-memory tiles are row-padded (stride cols + 1) and every thread owns rows r, r + 16,
+// r + 32, r + 48 and columns c, c + 16, ...: the 16 threads that read different rows of one
+// column hit 16 different banks, and threads that share a row read one broadcast word.
+template <int COLS>
+struct Pad { static constexpr int v = COLS + 1; };
+
+// Load `rows` rows (<= C) of an (B,S,heads,HD) tensor at (b, s0, head) into smem [C][COLS+1] as
+// fp32, applying phi when PHI (only the first COLS columns are loaded).
+template <int COLS, bool PHI>
 __device__ __forceinline__ void load_rows(float* dst, const __nv_bfloat16* src, int b, int s0, int rows, int head,
                                           int heads, int HD, int S) {
-  for (int idx = threadIdx.x; idx < C * LD; idx += NT) {
-    const int i = idx / LD, c = idx % LD;
+  constexpr int LDS = Pad<COLS>::v;
+  for (int idx = threadIdx.x; idx < C * COLS; idx += NT) {
+    const int i = idx / COLS, c = idx % COLS;
     float x = 0.f;
     if (i < rows) {
       x = __bfloat162float(src[(((int64_t)b * S + s0 + i) * heads + head) * HD + c]);
       if (PHI) x = phi_f(x);
     }
-    dst[i * LD + c] = x;
+    dst[i * LDS + c] = x;
   }
 }
 
@@ -70,12 +78,13 @@ __device__ __forceinline__ void load_rows(float* dst, const __nv_bfloat16* src, 
 template <int K, int HD>
 __global__ void __launch_bounds__(NT) la_state_kernel(Params p) {
   extern __shared__ float sm[];
-  float* sK = sm;                 // C x K
-  float* sV = sK + C * K;         // C x HD
+  constexpr int LK = Pad<K>::v, LD = Pad<HD>::v;
+  float* sK = sm;                 // C x LK
+  float* sV = sK + C * LK;        // C x LD
   const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int s0 = c * C, rows = min(C, p.S - s0);
-  load_rows<K, K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
-  load_rows<K, HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
   __syncthreads();
   constexpr int RK = K / 16, RD = HD / 16;
   const int tk = threadIdx.x / 16, td = threadIdx.x % 16;
@@ -87,9 +96,9 @@ __global__ void __launch_bounds__(NT) la_state_kernel(Params p) {
   for (int j = 0; j < rows; ++j) {
     float kk[RK], vv[RD];
 #pragma unroll
-    for (int a = 0; a < RK; ++a) kk[a] = sK[j * K + tk * RK + a];
+    for (int a = 0; a < RK; ++a) kk[a] = sK[j * LK + tk + 16 * a];
 #pragma unroll
-    for (int e = 0; e < RD; ++e) vv[e] = sV[j * HD + td * RD + e];
+    for (int e = 0; e < RD; ++e) vv[e] = sV[j * LD + td + 16 * e];
 #pragma unroll
     for (int a = 0; a < RK; ++a)
 #pragma unroll
@@ -99,10 +108,10 @@ __global__ void __launch_bounds__(NT) la_state_kernel(Params p) {
 #pragma unroll
   for (int a = 0; a < RK; ++a)
 #pragma unroll
-    for (int e = 0; e < RD; ++e) S[(tk * RK + a) * HD + td * RD + e] = acc[a][e];
+    for (int e = 0; e < RD; ++e) S[(tk + 16 * a) * HD + td + 16 * e] = acc[a][e];
   if (threadIdx.x < K) {
     float s = 0.f;
-    for (int j = 0; j < rows; ++j) s += sK[j * K + threadIdx.x];
+    for (int j = 0; j < rows; ++j) s += sK[j * LK + threadIdx.x];
     p.zs[(((int64_t)b * p.G + g) * p.NC + c) * K + threadIdx.x] = s;
   }
 }
@@ -128,42 +137,41 @@ __global__ void la_prefix_kernel(float* dst, const float* src, int64_t elems, in
   }
 }
 
-// A = tril(Pq Pk^T) for this thread's 4x4 tile -> smem sA (C x C)
+// A = tril(Pq Pk^T): thread (ti, tj) owns rows ti + 16x and columns tj + 16y
 template <int K>
 __device__ __forceinline__ void tile_A(float* sA, const float* sQ, const float* sK, int rows) {
+  constexpr int LK = Pad<K>::v, LC = Pad<C>::v;
   const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
   float a[4][4];
 #pragma unroll
   for (int x = 0; x < 4; ++x)
 #pragma unroll
     for (int y = 0; y < 4; ++y) a[x][y] = 0.f;
-  if (tj <= ti) {
-    for (int kk = 0; kk < K; ++kk) {
-      float q[4], k[4];
+  for (int kk = 0; kk < K; ++kk) {
+    float q[4], k[4];
 #pragma unroll
-      for (int x = 0; x < 4; ++x) q[x] = sQ[(ti * 4 + x) * K + kk];
+    for (int x = 0; x < 4; ++x) q[x] = sQ[(ti + 16 * x) * LK + kk];
 #pragma unroll
-      for (int y = 0; y < 4; ++y) k[y] = sK[(tj * 4 + y) * K + kk];
+    for (int y = 0; y < 4; ++y) k[y] = sK[(tj + 16 * y) * LK + kk];
 #pragma unroll
-      for (int x = 0; x < 4; ++x)
+    for (int x = 0; x < 4; ++x)
 #pragma unroll
-        for (int y = 0; y < 4; ++y) a[x][y] += q[x] * k[y];
-    }
+      for (int y = 0; y < 4; ++y) a[x][y] += q[x] * k[y];
   }
 #pragma unroll
   for (int x = 0; x < 4; ++x)
 #pragma unroll
     for (int y = 0; y < 4; ++y) {
-      const int i = ti * 4 + x, j = tj * 4 + y;
-      sA[i * C + j] = (j <= i && i < rows && j < rows) ? a[x][y] : 0.f;
+      const int i = ti + 16 * x, j = tj + 16 * y;
+      sA[i * LC + j] = (j <= i && i < rows && j < rows) ? a[x][y] : 0.f;
     }
 }
 
-// N (4 x HD/16 tile) = A V + Pq S; D (per row, in sD) = rowsum A + Pq . z
+// N (rows ti + 16x, columns td + 16e) = A V + Pq S; D (per row, in sD) = rowsum A + Pq . z
 template <int K, int HD>
 __device__ __forceinline__ void num_den(float (&n)[4][HD / 16], float* sD, const float* sA, const float* sV,
                                         const float* sQ, const float* S, const float* z, bool has_state) {
-  constexpr int RD = HD / 16;
+  constexpr int RD = HD / 16, LK = Pad<K>::v, LD = Pad<HD>::v, LC = Pad<C>::v;
   const int ti = threadIdx.x / 16, td = threadIdx.x % 16;
 #pragma unroll
   for (int x = 0; x < 4; ++x)
@@ -172,9 +180,9 @@ __device__ __forceinline__ void num_den(float (&n)[4][HD / 16], float* sD, const
   for (int j = 0; j < C; ++j) {
     float a[4], v[RD];
 #pragma unroll
-    for (int x = 0; x < 4; ++x) a[x] = sA[(ti * 4 + x) * C + j];
+    for (int x = 0; x < 4; ++x) a[x] = sA[(ti + 16 * x) * LC + j];
 #pragma unroll
-    for (int e = 0; e < RD; ++e) v[e] = sV[j * HD + td * RD + e];
+    for (int e = 0; e < RD; ++e) v[e] = sV[j * LD + td + 16 * e];
 #pragma unroll
     for (int x = 0; x < 4; ++x)
 #pragma unroll
@@ -184,9 +192,9 @@ __device__ __forceinline__ void num_den(float (&n)[4][HD / 16], float* sD, const
     for (int kk = 0; kk < K; ++kk) {
       float q[4], s[RD];
 #pragma unroll
-      for (int x = 0; x < 4; ++x) q[x] = sQ[(ti * 4 + x) * K + kk];
+      for (int x = 0; x < 4; ++x) q[x] = sQ[(ti + 16 * x) * LK + kk];
 #pragma unroll
-      for (int e = 0; e < RD; ++e) s[e] = S[kk * HD + td * RD + e];
+      for (int e = 0; e < RD; ++e) s[e] = S[kk * HD + td + 16 * e];
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
@@ -196,9 +204,9 @@ __device__ __forceinline__ void num_den(float (&n)[4][HD / 16], float* sD, const
   if (threadIdx.x < C) {
     const int i = threadIdx.x;
     float d = 0.f;
-    for (int j = 0; j < C; ++j) d += sA[i * C + j];
+    for (int j = 0; j < C; ++j) d += sA[i * LC + j];
     if (has_state)
-      for (int kk = 0; kk < K; ++kk) d += sQ[i * K + kk] * z[kk];
+      for (int kk = 0; kk < K; ++kk) d += sQ[i * LK + kk] * z[kk];
     sD[i] = d + 1e-8f;
   }
 }
@@ -206,26 +214,27 @@ __device__ __forceinline__ void num_den(float (&n)[4][HD / 16], float* sD, const
 template <int K, int HD>
 __global__ void __launch_bounds__(NT) la_fwd_kernel(Params p) {
   extern __shared__ float sm[];
-  float* sQ = sm;                  // C x K
-  float* sK = sQ + C * K;          // C x K
-  float* sV = sK + C * K;          // C x HD
-  float* sA = sV + C * HD;         // C x C
-  float* sD = sA + C * C;          // C
+  constexpr int LK = Pad<K>::v, LD = Pad<HD>::v, LC = Pad<C>::v;
+  float* sQ = sm;                   // C x LK
+  float* sK = sQ + C * LK;          // C x LK
+  float* sV = sK + C * LK;          // C x LD
+  float* sA = sV + C * LD;          // C x LC
+  float* sD = sA + C * LC;          // C
   constexpr int RD = HD / 16;
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int g = h / (p.H / p.G);
   const int s0 = c * C, rows = min(C, p.S - s0);
   const float* S = p.st + ((((int64_t)b * p.G + g) * p.NC + c) * K) * HD;
   const float* z = p.zs + (((int64_t)b * p.G + g) * p.NC + c) * K;
-  load_rows<K, K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
-  load_rows<K, HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
   const float lam = p.lam[h];
   const float inv = 1.f / (1.f - lam + 1e-8f);
   float o[4][RD];
   const int ti = threadIdx.x / 16, td = threadIdx.x % 16;
   for (int m = 0; m < 2; ++m) {
     __syncthreads();
-    load_rows<K, K, true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, HD, p.S);
+    load_rows<K, true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, HD, p.S);
     __syncthreads();
     tile_A<K>(sA, sQ, sK, rows);
     __syncthreads();
@@ -234,7 +243,7 @@ __global__ void __launch_bounds__(NT) la_fwd_kernel(Params p) {
     __syncthreads();
 #pragma unroll
     for (int x = 0; x < 4; ++x) {
-      const float rd = 1.f / sD[ti * 4 + x];
+      const float rd = 1.f / sD[ti + 16 * x];
 #pragma unroll
       for (int e = 0; e < RD; ++e) {
         const float val = n[x][e] * rd;
@@ -244,11 +253,11 @@ __global__ void __launch_bounds__(NT) la_fwd_kernel(Params p) {
   }
 #pragma unroll
   for (int x = 0; x < 4; ++x) {
-    const int i = ti * 4 + x;
+    const int i = ti + 16 * x;
     if (i >= rows) continue;
-    __nv_bfloat16* dst = p.out + (((int64_t)b * p.S + s0 + i) * p.H + h) * HD + td * RD;
+    __nv_bfloat16* dst = p.out + (((int64_t)b * p.S + s0 + i) * p.H + h) * HD;
 #pragma unroll
-    for (int e = 0; e < RD; ++e) dst[e] = __float2bfloat16(o[x][e]);
+    for (int e = 0; e < RD; ++e) dst[td + 16 * e] = __float2bfloat16(o[x][e]);
   }
 }
 
@@ -256,13 +265,14 @@ __global__ void __launch_bounds__(NT) la_fwd_kernel(Params p) {
 template <int K, int HD>
 __global__ void __launch_bounds__(NT) la_bwd_dn_kernel(Params p) {
   extern __shared__ float sm[];
-  float* sQ = sm;                   // C x K  (query m)
-  float* sK = sQ + C * K;
-  float* sV = sK + C * K;
-  float* sA = sV + C * HD;
-  float* sD = sA + C * C;           // C
-  float* sdN = sD + C;              // C x HD (dN of query m)
-  float* sdD = sdN + C * HD;        // C
+  constexpr int LK = Pad<K>::v, LD = Pad<HD>::v, LC = Pad<C>::v;
+  float* sQ = sm;                   // C x LK  (query m)
+  float* sK = sQ + C * LK;
+  float* sV = sK + C * LK;          // C x LD
+  float* sA = sV + C * LD;          // C x LC
+  float* sD = sA + C * LC;          // C
+  float* sdN = sD + C;              // C x LD (dN of query m)
+  float* sdD = sdN + C * LD;        // C
   float* sRed = sdD + C;            // 32
   constexpr int RD = HD / 16, RK = K / 16;
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -270,18 +280,18 @@ __global__ void __launch_bounds__(NT) la_bwd_dn_kernel(Params p) {
   const int s0 = c * C, rows = min(C, p.S - s0);
   const float* S = p.st + ((((int64_t)b * p.G + g) * p.NC + c) * K) * HD;
   const float* z = p.zs + (((int64_t)b * p.G + g) * p.NC + c) * K;
-  load_rows<K, K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
-  load_rows<K, HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
   const float lam = p.lam[h];
   const float inv = 1.f / (1.f - lam + 1e-8f);
   const int ti = threadIdx.x / 16, td = threadIdx.x % 16;
   float dout[4][RD], o1[4][RD];
 #pragma unroll
   for (int x = 0; x < 4; ++x) {
-    const int i = ti * 4 + x;
+    const int i = ti + 16 * x;
 #pragma unroll
     for (int e = 0; e < RD; ++e)
-      dout[x][e] = (i < rows) ? __bfloat162float(p.dout[(((int64_t)b * p.S + s0 + i) * p.H + h) * HD + td * RD + e])
+      dout[x][e] = (i < rows) ? __bfloat162float(p.dout[(((int64_t)b * p.S + s0 + i) * p.H + h) * HD + td + 16 * e])
                               : 0.f;
   }
   // chunk partial of the reverse state for this query head: dR = sum_m Pq_m^T dN_m, dr = sum_m Pq_m^T dD_m
@@ -295,7 +305,7 @@ __global__ void __launch_bounds__(NT) la_bwd_dn_kernel(Params p) {
   float dl = 0.f;
   for (int m = 0; m < 2; ++m) {
     __syncthreads();
-    load_rows<K, K, true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, HD, p.S);
+    load_rows<K, true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, HD, p.S);
     __syncthreads();
     tile_A<K>(sA, sQ, sK, rows);
     __syncthreads();
@@ -306,7 +316,7 @@ __global__ void __launch_bounds__(NT) la_bwd_dn_kernel(Params p) {
     // dN = cm dout / D;  dD = -(cm dout . o) / D  (row reduction over the 16 threads of a row)
 #pragma unroll
     for (int x = 0; x < 4; ++x) {
-      const int i = ti * 4 + x;
+      const int i = ti + 16 * x;
       const float rd = 1.f / sD[i];
       float part = 0.f;
 #pragma unroll
@@ -314,8 +324,7 @@ __global__ void __launch_bounds__(NT) la_bwd_dn_kernel(Params p) {
         const float o = n[x][e] * rd;
         if (m == 0) o1[x][e] = o;
         else dl += dout[x][e] * (o1[x][e] - o);
-        const float dn = cm * dout[x][e] * rd;
-        sdN[i * HD + td * RD + e] = dn;
+        sdN[i * LD + td + 16 * e] = cm * dout[x][e] * rd;
         part += cm * dout[x][e] * o;
       }
 #pragma unroll
@@ -326,29 +335,29 @@ __global__ void __launch_bounds__(NT) la_bwd_dn_kernel(Params p) {
     // store dN, dD for the dq/dk/dv kernel
     for (int idx = threadIdx.x; idx < rows * HD; idx += NT) {
       const int i = idx / HD, e = idx % HD;
-      p.dN[((((int64_t)b * p.S + s0 + i) * p.H + h) * 2 + m) * HD + e] = sdN[i * HD + e];
+      p.dN[((((int64_t)b * p.S + s0 + i) * p.H + h) * 2 + m) * HD + e] = sdN[i * LD + e];
     }
     if (threadIdx.x < rows) p.dD[(((int64_t)b * p.S + s0 + threadIdx.x) * p.H + h) * 2 + m] = sdD[threadIdx.x];
     // accumulate dR += Pq^T dN, dr += Pq^T dD over the chunk rows
     for (int i = 0; i < rows; ++i) {
       float q[RK], dn[RD];
 #pragma unroll
-      for (int a = 0; a < RK; ++a) q[a] = sQ[i * K + tk * RK + a];
+      for (int a = 0; a < RK; ++a) q[a] = sQ[i * LK + tk + 16 * a];
 #pragma unroll
-      for (int e = 0; e < RD; ++e) dn[e] = sdN[i * HD + td * RD + e];
+      for (int e = 0; e < RD; ++e) dn[e] = sdN[i * LD + td + 16 * e];
 #pragma unroll
       for (int a = 0; a < RK; ++a)
 #pragma unroll
         for (int e = 0; e < RD; ++e) accR[a][e] += q[a] * dn[e];
     }
     if (threadIdx.x < K)
-      for (int i = 0; i < rows; ++i) accr += sQ[i * K + threadIdx.x] * sdD[i];
+      for (int i = 0; i < rows; ++i) accr += sQ[i * LK + threadIdx.x] * sdD[i];
   }
   float* R = p.R + ((((int64_t)b * p.H + h) * p.NC + c) * K) * HD;
 #pragma unroll
   for (int a = 0; a < RK; ++a)
 #pragma unroll
-    for (int e = 0; e < RD; ++e) R[(tk * RK + a) * HD + td * RD + e] = accR[a][e];
+    for (int e = 0; e < RD; ++e) R[(tk + 16 * a) * HD + td + 16 * e] = accR[a][e];
   if (threadIdx.x < K) p.r[(((int64_t)b * p.H + h) * p.NC + c) * K + threadIdx.x] = accr;
   // dlam = sum dout . (o1 - o2) / (1 - lam)^2
   dl = warp_sum(dl);
@@ -364,13 +373,14 @@ __global__ void __launch_bounds__(NT) la_bwd_dn_kernel(Params p) {
 template <int K, int HD>
 __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
   extern __shared__ float sm[];
-  float* sK = sm;                   // C x K (phi k)
-  float* sV = sK + C * K;           // C x HD
-  float* sQ = sV + C * HD;          // C x K (phi q of the current head / query)
-  float* sdN = sQ + C * K;          // C x HD
-  float* sA = sdN + C * HD;         // C x C
-  float* sdA = sA + C * C;          // C x C
-  float* sdD = sdA + C * C;         // C
+  constexpr int LK = Pad<K>::v, LD = Pad<HD>::v, LC = Pad<C>::v;
+  float* sK = sm;                   // C x LK (phi k)
+  float* sV = sK + C * LK;          // C x LD
+  float* sQ = sV + C * LD;          // C x LK (phi q of the current head / query)
+  float* sdN = sQ + C * LK;         // C x LD
+  float* sA = sdN + C * LD;         // C x LC
+  float* sdA = sA + C * LC;         // C x LC
+  float* sdD = sdA + C * LC;        // C
   constexpr int RD = HD / 16, RK = K / 16;
   const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int groups = p.H / p.G;
@@ -379,8 +389,8 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
   const float* z = p.zs + (((int64_t)b * p.G + g) * p.NC + c) * K;
   const float* Rn = p.Rg + ((((int64_t)b * p.G + g) * p.NC + c) * K) * HD;
   const float* rn = p.rg + (((int64_t)b * p.G + g) * p.NC + c) * K;
-  load_rows<K, K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
-  load_rows<K, HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<K, true>(sK, p.k, b, s0, rows, g, p.G, HD, p.S);
+  load_rows<HD, false>(sV, p.v, b, s0, rows, g, p.G, HD, p.S);
   const int ti = threadIdx.x / 16, tc = threadIdx.x % 16;
   float dPk[4][RK], dVv[4][RD];
 #pragma unroll
@@ -394,10 +404,10 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
     const int h = g * groups + hh;
     for (int m = 0; m < 2; ++m) {
       __syncthreads();
-      load_rows<K, K, true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, HD, p.S);
+      load_rows<K, true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, HD, p.S);
       for (int idx = threadIdx.x; idx < C * HD; idx += NT) {
         const int i = idx / HD, e = idx % HD;
-        sdN[idx] = (i < rows) ? p.dN[((((int64_t)b * p.S + s0 + i) * p.H + h) * 2 + m) * HD + e] : 0.f;
+        sdN[i * LD + e] = (i < rows) ? p.dN[((((int64_t)b * p.S + s0 + i) * p.H + h) * 2 + m) * HD + e] : 0.f;
       }
       if (threadIdx.x < C)
         sdD[threadIdx.x] = (threadIdx.x < rows) ? p.dD[(((int64_t)b * p.S + s0 + threadIdx.x) * p.H + h) * 2 + m] : 0.f;
@@ -410,30 +420,27 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
         for (int x = 0; x < 4; ++x)
 #pragma unroll
           for (int y = 0; y < 4; ++y) a[x][y] = 0.f;
-        const int tj = tc;
-        if (tj <= ti) {
-          for (int e = 0; e < HD; ++e) {
-            float dn[4], vv[4];
+        for (int e = 0; e < HD; ++e) {
+          float dn[4], vv[4];
 #pragma unroll
-            for (int x = 0; x < 4; ++x) dn[x] = sdN[(ti * 4 + x) * HD + e];
+          for (int x = 0; x < 4; ++x) dn[x] = sdN[(ti + 16 * x) * LD + e];
 #pragma unroll
-            for (int y = 0; y < 4; ++y) vv[y] = sV[(tj * 4 + y) * HD + e];
+          for (int y = 0; y < 4; ++y) vv[y] = sV[(tc + 16 * y) * LD + e];
 #pragma unroll
-            for (int x = 0; x < 4; ++x)
+          for (int x = 0; x < 4; ++x)
 #pragma unroll
-              for (int y = 0; y < 4; ++y) a[x][y] += dn[x] * vv[y];
-          }
+            for (int y = 0; y < 4; ++y) a[x][y] += dn[x] * vv[y];
         }
 #pragma unroll
         for (int x = 0; x < 4; ++x)
 #pragma unroll
           for (int y = 0; y < 4; ++y) {
-            const int i = ti * 4 + x, j = tj * 4 + y;
-            sdA[i * C + j] = (j <= i && i < rows && j < rows) ? a[x][y] + sdD[i] : 0.f;
+            const int i = ti + 16 * x, j = tc + 16 * y;
+            sdA[i * LC + j] = (j <= i && i < rows && j < rows) ? a[x][y] + sdD[i] : 0.f;
           }
       }
       __syncthreads();
-      // dPq (4 x RK tile) = dA Pk + dN S^T + dD z  ->  dq
+      // dPq (rows ti + 16x, columns tc + 16a) = dA Pk + dN S^T + dD z  ->  dq
       {
         float dq[4][RK];
 #pragma unroll
@@ -443,9 +450,9 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
         for (int j = 0; j < C; ++j) {
           float da[4], kk[RK];
 #pragma unroll
-          for (int x = 0; x < 4; ++x) da[x] = sdA[(ti * 4 + x) * C + j];
+          for (int x = 0; x < 4; ++x) da[x] = sdA[(ti + 16 * x) * LC + j];
 #pragma unroll
-          for (int a = 0; a < RK; ++a) kk[a] = sK[j * K + tc * RK + a];
+          for (int a = 0; a < RK; ++a) kk[a] = sK[j * LK + tc + 16 * a];
 #pragma unroll
           for (int x = 0; x < 4; ++x)
 #pragma unroll
@@ -455,9 +462,9 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
           for (int e = 0; e < HD; ++e) {
             float dn[4], s[RK];
 #pragma unroll
-            for (int x = 0; x < 4; ++x) dn[x] = sdN[(ti * 4 + x) * HD + e];
+            for (int x = 0; x < 4; ++x) dn[x] = sdN[(ti + 16 * x) * LD + e];
 #pragma unroll
-            for (int a = 0; a < RK; ++a) s[a] = S[(tc * RK + a) * HD + e];
+            for (int a = 0; a < RK; ++a) s[a] = S[(tc + 16 * a) * HD + e];
 #pragma unroll
             for (int x = 0; x < 4; ++x)
 #pragma unroll
@@ -466,35 +473,35 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
 #pragma unroll
           for (int x = 0; x < 4; ++x)
 #pragma unroll
-            for (int a = 0; a < RK; ++a) dq[x][a] += sdD[ti * 4 + x] * z[tc * RK + a];
+            for (int a = 0; a < RK; ++a) dq[x][a] += sdD[ti + 16 * x] * z[tc + 16 * a];
         }
         __nv_bfloat16* dqp = (m == 0) ? p.dq1 : p.dq2;
         const __nv_bfloat16* qp = (m == 0) ? p.q1 : p.q2;
 #pragma unroll
         for (int x = 0; x < 4; ++x) {
-          const int i = ti * 4 + x;
+          const int i = ti + 16 * x;
           if (i >= rows) continue;
           const int64_t base = (((int64_t)b * p.S + s0 + i) * p.H + h) * HD;
 #pragma unroll
           for (int a = 0; a < RK; ++a) {
-            const int col = tc * RK + a;
+            const int col = tc + 16 * a;
             dqp[base + col] = __float2bfloat16(dq[x][a] * dphi_f(__bfloat162float(qp[base + col])));
           }
           for (int col = K + tc; col < HD; col += 16) dqp[base + col] = __float2bfloat16(0.f);
         }
       }
-      // dPk += dA^T Pq ;  dV += A^T dN   (rows j = ti*4+x of this thread)
+      // dPk += dA^T Pq ;  dV += A^T dN   (rows j = ti + 16x of this thread)
       for (int i = 0; i < C; ++i) {
         float da[4], aa[4], q[RK], dn[RD];
 #pragma unroll
         for (int x = 0; x < 4; ++x) {
-          da[x] = sdA[i * C + ti * 4 + x];
-          aa[x] = sA[i * C + ti * 4 + x];
+          da[x] = sdA[i * LC + ti + 16 * x];
+          aa[x] = sA[i * LC + ti + 16 * x];
         }
 #pragma unroll
-        for (int a = 0; a < RK; ++a) q[a] = sQ[i * K + tc * RK + a];
+        for (int a = 0; a < RK; ++a) q[a] = sQ[i * LK + tc + 16 * a];
 #pragma unroll
-        for (int e = 0; e < RD; ++e) dn[e] = sdN[i * HD + tc * RD + e];
+        for (int e = 0; e < RD; ++e) dn[e] = sdN[i * LD + tc + 16 * e];
 #pragma unroll
         for (int x = 0; x < 4; ++x) {
 #pragma unroll
@@ -510,9 +517,9 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
     for (int e = 0; e < HD; ++e) {
       float vv[4], Rr[RK];
 #pragma unroll
-      for (int x = 0; x < 4; ++x) vv[x] = sV[(ti * 4 + x) * HD + e];
+      for (int x = 0; x < 4; ++x) vv[x] = sV[(ti + 16 * x) * LD + e];
 #pragma unroll
-      for (int a = 0; a < RK; ++a) Rr[a] = Rn[(tc * RK + a) * HD + e];
+      for (int a = 0; a < RK; ++a) Rr[a] = Rn[(tc + 16 * a) * HD + e];
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
@@ -521,13 +528,13 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
 #pragma unroll
     for (int x = 0; x < 4; ++x)
 #pragma unroll
-      for (int a = 0; a < RK; ++a) dPk[x][a] += rn[tc * RK + a];
+      for (int a = 0; a < RK; ++a) dPk[x][a] += rn[tc + 16 * a];
     for (int kk = 0; kk < K; ++kk) {
       float pk[4], Rr[RD];
 #pragma unroll
-      for (int x = 0; x < 4; ++x) pk[x] = sK[(ti * 4 + x) * K + kk];
+      for (int x = 0; x < 4; ++x) pk[x] = sK[(ti + 16 * x) * LK + kk];
 #pragma unroll
-      for (int e = 0; e < RD; ++e) Rr[e] = Rn[kk * HD + tc * RD + e];
+      for (int e = 0; e < RD; ++e) Rr[e] = Rn[kk * HD + tc + 16 * e];
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
@@ -536,26 +543,26 @@ __global__ void __launch_bounds__(NT) la_bwd_dqkv_kernel(Params p) {
   }
 #pragma unroll
   for (int x = 0; x < 4; ++x) {
-    const int j = ti * 4 + x;
+    const int j = ti + 16 * x;
     if (j >= rows) continue;
     const int64_t base = (((int64_t)b * p.S + s0 + j) * p.G + g) * HD;
 #pragma unroll
     for (int a = 0; a < RK; ++a) {
-      const int col = tc * RK + a;
+      const int col = tc + 16 * a;
       p.dk[base + col] = __float2bfloat16(dPk[x][a] * dphi_f(__bfloat162float(p.k[base + col])));
     }
     for (int col = K + tc; col < HD; col += 16) p.dk[base + col] = __float2bfloat16(0.f);
 #pragma unroll
-    for (int e = 0; e < RD; ++e) p.dv[base + tc * RD + e] = __float2bfloat16(dVv[x][e]);
+    for (int e = 0; e < RD; ++e) p.dv[base + tc + 16 * e] = __float2bfloat16(dVv[x][e]);
   }
 }
 
 template <int K, int HD>
-constexpr int fwd_smem() { return (2 * C * K + C * HD + C * C + C) * 4; }
+constexpr int fwd_smem() { return (2 * C * Pad<K>::v + C * Pad<HD>::v + C * Pad<C>::v + C) * 4; }
 template <int K, int HD>
-constexpr int dn_smem() { return (2 * C * K + C * HD + C * C + C + C * HD + C + 32) * 4; }
+constexpr int dn_smem() { return (2 * C * Pad<K>::v + 2 * C * Pad<HD>::v + C * Pad<C>::v + 2 * C + 32) * 4; }
 template <int K, int HD>
-constexpr int dqkv_smem() { return (2 * C * K + 2 * C * HD + 2 * C * C + C) * 4; }
+constexpr int dqkv_smem() { return (2 * C * Pad<K>::v + 2 * C * Pad<HD>::v + 2 * C * Pad<C>::v + C) * 4; }
 
 template <typename F>
 static void set_smem(F k, int bytes) {
@@ -565,7 +572,7 @@ static void set_smem(F k, int bytes) {
 template <int K, int HD>
 static void run_states(Params& p) {
   dim3 gs(p.NC, p.G, p.B);
-  const int sm_state = (C * K + C * HD) * 4;
+  const int sm_state = (C * Pad<K>::v + C * Pad<HD>::v) * 4;
   set_smem(la_state_kernel<K, HD>, sm_state);
   la_state_kernel<K, HD><<<gs, NT, sm_state, stream()>>>(p);
   MAMF_LAUNCH_CHECK();

@@ -61,9 +61,11 @@ def test_moe_expert_outputs():
     assert out.shape == (100, 2, 128) and _rel(out, ro) < 2e-2
 
 
+@pytest.mark.parametrize("keep", ["4", "0"])          # logits kept for the backward / recomputed
 @pytest.mark.parametrize("T,V,d", [(300, 1000, 128), (2048, 32000, 256)])
-def test_linear_cross_entropy(T, V, d):
+def test_linear_cross_entropy(T, V, d, keep, monkeypatch):
     from mamformer_b200.ops import linear_ce
+    monkeypatch.setenv("MAMF_CE_SAVE_GB", keep)
     g = torch.Generator(device="cuda").manual_seed(3)
     h = torch.randn(T, d, device="cuda", generator=g).bfloat16().requires_grad_()
     W = (0.05 * torch.randn(V, d, device="cuda", generator=g)).bfloat16().requires_grad_()
