@@ -48,6 +48,12 @@ std::vector<at::Tensor> linear_attn_fwd(at::Tensor q1, at::Tensor q2, at::Tensor
                                         int64_t kernel_dim);
 std::vector<at::Tensor> linear_attn_bwd(at::Tensor q1, at::Tensor q2, at::Tensor k, at::Tensor v, at::Tensor lam,
                                         int64_t kernel_dim, at::Tensor Sst, at::Tensor zst, at::Tensor dout);
+std::vector<at::Tensor> router_topk(at::Tensor scores, int64_t k);
+at::Tensor router_topk_bwd(at::Tensor dg, at::Tensor gates, at::Tensor idx, int64_t E);
+at::Tensor expert_histogram(at::Tensor idx, int64_t E);
+std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, int64_t lo, int64_t hi, double scale);
+std::vector<at::Tensor> flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor lse,
+                                       at::Tensor dout, int64_t lo, int64_t hi, double scale);
 }  // namespace mamf
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -81,4 +87,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_clear_error", &mamf::comm_clear_error);
   m.def("linear_attn_fwd", &mamf::linear_attn_fwd);
   m.def("linear_attn_bwd", &mamf::linear_attn_bwd);
+  m.def("router_topk", &mamf::router_topk);
+  m.def("router_topk_bwd", &mamf::router_topk_bwd);
+  m.def("expert_histogram", &mamf::expert_histogram);
+  m.def("flash_attn_fwd", &mamf::flash_attn_fwd);
+  m.def("flash_attn_bwd", &mamf::flash_attn_bwd);
 }

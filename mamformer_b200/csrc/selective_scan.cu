@@ -7,12 +7,14 @@
 // Reference semantics: mamformer/layers/mamba2.py:70-130 (scan), 249-368 (block).
 //
 // Work split (sm_100a, 148 SMs): one CTA per (batch, 32-channel block); warp w owns states
-// [32w, 32w+32) of all 32 channels; lane = channel.  Each thread keeps its 32 states in
-// registers, so the time recurrence is 32 independent FMA chains per thread (ILP) and the
-// decay exp2 runs on the MUFU pipe.  Inputs of a 32-step chunk are staged in shared memory
-// (B/C rows are broadcast reads).  Reductions over channels (h_states, dB, dC) use a 5-step
-// in-warp reduce-scatter after which lane l holds the 32-channel sum for state 32w+l; the
-// per-block partial rows are written to [batch, channel-block, S, N] and summed by the caller.
+// [16w, 16w+16) of all 32 channels (N/16 warps per CTA); lane = channel.  Each thread keeps
+// its 16 states in registers, so the time recurrence is 16 independent FMA chains per thread
+// and the decay exp2 runs on the MUFU pipe.  Inputs of a 32-step chunk are staged in shared
+// memory (B/C rows are broadcast reads); the forward loads the next chunk into registers while
+// the current chunk's recurrence runs.  Reductions over channels (h_states, dB, dC) use an
+// in-warp reduce-scatter after which lanes 2s, 2s+1 hold the 32-channel sum for state 16w+s;
+// the per-block partial rows are written to [batch, channel-block, S, N] and summed by the
+// caller.  Forward per-warp partial outputs go to separate shared rows (no atomics).
 //
 // Backward: the forward stores the state at every 32-step chunk start (fp32).  The backward
 // walks chunks in reverse: phase A recomputes the chunk forward (saving 4-step
@@ -76,6 +78,40 @@ __device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
   return v[0];
 }
 
+// 16 values per lane: afterwards lanes 2s and 2s+1 both hold sum over the 32 lanes of v[s].
+__device__ __forceinline__ float reduce_scatter16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const bool up = lane & 16;
+    float send = up ? v[j] : v[j + 8];
+    float keep = up ? v[j + 8] : v[j];
+    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const bool up = lane & 8;
+    float send = up ? v[j] : v[j + 4];
+    float keep = up ? v[j + 4] : v[j];
+    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const bool up = lane & 4;
+    float send = up ? v[j] : v[j + 2];
+    float keep = up ? v[j + 2] : v[j];
+    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool up = lane & 2;
+    float send = up ? v[0] : v[1];
+    float keep = up ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+constexpr int SW = 16;      // states per warp (lane = channel, 32 channels per CTA)
+
 struct Params {
   int Bsz, S, Di, N, G, nck;
   // inputs: [b, t, c] / [b, t, n] with unit inner stride
@@ -99,7 +135,7 @@ struct Params {
   float* dB_part; float* dC_part;  // [Bsz, G, S, N]
   float* dA;                // [N]   (d loss / d A[n])
   float* dD;                // [Di]
-  float* scratch;           // per CTA: [CK/SUB][32][NT]
+  float* scratch;           // per CTA: [CK/SUB][SW][NT]
 };
 
 template <typename T>
@@ -108,10 +144,55 @@ __device__ __forceinline__ float ldf(const void* base, int64_t off) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Per-thread register staging of the next chunk's inputs (issued before the current chunk's
+// time loop, so the global-load latency overlaps the recurrence).
+template <typename T, int NT, int N>
+struct Stage {
+  static constexpr int NBC = (CK * N + NT - 1) / NT;     // B / C elements per thread
+  static constexpr int NXD = (CK * 32 + NT - 1) / NT;    // dt / x elements per thread
+  float b[NBC], c[NBC], d[NXD], x[NXD];
+
+  __device__ __forceinline__ void load(const Params& p, int b_, int cblk, int t0, int L) {
+#pragma unroll
+    for (int k = 0; k < NBC; ++k) {
+      const int i = threadIdx.x + k * NT;
+      const int tt = i / N, n = i - tt * N;
+      const bool ok = i < CK * N && tt < L;
+      b[k] = ok ? ldf<T>(p.Bm, (int64_t)b_ * p.B_bs + (int64_t)(t0 + tt) * p.B_ts + n) : 0.f;
+      c[k] = ok ? ldf<T>(p.Cm, (int64_t)b_ * p.C_bs + (int64_t)(t0 + tt) * p.C_ts + n) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < NXD; ++k) {
+      const int i = threadIdx.x + k * NT;
+      const int tt = i >> 5, cc = cblk * 32 + (i & 31);
+      const bool ok = i < CK * 32 && tt < L && cc < p.Di;
+      d[k] = ok ? ldf<T>(p.dt, (int64_t)b_ * p.dt_bs + (int64_t)(t0 + tt) * p.dt_ts + cc) : 0.f;
+      x[k] = ok ? ldf<T>(p.x, (int64_t)b_ * p.x_bs + (int64_t)(t0 + tt) * p.x_ts + cc) : 0.f;
+    }
+  }
+  template <bool SOFTPLUS>
+  __device__ __forceinline__ void store(float* sB, float* sC, float* sDt, float* sDtx) const {
+#pragma unroll
+    for (int k = 0; k < NBC; ++k) {
+      const int i = threadIdx.x + k * NT;
+      if (i < CK * N) { sB[i] = b[k]; sC[i] = c[k]; }
+    }
+#pragma unroll
+    for (int k = 0; k < NXD; ++k) {
+      const int i = threadIdx.x + k * NT;
+      if (i < CK * 32) {
+        const float dd = SOFTPLUS ? softplus_f(d[k]) : d[k];
+        sDt[i] = dd;
+        sDtx[i] = dd * x[k];
+      }
+    }
+  }
+};
+
 template <typename T, int NW, bool SOFTPLUS, bool GATE, bool HS>
 __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
   constexpr int NT = NW * 32;
-  const int N = NW * 32;
+  constexpr int N = NW * SW;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int b = blockIdx.y, cblk = blockIdx.x;
   const int c = cblk * 32 + lane;
@@ -122,52 +203,40 @@ __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
   float* sC = sB + CK * N;          // [CK][N]
   float* sDt = sC + CK * N;         // [CK][32]
   float* sDtx = sDt + CK * 32;      // [CK][32]
-  float* sY = sDtx + CK * 32;       // [CK][32]
+  float* sYw = sDtx + CK * 32;      // [NW][CK][32] per-warp partial outputs
 
-  float A2[32];
+  float A2[SW];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float al = fminf(fmaxf(p.A_log[w * 32 + j], -5.f), 5.f);
+  for (int j = 0; j < SW; ++j) {
+    float al = fminf(fmaxf(p.A_log[w * SW + j], -5.f), 5.f);
     A2[j] = -__expf(al) * LOG2E;
   }
-  float h[32];
+  float h[SW];
 #pragma unroll
-  for (int j = 0; j < 32; ++j)
-    h[j] = (p.h0 && cvalid) ? p.h0[((int64_t)b * p.Di + c) * N + w * 32 + j] : 0.f;
+  for (int j = 0; j < SW; ++j)
+    h[j] = (p.h0 && cvalid) ? p.h0[((int64_t)b * p.Di + c) * N + w * SW + j] : 0.f;
 
+  Stage<T, NT, N> st;
+  st.load(p, b, cblk, 0, min(CK, p.S));
   for (int t0 = 0, ck = 0; t0 < p.S; t0 += CK, ++ck) {
     const int L = min(CK, p.S - t0);
     if (p.ckpt && cvalid) {
-      float4* dst = reinterpret_cast<float4*>(p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + c) * N + w * 32);
+      float4* dst = reinterpret_cast<float4*>(p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + c) * N + w * SW);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+      for (int j = 0; j < SW / 4; ++j) dst[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < L * N; i += NT) {
-      const int tt = i / N, n = i - tt * N;
-      sB[i] = ldf<T>(p.Bm, (int64_t)b * p.B_bs + (int64_t)(t0 + tt) * p.B_ts + n);
-      sC[i] = ldf<T>(p.Cm, (int64_t)b * p.C_bs + (int64_t)(t0 + tt) * p.C_ts + n);
-    }
-    for (int i = threadIdx.x; i < L * 32; i += NT) {
-      const int tt = i >> 5, cc = cblk * 32 + (i & 31);
-      float d = 0.f, xv = 0.f;
-      if (cc < p.Di) {
-        d = ldf<T>(p.dt, (int64_t)b * p.dt_bs + (int64_t)(t0 + tt) * p.dt_ts + cc);
-        if (SOFTPLUS) d = softplus_f(d);
-        xv = ldf<T>(p.x, (int64_t)b * p.x_bs + (int64_t)(t0 + tt) * p.x_ts + cc);
-      }
-      sDt[i] = d;
-      sDtx[i] = d * xv;
-      sY[i] = 0.f;
-    }
+    st.template store<SOFTPLUS>(sB, sC, sDt, sDtx);
     __syncthreads();
+    if (t0 + CK < p.S) st.load(p, b, cblk, t0 + CK, min(CK, p.S - t0 - CK));   // next chunk in flight
+    float* yw = sYw + w * CK * 32;
     for (int tt = 0; tt < L; ++tt) {
       const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
-      const float4* Bt = reinterpret_cast<const float4*>(sB + tt * N + w * 32);
-      const float4* Ct = reinterpret_cast<const float4*>(sC + tt * N + w * 32);
+      const float4* Bt = reinterpret_cast<const float4*>(sB + tt * N + w * SW);
+      const float4* Ct = reinterpret_cast<const float4*>(sC + tt * N + w * SW);
       float yp = 0.f;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < SW / 4; ++q) {
         const float4 bq = Bt[q], cq = Ct[q];
         const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
         const float cc[4] = {cq.x, cq.y, cq.z, cq.w};
@@ -179,29 +248,33 @@ __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
           yp = fmaf(cc[r], h[j], yp);
         }
       }
-      atomicAdd(&sY[tt * 32 + lane], yp);
+      yw[tt * 32 + lane] = yp;
       if (HS) {
-        float tmp[32];
+        float tmp[SW];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) tmp[j] = h[j];
-        const float r = reduce_scatter32(tmp, lane);
-        p.hs_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * 32 + lane] = r;
+        for (int j = 0; j < SW; ++j) tmp[j] = h[j];
+        const float r = reduce_scatter16(tmp, lane);
+        if ((lane & 1) == 0)
+          p.hs_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
       }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < L * 32; i += NT) {
       const int tt = i >> 5, cc = cblk * 32 + (i & 31);
       if (cc >= p.Di) continue;
+      float yv = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < NW; ++ww) yv += sYw[ww * CK * 32 + i];
       const float xv = ldf<T>(p.x, (int64_t)b * p.x_bs + (int64_t)(t0 + tt) * p.x_ts + cc);
-      float yv = sY[i] + p.D[cc] * xv;
+      yv += p.D[cc] * xv;
       if (GATE) yv *= silu_f(ldf<T>(p.z, (int64_t)b * p.z_bs + (int64_t)(t0 + tt) * p.z_ts + cc));
       reinterpret_cast<T*>(p.y)[(int64_t)b * p.y_bs + (int64_t)(t0 + tt) * p.y_ts + cc] = from_f<T>(yv);
     }
   }
   if (p.final_state && cvalid) {
-    float* dst = p.final_state + ((int64_t)b * p.Di + c) * N + w * 32;
+    float* dst = p.final_state + ((int64_t)b * p.Di + c) * N + w * SW;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) dst[j] = h[j];
+    for (int j = 0; j < SW; ++j) dst[j] = h[j];
   }
 }
 
@@ -209,7 +282,7 @@ __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
 template <typename T, int NW, bool SOFTPLUS, bool GATE, bool HS>
 __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
   constexpr int NT = NW * 32;
-  const int N = NW * 32;
+  constexpr int N = NW * SW;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int b = blockIdx.y, cblk = blockIdx.x;
   const int c = cblk * 32 + lane;
@@ -229,18 +302,18 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
   float* sDD = sDU + CK * 32;
   float* sA2 = sDD + CK * 32;             // [N]
   float* sDsum = sA2 + N;                 // [32]
-  __nv_bfloat16* sG = reinterpret_cast<__nv_bfloat16*>(sDsum + 32);   // [SUB][32][NT]
+  __nv_bfloat16* sG = reinterpret_cast<__nv_bfloat16*>(sDsum + 32);   // [SUB][SW][NT]
 
   for (int i = tid; i < N; i += NT) {
     float al = fminf(fmaxf(p.A_log[i], -5.f), 5.f);
     sA2[i] = -__expf(al) * LOG2E;
   }
   if (tid < 32) sDsum[tid] = 0.f;
-  float* scratch = p.scratch + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * (CK / SUB) * 32 * NT;
+  float* scratch = p.scratch + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * (CK / SUB) * SW * NT;
 
-  float P[32], dAacc[32];
+  float P[SW], dAacc[SW];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) { P[j] = 0.f; dAacc[j] = 0.f; }
+  for (int j = 0; j < SW; ++j) { P[j] = 0.f; dAacc[j] = 0.f; }
   __syncthreads();
 
   for (int ck = p.nck - 1; ck >= 0; --ck) {
@@ -270,31 +343,32 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
 
     // ---- phase A: recompute the chunk forward --------------------------------------------
     {
-      float h[32];
-      const float* src = p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + (cvalid ? c : 0)) * N + w * 32;
+      float h[SW];
+      const float* src = p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + (cvalid ? c : 0)) * N + w * SW;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) h[j] = cvalid ? src[j] : 0.f;
+      for (int j = 0; j < SW; ++j) h[j] = cvalid ? src[j] : 0.f;
       for (int tt = 0; tt < L; ++tt) {
         if ((tt % SUB) == 0) {
-          float* dst = scratch + (int64_t)(tt / SUB) * 32 * NT;
+          float* dst = scratch + (int64_t)(tt / SUB) * SW * NT;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) dst[j * NT + tid] = h[j];
+          for (int j = 0; j < SW; ++j) dst[j * NT + tid] = h[j];
         }
         const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
-        const float* Bt = sB + tt * N + w * 32;
-        const float* Ct = sC + tt * N + w * 32;
+        const float* Bt = sB + tt * N + w * SW;
+        const float* Ct = sC + tt * N + w * SW;
         float yp = 0.f;
-        float tmp[32];
+        float tmp[SW];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float a = ex2(sA2[w * 32 + j] * d);
+        for (int j = 0; j < SW; ++j) {
+          const float a = ex2(sA2[w * SW + j] * d);
           h[j] = fmaf(a, h[j], Bt[j] * dxv);
           yp = fmaf(Ct[j], h[j], yp);
           tmp[j] = h[j] * dyp;
         }
         atomicAdd(&sY[tt * 32 + lane], yp);
-        const float r = reduce_scatter32(tmp, lane);
-        p.dC_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * 32 + lane] = r;
+        const float r = reduce_scatter16(tmp, lane);
+        if ((lane & 1) == 0)
+          p.dC_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
       }
     }
     __syncthreads();
@@ -322,39 +396,40 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
       // B1: G recurrence (reverse)
       for (int tt = s1 - 1; tt >= s0; --tt) {
         const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
-        const float* Bt = sB + tt * N + w * 32;
-        const float* Ct = sC + tt * N + w * 32;
-        const float* Ht = sDhs + tt * N + w * 32;
+        const float* Bt = sB + tt * N + w * SW;
+        const float* Ct = sC + tt * N + w * SW;
+        const float* Ht = sDhs + tt * N + w * SW;
         float du = 0.f;
-        float gb[32];
-        __nv_bfloat16* gdst = sG + (int64_t)(tt - s0) * 32 * NT + tid;
+        float gb[SW];
+        __nv_bfloat16* gdst = sG + (int64_t)(tt - s0) * SW * NT + tid;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < SW; ++j) {
           float G = fmaf(Ct[j], dyp, P[j]);
           if (HS) G += Ht[j];
           gdst[j * NT] = __float2bfloat16(G);
           du = fmaf(G, Bt[j], du);
           gb[j] = G * dxv;
-          P[j] = ex2(sA2[w * 32 + j] * d) * G;
+          P[j] = ex2(sA2[w * SW + j] * d) * G;
         }
         atomicAdd(&sDU[tt * 32 + lane], du);
-        const float r = reduce_scatter32(gb, lane);
-        p.dB_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * 32 + lane] = r;
+        const float r = reduce_scatter16(gb, lane);
+        if ((lane & 1) == 0)
+          p.dB_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
       }
       // B2: recompute h over the sub-chunk and form the decay gradients
       {
-        float h[32];
-        const float* src = scratch + (int64_t)sub * 32 * NT;
+        float h[SW];
+        const float* src = scratch + (int64_t)sub * SW * NT;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) h[j] = src[j * NT + tid];
+        for (int j = 0; j < SW; ++j) h[j] = src[j * NT + tid];
         for (int tt = s0; tt < s1; ++tt) {
           const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
-          const float* Bt = sB + tt * N + w * 32;
-          const __nv_bfloat16* gsrc = sG + (int64_t)(tt - s0) * 32 * NT + tid;
+          const float* Bt = sB + tt * N + w * SW;
+          const __nv_bfloat16* gsrc = sG + (int64_t)(tt - s0) * SW * NT + tid;
           float dd = 0.f;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float A2j = sA2[w * 32 + j];
+          for (int j = 0; j < SW; ++j) {
+            const float A2j = sA2[w * SW + j];
             const float a = ex2(A2j * d);
             const float v = a * h[j];
             h[j] = fmaf(Bt[j], dxv, v);
@@ -385,14 +460,14 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
   }
   __syncthreads();
   {
-    const float r = reduce_scatter32(dAacc, lane);
-    atomicAdd(&p.dA[w * 32 + lane], r);
+    const float r = reduce_scatter16(dAacc, lane);
+    if ((lane & 1) == 0) atomicAdd(&p.dA[w * SW + (lane >> 1)], r);
   }
   if (tid < 32 && cvalid) atomicAdd(&p.dD[c], sDsum[tid]);
 }
 
 // ---------------------------------------------------------------------------------------------
-inline size_t fwd_smem(int N) { return (size_t)(2 * CK * N + 3 * CK * 32) * sizeof(float); }
+inline size_t fwd_smem(int N) { return (size_t)(2 * CK * N + 2 * CK * 32 + (N / SW) * CK * 32) * sizeof(float); }
 inline size_t bwd_smem(int N, bool hs) {
   size_t f = (size_t)(2 * CK * N + (hs ? CK * N : 0) + 7 * CK * 32 + N + 32) * sizeof(float);
   return f + (size_t)SUB * 32 * N * sizeof(__nv_bfloat16);
@@ -401,7 +476,7 @@ inline size_t bwd_smem(int N, bool hs) {
 template <typename T, int NW, bool SP, bool GATE, bool HS>
 void launch_fwd(const Params& p) {
   auto k = scan_fwd_kernel<T, NW, SP, GATE, HS>;
-  size_t sm = fwd_smem(NW * 32);
+  size_t sm = fwd_smem(NW * SW);
   MAMF_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   dim3 grid((p.Di + 31) / 32, p.Bsz);
   k<<<grid, NW * 32, sm, stream()>>>(p);
@@ -411,7 +486,7 @@ void launch_fwd(const Params& p) {
 template <typename T, int NW, bool SP, bool GATE, bool HS>
 void launch_bwd(const Params& p) {
   auto k = scan_bwd_kernel<T, NW, SP, GATE, HS>;
-  size_t sm = bwd_smem(NW * 32, HS);
+  size_t sm = bwd_smem(NW * SW, HS);
   MAMF_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   dim3 grid((p.Di + 31) / 32, p.Bsz);
   k<<<grid, NW * 32, sm, stream()>>>(p);
@@ -434,9 +509,9 @@ void dispatch_flags(const Params& p, bool sp, bool gate, bool hs) {
 template <bool FWD, typename T>
 void dispatch_nw(const Params& p, bool sp, bool gate, bool hs) {
   switch (p.N) {
-    case 32: dispatch_flags<FWD, T, 1>(p, sp, gate, hs); break;
-    case 64: dispatch_flags<FWD, T, 2>(p, sp, gate, hs); break;
-    case 128: dispatch_flags<FWD, T, 4>(p, sp, gate, hs); break;
+    case 32: dispatch_flags<FWD, T, 2>(p, sp, gate, hs); break;
+    case 64: dispatch_flags<FWD, T, 4>(p, sp, gate, hs); break;
+    case 128: dispatch_flags<FWD, T, 8>(p, sp, gate, hs); break;
     default: TORCH_CHECK(false, "selective scan: d_state must be 32, 64 or 128, got ", p.N);
   }
 }

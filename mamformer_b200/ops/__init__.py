@@ -133,10 +133,12 @@ def attention(q, k, v, window: int = 0, window_mode: str = "reference",
               attention_mask: Optional[torch.Tensor] = None, dropout_p: float = 0.0):
     """GQA softmax attention, reference masking semantics (see models.attention)."""
     same_len = q.shape[1] == k.shape[1]
-    native_ok = (attention_mask is None and same_len and dropout_p == 0.0
-                 and (window <= 0 or window_mode == "causal"))
+    native_ok = attention_mask is None and same_len and dropout_p == 0.0
     if _native(q) and "attention" in NATIVE and native_ok:
-        lo, hi = _window_bounds(window, window_mode)
+        if window > 0 and window_mode == "reference":
+            lo, hi = 0, window - 1          # reference GQA window: 0 <= key - query < W, no causal mask
+        else:
+            lo, hi = _window_bounds(window, window_mode)
         return _nat().attention(q, k, v, lo, hi)
     if window > 0 and window_mode == "causal":
         S, Skv = q.shape[1], k.shape[1]

@@ -245,3 +245,83 @@ def linear_diff_attention(q1, q2, k, v, lam, kernel_dim, chunk=256, state=None, 
                                                return_state=return_state)
     return _LinearDiffAttn.apply(q1.contiguous(), q2.contiguous(), k.contiguous(), v.contiguous(), lam,
                                  kernel_dim)
+
+
+# ---------------------------------------------------------------------------------------------
+class _RouterTopK(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, scores, k):
+        gates, idx, _ = _C.router_topk(scores.float().contiguous(), int(k))
+        ctx.save_for_backward(gates, idx)
+        ctx.E = scores.shape[1]
+        ctx.dtype = scores.dtype
+        ctx.mark_non_differentiable(idx)
+        return gates, idx
+
+    @staticmethod
+    def backward(ctx, dg, didx):
+        gates, idx = ctx.saved_tensors
+        return _C.router_topk_bwd(dg, gates, idx, ctx.E).to(ctx.dtype), None
+
+
+@_register("router_topk", "csrc/router.cu")
+def router_topk(scores, k):
+    if scores.dim() != 2 or scores.shape[1] > 256 or k > 16:
+        from mamformer_b200.ops import reference
+        return reference.router_topk(scores, k)
+    return _RouterTopK.apply(scores, k)
+
+
+@_register("expert_histogram", "csrc/router.cu")
+def expert_histogram(idx, n_experts):
+    return _C.expert_histogram(idx, int(n_experts))
+
+
+# ---------------------------------------------------------------------------------------------
+_BIG = 1 << 30
+
+
+class _FlashAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, lo, hi, scale):
+        out, lse = _C.flash_attn_fwd(q, k, v, int(lo), int(hi), float(scale))
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.args = (int(lo), int(hi), float(scale))
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = _C.flash_attn_bwd(q, k, v, out, lse, dout.to(q.dtype).contiguous(), *ctx.args)
+        return dq, dk, dv, None, None, None
+
+
+def _fa_ok(q, k):
+    return q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and q.shape[-1] in (64, 128) \
+        and q.shape[2] % k.shape[2] == 0
+
+
+def flash_attention(q, k, v, lo=-_BIG, hi=0, scale=None):
+    """softmax(q k^T * scale) v over keys with lo <= key - query position <= hi; (B, S, H, hd)."""
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    return _FlashAttn.apply(q.contiguous(), k.contiguous(), v.contiguous(), lo, hi, scale)
+
+
+@_register("attention", "csrc/flash_attn.cu")
+def attention(q, k, v, lo, hi):
+    if not _fa_ok(q, k):
+        from mamformer_b200.ops import reference
+        return reference.attention_band(q, k, v, lo, hi)
+    return flash_attention(q, k, v, lo, hi)
+
+
+@_register("diff_attention", "csrc/flash_attn.cu")
+def diff_attention(q1, q2, k, v, lam, lo, hi, scale=None):
+    """(softmax(q1 k^T s) - lam softmax(q2 k^T s)) v / (1 - lam): two flash passes combined."""
+    if not _fa_ok(q1, k):
+        from mamformer_b200.ops import reference
+        return reference.diff_attention_band(q1, q2, k, v, lam, lo, hi, scale)
+    o1 = flash_attention(q1, k, v, lo, hi, scale)
+    o2 = flash_attention(q2, k, v, lo, hi, scale)
+    lam4 = lam.view(1, 1, -1, 1).to(o1.dtype)
+    return (o1 - lam4 * o2) / (1.0 - lam4 + 1e-8)

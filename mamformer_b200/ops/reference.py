@@ -329,3 +329,30 @@ def linear_cross_entropy(h: torch.Tensor, weight: torch.Tensor, labels: torch.Te
     logits = F.linear(h, weight.to(h.dtype))
     return F.cross_entropy(logits.float() if logits.dtype != torch.float32 else logits,
                            labels, ignore_index=ignore_index)
+
+
+def _band_mask(S, Skv, lo, hi, device, dtype):
+    iq = torch.arange(S, device=device).unsqueeze(1) + (Skv - S)
+    ik = torch.arange(Skv, device=device).unsqueeze(0)
+    dist = ik - iq
+    ok = (dist >= lo) & (dist <= hi)
+    return torch.zeros(S, Skv, device=device, dtype=dtype).masked_fill(~ok, float("-inf"))
+
+
+def attention_band(q, k, v, lo, hi, scale=None):
+    """GQA softmax attention over keys with lo <= key - query position <= hi (bshd)."""
+    groups = q.shape[2] // k.shape[2]
+    qt = q.transpose(1, 2).float()
+    kt = _expand_kv(k, groups).transpose(1, 2).float()
+    vt = _expand_kv(v, groups).transpose(1, 2).float()
+    s = (qt @ kt.transpose(-1, -2)) * (q.shape[-1] ** -0.5 if scale is None else scale)
+    s = s + _band_mask(q.shape[1], k.shape[1], lo, hi, q.device, s.dtype)
+    p = torch.softmax(s, -1).nan_to_num(0.0)
+    return (p @ vt).transpose(1, 2).to(q.dtype)
+
+
+def diff_attention_band(q1, q2, k, v, lam, lo, hi, scale=None):
+    o1 = attention_band(q1, k, v, lo, hi, scale)
+    o2 = attention_band(q2, k, v, lo, hi, scale)
+    lam4 = lam.view(1, 1, -1, 1).to(o1.dtype)
+    return (o1 - lam4 * o2) / (1.0 - lam4 + 1e-8)

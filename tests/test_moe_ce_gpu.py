@@ -81,3 +81,22 @@ def test_linear_cross_entropy(T, V, d, keep, monkeypatch):
     assert abs(loss.item() - lr.item()) < 2e-3 * lr.item()
     assert _rel(h.grad, hr.grad) < 3e-2
     assert _rel(W.grad, Wr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("T,E,k", [(1000, 128, 8), (77, 16, 4), (64, 256, 2)])
+def test_router_topk_and_histogram(T, E, k):
+    from mamformer_b200.ops import native
+    g = torch.Generator(device="cuda").manual_seed(7)
+    s = torch.randn(T, E, device="cuda", generator=g).requires_grad_()
+    gates, idx = native.router_topk(s, k)
+    sr = s.detach().clone().requires_grad_()
+    vr, ir = torch.topk(sr, k, dim=-1)
+    gr = torch.softmax(vr, -1)
+    assert torch.equal(idx, ir)
+    assert torch.allclose(gates, gr, atol=1e-5, rtol=1e-5)
+    dg = torch.randn(T, k, device="cuda", generator=g)
+    gates.backward(dg)
+    gr.backward(dg)
+    assert torch.allclose(s.grad, sr.grad, atol=1e-5, rtol=1e-4)
+    h = native.expert_histogram(idx, E)
+    assert torch.equal(h, torch.bincount(idx.flatten(), minlength=E))
