@@ -112,6 +112,16 @@ __device__ __forceinline__ float reduce_scatter16(float (&v)[16], int lane) {
 
 constexpr int SW = 16;      // states per warp (lane = channel, 32 channels per CTA)
 
+// 16 consecutive shared-memory floats (16-byte aligned) into registers with 4 vector loads
+__device__ __forceinline__ void ld_row16(float (&r)[16], const float* src) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 v = s4[q];
+    r[4 * q] = v.x; r[4 * q + 1] = v.y; r[4 * q + 2] = v.z; r[4 * q + 3] = v.w;
+  }
+}
+
 struct Params {
   int Bsz, S, Di, N, G, nck;
   // inputs: [b, t, c] / [b, t, n] with unit inner stride
@@ -311,10 +321,12 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
   if (tid < 32) sDsum[tid] = 0.f;
   float* scratch = p.scratch + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * (CK / SUB) * SW * NT;
 
-  float P[SW], dAacc[SW];
+  float P[SW], dAacc[SW], A2[SW];
 #pragma unroll
   for (int j = 0; j < SW; ++j) { P[j] = 0.f; dAacc[j] = 0.f; }
   __syncthreads();
+#pragma unroll
+  for (int j = 0; j < SW; ++j) A2[j] = sA2[w * SW + j];
 
   for (int ck = p.nck - 1; ck >= 0; --ck) {
     const int t0 = ck * CK;
@@ -354,13 +366,14 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
           for (int j = 0; j < SW; ++j) dst[j * NT + tid] = h[j];
         }
         const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
-        const float* Bt = sB + tt * N + w * SW;
-        const float* Ct = sC + tt * N + w * SW;
+        float Bt[SW], Ct[SW];
+        ld_row16(Bt, sB + tt * N + w * SW);
+        ld_row16(Ct, sC + tt * N + w * SW);
         float yp = 0.f;
         float tmp[SW];
 #pragma unroll
         for (int j = 0; j < SW; ++j) {
-          const float a = ex2(sA2[w * SW + j] * d);
+          const float a = ex2(A2[j] * d);
           h[j] = fmaf(a, h[j], Bt[j] * dxv);
           yp = fmaf(Ct[j], h[j], yp);
           tmp[j] = h[j] * dyp;
@@ -396,20 +409,25 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
       // B1: G recurrence (reverse)
       for (int tt = s1 - 1; tt >= s0; --tt) {
         const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
-        const float* Bt = sB + tt * N + w * SW;
-        const float* Ct = sC + tt * N + w * SW;
-        const float* Ht = sDhs + tt * N + w * SW;
+        float Bt[SW], Ct[SW], Ht[SW];
+        ld_row16(Bt, sB + tt * N + w * SW);
+        ld_row16(Ct, sC + tt * N + w * SW);
+        if (HS) ld_row16(Ht, sDhs + tt * N + w * SW);
         float du = 0.f;
         float gb[SW];
-        __nv_bfloat16* gdst = sG + (int64_t)(tt - s0) * SW * NT + tid;
+        uint32_t* gdst = reinterpret_cast<uint32_t*>(sG) + (int64_t)(tt - s0) * (SW / 2) * NT + tid;
 #pragma unroll
-        for (int j = 0; j < SW; ++j) {
-          float G = fmaf(Ct[j], dyp, P[j]);
-          if (HS) G += Ht[j];
-          gdst[j * NT] = __float2bfloat16(G);
-          du = fmaf(G, Bt[j], du);
-          gb[j] = G * dxv;
-          P[j] = ex2(sA2[w * SW + j] * d) * G;
+        for (int j = 0; j < SW; j += 2) {
+          float G0 = fmaf(Ct[j], dyp, P[j]), G1 = fmaf(Ct[j + 1], dyp, P[j + 1]);
+          if (HS) { G0 += Ht[j]; G1 += Ht[j + 1]; }
+          __nv_bfloat162 gp = __floats2bfloat162_rn(G0, G1);
+          gdst[(j / 2) * NT] = *reinterpret_cast<uint32_t*>(&gp);
+          du = fmaf(G0, Bt[j], du);
+          du = fmaf(G1, Bt[j + 1], du);
+          gb[j] = G0 * dxv;
+          gb[j + 1] = G1 * dxv;
+          P[j] = ex2(A2[j] * d) * G0;
+          P[j + 1] = ex2(A2[j + 1] * d) * G1;
         }
         atomicAdd(&sDU[tt * 32 + lane], du);
         const float r = reduce_scatter16(gb, lane);
@@ -424,18 +442,23 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
         for (int j = 0; j < SW; ++j) h[j] = src[j * NT + tid];
         for (int tt = s0; tt < s1; ++tt) {
           const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
-          const float* Bt = sB + tt * N + w * SW;
-          const __nv_bfloat16* gsrc = sG + (int64_t)(tt - s0) * SW * NT + tid;
+          float Bt[SW];
+          ld_row16(Bt, sB + tt * N + w * SW);
+          const uint32_t* gsrc = reinterpret_cast<const uint32_t*>(sG) + (int64_t)(tt - s0) * (SW / 2) * NT + tid;
           float dd = 0.f;
 #pragma unroll
-          for (int j = 0; j < SW; ++j) {
-            const float A2j = sA2[w * SW + j];
-            const float a = ex2(A2j * d);
-            const float v = a * h[j];
-            h[j] = fmaf(Bt[j], dxv, v);
-            const float gv = __bfloat162float(gsrc[j * NT]) * v;
-            dd = fmaf(gv, A2j, dd);
-            dAacc[j] = fmaf(gv, -d, dAacc[j]);
+          for (int j = 0; j < SW; j += 2) {
+            const uint32_t gw = gsrc[(j / 2) * NT];
+            const float2 gf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw));
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float a = ex2(A2[j + u] * d);
+              const float v = a * h[j + u];
+              h[j + u] = fmaf(Bt[j + u], dxv, v);
+              const float gv = (u == 0 ? gf.x : gf.y) * v;
+              dd = fmaf(gv, A2[j + u], dd);
+              dAacc[j + u] = fmaf(gv, -d, dAacc[j + u]);
+            }
           }
           atomicAdd(&sDD[tt * 32 + lane], dd);
         }

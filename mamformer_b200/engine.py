@@ -53,6 +53,9 @@ class Trainer:
         self.model = model
         if cfg.compute_dtype != torch.float32:
             to_compute_dtype(model, cfg.compute_dtype)
+            if next(model.parameters()).is_cuda:
+                from mamformer_b200.ops.linear import use_native_linear
+                use_native_linear(model)
         model.return_logits = False
         model.train()
         if cfg.gradient_checkpointing:

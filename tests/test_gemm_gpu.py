@@ -84,3 +84,28 @@ def test_grouped_m_and_k():
             assert _rel(dw[g], dy[rows].float().t() @ x[rows].float()) < 1e-2, g
         else:
             assert dw[g].abs().max() == 0
+
+
+@pytest.mark.parametrize("M,K,N,bias", [(4096, 1024, 512, False), (300, 256, 72, True)])
+def test_fused_linear_matches_torch(M, K, N, bias):
+    import torch.nn as nn
+    from mamformer_b200.ops.linear import FusedLinear, use_native_linear
+    torch.manual_seed(0)
+    ref = nn.Linear(K, N, bias=bias).cuda().bfloat16()
+    mod = nn.Linear(K, N, bias=bias).cuda().bfloat16()
+    mod.load_state_dict(ref.state_dict())
+    assert use_native_linear(mod) == 1 and isinstance(mod, FusedLinear)  # the root module itself
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    xr, xn = x.clone().requires_grad_(), x.clone().requires_grad_()
+    yr, yn = ref(xr), mod(xn)
+    assert (yn.float() - yr.float()).norm() / yr.float().norm() < 1e-2
+    g = torch.randn_like(yr)
+    yr.backward(g)
+    yn.backward(g)
+    for a, b in ((xn.grad, xr.grad), (mod.weight.grad, ref.weight.grad)):
+        assert (a.float() - b.float()).norm() / b.float().norm() < 2e-2
+    mod.weight.main_grad = torch.zeros(N, K, device="cuda")
+    mod.weight.grad = None
+    mod(xn).backward(g)
+    assert mod.weight.grad is None
+    assert (mod.weight.main_grad - ref.weight.grad.float()).norm() / ref.weight.grad.float().norm() < 2e-2
