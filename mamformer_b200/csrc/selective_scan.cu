@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
       const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
       const float4* Bt = reinterpret_cast<const float4*>(sB + tt * N + w * SW);
       const float4* Ct = reinterpret_cast<const float4*>(sC + tt * N + w * SW);
-      float yp = 0.f;
+      float yq[4] = {0.f, 0.f, 0.f, 0.f};     // 4 independent partial sums (short FMA chains)
 #pragma unroll
       for (int q = 0; q < SW / 4; ++q) {
         const float4 bq = Bt[q], cq = Ct[q];
@@ -255,10 +255,10 @@ __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
           const int j = 4 * q + r;
           const float a = ex2(A2[j] * d);
           h[j] = fmaf(a, h[j], bb[r] * dxv);
-          yp = fmaf(cc[r], h[j], yp);
+          yq[r] = fmaf(cc[r], h[j], yq[r]);
         }
       }
-      yw[tt * 32 + lane] = yp;
+      yw[tt * 32 + lane] = (yq[0] + yq[1]) + (yq[2] + yq[3]);
       if (HS) {
         float tmp[SW];
 #pragma unroll
@@ -369,16 +369,16 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
         float Bt[SW], Ct[SW];
         ld_row16(Bt, sB + tt * N + w * SW);
         ld_row16(Ct, sC + tt * N + w * SW);
-        float yp = 0.f;
+        float yq[4] = {0.f, 0.f, 0.f, 0.f};
         float tmp[SW];
 #pragma unroll
         for (int j = 0; j < SW; ++j) {
           const float a = ex2(A2[j] * d);
           h[j] = fmaf(a, h[j], Bt[j] * dxv);
-          yp = fmaf(Ct[j], h[j], yp);
+          yq[j & 3] = fmaf(Ct[j], h[j], yq[j & 3]);
           tmp[j] = h[j] * dyp;
         }
-        atomicAdd(&sY[tt * 32 + lane], yp);
+        atomicAdd(&sY[tt * 32 + lane], (yq[0] + yq[1]) + (yq[2] + yq[3]));
         const float r = reduce_scatter16(tmp, lane);
         if ((lane & 1) == 0)
           p.dC_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
         ld_row16(Bt, sB + tt * N + w * SW);
         ld_row16(Ct, sC + tt * N + w * SW);
         if (HS) ld_row16(Ht, sDhs + tt * N + w * SW);
-        float du = 0.f;
+        float duq[4] = {0.f, 0.f, 0.f, 0.f};
         float gb[SW];
         uint32_t* gdst = reinterpret_cast<uint32_t*>(sG) + (int64_t)(tt - s0) * (SW / 2) * NT + tid;
 #pragma unroll
@@ -422,14 +422,14 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
           if (HS) { G0 += Ht[j]; G1 += Ht[j + 1]; }
           __nv_bfloat162 gp = __floats2bfloat162_rn(G0, G1);
           gdst[(j / 2) * NT] = *reinterpret_cast<uint32_t*>(&gp);
-          du = fmaf(G0, Bt[j], du);
-          du = fmaf(G1, Bt[j + 1], du);
+          duq[j & 3] = fmaf(G0, Bt[j], duq[j & 3]);
+          duq[(j + 1) & 3] = fmaf(G1, Bt[j + 1], duq[(j + 1) & 3]);
           gb[j] = G0 * dxv;
           gb[j + 1] = G1 * dxv;
           P[j] = ex2(A2[j] * d) * G0;
           P[j + 1] = ex2(A2[j + 1] * d) * G1;
         }
-        atomicAdd(&sDU[tt * 32 + lane], du);
+        atomicAdd(&sDU[tt * 32 + lane], (duq[0] + duq[1]) + (duq[2] + duq[3]));
         const float r = reduce_scatter16(gb, lane);
         if ((lane & 1) == 0)
           p.dB_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
           float Bt[SW];
           ld_row16(Bt, sB + tt * N + w * SW);
           const uint32_t* gsrc = reinterpret_cast<const uint32_t*>(sG) + (int64_t)(tt - s0) * (SW / 2) * NT + tid;
-          float dd = 0.f;
+          float ddq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int j = 0; j < SW; j += 2) {
             const uint32_t gw = gsrc[(j / 2) * NT];
@@ -456,11 +456,11 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
               const float v = a * h[j + u];
               h[j + u] = fmaf(Bt[j + u], dxv, v);
               const float gv = (u == 0 ? gf.x : gf.y) * v;
-              dd = fmaf(gv, A2[j + u], dd);
+              ddq[(j + u) & 3] = fmaf(gv, A2[j + u], ddq[(j + u) & 3]);
               dAacc[j + u] = fmaf(gv, -d, dAacc[j + u]);
             }
           }
-          atomicAdd(&sDD[tt * 32 + lane], dd);
+          atomicAdd(&sDD[tt * 32 + lane], (ddq[0] + ddq[1]) + (ddq[2] + ddq[3]));
         }
       }
     }
