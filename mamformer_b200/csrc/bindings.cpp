@@ -54,6 +54,10 @@ at::Tensor expert_histogram(at::Tensor idx, int64_t E);
 std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, int64_t lo, int64_t hi, double scale);
 std::vector<at::Tensor> flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor lse,
                                        at::Tensor dout, int64_t lo, int64_t hi, double scale);
+void gemm_ag(std::vector<int64_t> a_ptrs, int64_t shard_rows, int64_t lda, int64_t rank, at::Tensor B, bool b_mn,
+             at::Tensor D);
+void gemm_rs(at::Tensor A, at::Tensor B, bool b_mn, std::vector<int64_t> d_ptrs, int64_t shard_rows, int64_t ldd,
+             int64_t rank);
 }  // namespace mamf
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -92,4 +96,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("expert_histogram", &mamf::expert_histogram);
   m.def("flash_attn_fwd", &mamf::flash_attn_fwd);
   m.def("flash_attn_bwd", &mamf::flash_attn_bwd);
+  m.def("gemm_ag", &mamf::gemm_ag);
+  m.def("gemm_rs", &mamf::gemm_rs);
 }

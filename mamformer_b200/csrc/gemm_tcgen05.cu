@@ -12,6 +12,13 @@
 //                 64); group g multiplies by B[g] (3-D B).  MoE: X_perm @ W_e^T and dH @ W_e.
 //   2 grouped-K : the contraction dim is split by `seg`; group g writes D[g] (3-D D).
 //                 MoE: dW_e = dY_e^T X_e.  `seg` must be 64-aligned (zero-padded rows).
+//   3 gathered-A: tensor-parallel all-gather -> GEMM.  A's rows are split into shards of
+//                 `shard_rows`; shard r is read by TMA (no multicast) from tensor map r, which
+//                 covers rank r's symmetric buffer (peer memory over NVLink); each rank starts
+//                 with its own shard, so the remote tiles stream in while local tiles compute.
+//   4 scattered-D: GEMM -> reduce-scatter.  Rows of shard r are written by the epilogue to
+//                 d_ptrs[r] (rank r's staging slot for this rank, peer memory over NVLink);
+//                 each rank starts with the next rank's shard and does its own last.
 //
 // Structure (one CTA per SM, 192 threads):
 //   warp 0      TMA producer (one lane): A/B tiles -> a STAGES-deep shared-memory ring,
@@ -48,6 +55,9 @@ struct Params {
   int n_tiles_n;
   int total_tiles;
   int group_m;          // dense: tile raster walks group_m m-tiles before the next n-tile
+  int shard_rows;       // modes 3 / 4: rows per rank shard (multiple of BM)
+  int rank_shift;       // modes 3 / 4: m-tile rotation (start position of this rank)
+  void* d_ptrs[8];      // mode 4: per-shard output base
   void* D;
   int64_t ldd;          // row stride of D (elements)
   int64_t d_gstride;    // grouped-K: stride between D[g] (elements)
@@ -162,7 +172,7 @@ __device__ __forceinline__ Tile tile_of(const Params& p, int t) {
     r.m0 = p.seg[lo] + (tm - p.tile_off[lo]) * BM;
     r.m_end = p.seg[lo + 1];
     r.n0 = tn;
-  } else if (MODE == 0) {
+  } else if (MODE == 0 || MODE == 3 || MODE == 4) {
     // grouped raster: the CTAs running at one time share a panel of group_m m-tiles (A rows stay
     // in L2) and a few n-tiles, so each B tile is fetched from DRAM about once per panel
     const int m_tiles = (p.M + BM - 1) / BM;
@@ -170,8 +180,10 @@ __device__ __forceinline__ Tile tile_of(const Params& p, int t) {
     const int grp = t / span, first = grp * p.group_m;
     const int gm = min(p.group_m, m_tiles - first);
     const int local = t - grp * span;
-    const int tm = first + local % gm, tn = local / gm;
-    r.g = 0;
+    int tm = first + local % gm;
+    const int tn = local / gm;
+    if (MODE >= 3) tm = (tm + p.rank_shift) % m_tiles;
+    r.g = (MODE >= 3) ? (tm * BM) / p.shard_rows : 0;
     r.m0 = tm * BM;
     r.m_end = p.M;
     r.n0 = tn;
@@ -199,9 +211,12 @@ __device__ __forceinline__ void k_range(const Params& p, const Tile& tl, int& k0
 }
 
 // ---- the kernel -----------------------------------------------------------------------------------
+struct MapSet { CUtensorMap m[8]; };   // mode 3: one A tensor map per rank shard
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, typename OutT, bool ACCUM>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p,
+            const __grid_constant__ MapSet tmAs) {
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -250,7 +265,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         uint8_t* sB = sA + A_BYTES;
         mbar_expect_tx(&full[stage], STAGE_BYTES);
         const int kk = k0 + kb * BK;
-        if (!A_MN) {
+        if (MODE == 3) {
+          tma_load_2d(sA, &tmAs.m[tl.g], &full[stage], kk, tl.m0 - tl.g * p.shard_rows);
+        } else if (!A_MN) {
           tma_load_2d(sA, &tmA, &full[stage], kk, tl.m0);
         } else {
 #pragma unroll
@@ -322,8 +339,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       tc_fence_after();
       const int row = tl.m0 + row_in_tile;
       const bool row_ok = row < tl.m_end;
-      OutT* dbase = reinterpret_cast<OutT*>(p.D) + (MODE == 2 ? (int64_t)tl.g * p.d_gstride : 0) +
-                    (int64_t)row * p.ldd;
+      OutT* dbase = (MODE == 4)
+          ? reinterpret_cast<OutT*>(p.d_ptrs[tl.g]) + (int64_t)(row - tl.g * p.shard_rows) * p.ldd
+          : reinterpret_cast<OutT*>(p.D) + (MODE == 2 ? (int64_t)tl.g * p.d_gstride : 0) + (int64_t)row * p.ldd;
       const int n_base = tl.n0 * BN;
       if (nk == 0) {
         // empty contraction (a group without rows): the accumulator was never written
@@ -423,24 +441,29 @@ static CUtensorMap make_map(const void* base, int rank, const uint64_t* dims, co
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, typename OutT, bool ACCUM>
-static void launch(const CUtensorMap& a, const CUtensorMap& b, const Params& p) {
+static void launch(const CUtensorMap& a, const CUtensorMap& b, const Params& p, const MapSet& as) {
   auto k = gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, OutT, ACCUM>;
   const int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   MAMF_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int grid = std::max(1, std::min(p.total_tiles, num_sms()));
-  k<<<grid, NUM_THREADS, smem, stream()>>>(a, b, p);
+  k<<<grid, NUM_THREADS, smem, stream()>>>(a, b, p, as);
   MAMF_LAUNCH_CHECK();
 }
 
 template <bool A_MN, bool B_MN, int MODE>
 static void dispatch_out(const CUtensorMap& a, const CUtensorMap& b, const Params& p, at::ScalarType out,
-                         bool accum, int bn) {
+                         bool accum, int bn, const MapSet& as = MapSet{}) {
   auto run = [&](auto bnc) {
     constexpr int BNV = decltype(bnc)::value;
     constexpr int ST = BNV == 256 ? 4 : 6;
-    if (out == at::kBFloat16 && !accum) return launch<BNV, ST, A_MN, B_MN, MODE, __nv_bfloat16, false>(a, b, p);
-    if (out == at::kFloat && !accum) return launch<BNV, ST, A_MN, B_MN, MODE, float, false>(a, b, p);
-    if (out == at::kFloat && accum) return launch<BNV, ST, A_MN, B_MN, MODE, float, true>(a, b, p);
+    if (MODE >= 3) {
+      TORCH_CHECK(out == at::kBFloat16 && !accum, "tensor-parallel gemm: bf16 output without accumulation");
+      return launch<BNV, ST, A_MN, B_MN, MODE, __nv_bfloat16, false>(a, b, p, as);
+    } else {
+      if (out == at::kBFloat16 && !accum) return launch<BNV, ST, A_MN, B_MN, MODE, __nv_bfloat16, false>(a, b, p, as);
+      if (out == at::kFloat && !accum) return launch<BNV, ST, A_MN, B_MN, MODE, float, false>(a, b, p, as);
+      if (out == at::kFloat && accum) return launch<BNV, ST, A_MN, B_MN, MODE, float, true>(a, b, p, as);
+    }
     TORCH_CHECK(false, "tcgen05 gemm: unsupported output configuration");
   };
   if (bn == 256) run(std::integral_constant<int, 256>{});
@@ -556,6 +579,89 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
   } else {
     dispatch_out<true, true, 2>(ma, mb, p, out, accumulate, bn);
   }
+}
+
+// ---- tensor-parallel fused GEMMs -------------------------------------------------------------------
+static void tp_common(gemm::Params& p, int M, int N, int K, int shard_rows, int rank, int P, bool b_mn,
+                      const at::Tensor& B, CUtensorMap& mb, int& bn) {
+  using namespace gemm;
+  TORCH_CHECK(P >= 1 && P <= 8 && rank >= 0 && rank < P, "tensor-parallel gemm: 1..8 ranks");
+  TORCH_CHECK(shard_rows % BM == 0 && M == shard_rows * P, "tensor-parallel gemm: shard rows must be a multiple of 128");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0, "tensor-parallel gemm: K and N multiples of 8");
+  p.M = M; p.N = N; p.K = K; p.G = 1;
+  p.shard_rows = shard_rows;
+  const int pad128 = (N + 127) / 128 * 128, pad256 = (N + 255) / 256 * 256;
+  bn = (N >= 256 && pad256 <= pad128) ? 256 : 128;
+  p.n_tiles_n = (N + bn - 1) / bn;
+  const int m_tiles = M / BM;
+  p.total_tiles = m_tiles * p.n_tiles_n;
+  p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>({(int64_t)m_tiles, 32, (48ll << 20) / ((int64_t)BM * K * 2)}));
+  const uint64_t esz = 2;
+  if (!b_mn) {
+    TORCH_CHECK(B.size(0) == N && B.size(1) == K, "tensor-parallel gemm: B (N, K)");
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)N}, st[1] = {(uint64_t)B.stride(0) * esz};
+    mb = make_map(B.data_ptr(), 2, dims, st, BK, bn);
+  } else {
+    TORCH_CHECK(B.size(0) == K && B.size(1) == N, "tensor-parallel gemm: B (K, N)");
+    uint64_t dims[2] = {(uint64_t)N, (uint64_t)K}, st[1] = {(uint64_t)B.stride(0) * esz};
+    mb = make_map(B.data_ptr(), 2, dims, st, 64, BK);
+  }
+}
+
+// All-gather -> GEMM: D (P*shard_rows, N) = [A_0; ...; A_{P-1}] B^T, A_r = rows at a_ptrs[r] (bf16,
+// row stride lda elements, K columns; peer pointers of a symmetric buffer).
+void gemm_ag(std::vector<int64_t> a_ptrs, int64_t shard_rows, int64_t lda, int64_t rank, at::Tensor B, bool b_mn,
+             at::Tensor D) {
+  using namespace gemm;
+  c10::cuda::CUDAGuard guard(D.device());
+  const int P = (int)a_ptrs.size();
+  TORCH_CHECK(B.scalar_type() == at::kBFloat16 && D.scalar_type() == at::kBFloat16 && B.stride(-1) == 1 &&
+              D.is_contiguous(), "gemm_ag: bf16 operands");
+  const int K = b_mn ? B.size(0) : B.size(1), N = D.size(1), M = D.size(0);
+  Params p{};
+  CUtensorMap mb;
+  int bn;
+  tp_common(p, M, N, K, (int)shard_rows, (int)rank, P, b_mn, B, mb, bn);
+  p.D = D.data_ptr();
+  p.ldd = D.stride(0);
+  p.alpha = 1.f;
+  p.rank_shift = (int)(rank * (shard_rows / BM));
+  MapSet as{};
+  for (int r = 0; r < P; ++r) {
+    TORCH_CHECK(a_ptrs[r] % 16 == 0 && (lda * 2) % 16 == 0, "gemm_ag: 16-byte aligned shards");
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)shard_rows}, st[1] = {(uint64_t)lda * 2};
+    as.m[r] = make_map(reinterpret_cast<void*>(a_ptrs[r]), 2, dims, st, BK, BM);
+  }
+  if (!b_mn) dispatch_out<false, false, 3>(as.m[0], mb, p, at::kBFloat16, false, bn, as);
+  else dispatch_out<false, true, 3>(as.m[0], mb, p, at::kBFloat16, false, bn, as);
+}
+
+// GEMM -> reduce-scatter: rows of shard r of A B^T are written to d_ptrs[r] (bf16, row stride ldd).
+void gemm_rs(at::Tensor A, at::Tensor B, bool b_mn, std::vector<int64_t> d_ptrs, int64_t shard_rows, int64_t ldd,
+             int64_t rank) {
+  using namespace gemm;
+  c10::cuda::CUDAGuard guard(A.device());
+  const int P = (int)d_ptrs.size();
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && A.stride(-1) == 1 &&
+              B.stride(-1) == 1, "gemm_rs: bf16 operands");
+  const int M = A.size(0), K = A.size(1), N = b_mn ? B.size(1) : B.size(0);
+  Params p{};
+  CUtensorMap mb;
+  int bn;
+  tp_common(p, M, N, K, (int)shard_rows, (int)rank, P, b_mn, B, mb, bn);
+  p.ldd = ldd;
+  p.alpha = 1.f;
+  TORCH_CHECK((ldd * 2) % 16 == 0, "gemm_rs: 16-byte row stride");
+  for (int r = 0; r < P; ++r) {
+    TORCH_CHECK(d_ptrs[r] % 16 == 0, "gemm_rs: 16-byte aligned outputs");
+    p.d_ptrs[r] = reinterpret_cast<void*>(d_ptrs[r]);
+  }
+  // start with the next rank's shard, finish with this rank's own
+  p.rank_shift = (int)(((rank + 1) % P) * (shard_rows / BM));
+  uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, st[1] = {(uint64_t)A.stride(0) * 2};
+  CUtensorMap ma = make_map(A.data_ptr(), 2, dims, st, BK, BM);
+  if (!b_mn) dispatch_out<false, false, 4>(ma, mb, p, at::kBFloat16, false, bn);
+  else dispatch_out<false, true, 4>(ma, mb, p, at::kBFloat16, false, bn);
 }
 
 int64_t gemm_error() {

@@ -1,0 +1,216 @@
+"""Sequence-parallel tensor parallelism with the collectives fused into the GEMMs over NVLink.
+
+Activations between TP blocks are sharded by rows (tokens) over the TP group.  A column-parallel
+linear needs the full sequence: its all-gather is fused into the GEMM (mode "gathered-A" of the
+tcgen05 kernel: the TMA producer reads every rank's row shard straight from that rank's
+symmetric-memory buffer - plain TMA loads of peer memory, no multicast - starting with the local
+shard so the remote tiles stream in while local tiles compute).  A row-parallel linear produces
+partial sums that must be reduced onto the owning rank: the reduce-scatter is fused into the GEMM
+epilogue (mode "scattered-D": every tile of shard r is stored straight into rank r's staging
+slot for this rank; each rank starts with the next rank's shard), followed by a local sum of the
+P slots.  A bounded signal-pad barrier (the expert-parallel barrier kernel) orders producers and
+consumers; nothing waits on the host.
+
+Reference: ``mamformer/parallelism/tensor_parallel.py`` (``_tp_all_gather`` 90-103,
+``_tp_reduce_scatter`` 105-121 - defined there but unused; ``ColumnParallelLinear`` 136-190,
+``RowParallelLinear`` 192-250).  Backward: the column layer's input gradient is a GEMM ->
+reduce-scatter, the row layer's input gradient an all-gather -> GEMM (the same two fused modes);
+weight gradients use the gathered operand (pulled over NVLink into a local buffer) and
+accumulate into the optimizer's fp32 buffer in the GEMM epilogue.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+_SLOT0 = 320      # signal-pad words used by this module's barrier (after the expert-parallel ones)
+
+
+class _Workspace:
+    """Per-group symmetric buffers: `gather` (rows x K, this rank's shard) and `stage`
+    (P x rows x N, partial sums written by the peers); grown collectively."""
+
+    def __init__(self, group):
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.gather = self.stage = None
+        self.hg = self.hs = None
+        self.n_gather = self.n_stage = 0
+        self.epoch = 0
+
+    def _alloc(self, numel, device):
+        import torch.distributed._symmetric_memory as symm
+        t = symm.empty(numel, dtype=torch.bfloat16, device=device)
+        return t, symm.rendezvous(t, self.group)
+
+    def ensure(self, n_gather: int, n_stage: int, device) -> None:
+        if n_gather > self.n_gather or n_stage > self.n_stage:
+            torch.cuda.current_stream(device).synchronize()
+        if n_gather > self.n_gather:
+            self.n_gather = (n_gather * 5 // 4 + 63) // 64 * 64
+            self.gather, self.hg = self._alloc(self.n_gather, device)
+        if n_stage > self.n_stage:
+            self.n_stage = (n_stage * 5 // 4 + 63) // 64 * 64
+            self.stage, self.hs = self._alloc(self.n_stage, device)
+
+    def barrier(self, C) -> None:
+        self.epoch += 1
+        C.ep_barrier(self.hg.signal_pad_ptrs, self.rank, self.epoch, _SLOT0)
+
+
+_WS = {}
+
+
+def _ws(group) -> _Workspace:
+    key = id(group)
+    if key not in _WS:
+        _WS[key] = _Workspace(group)
+    return _WS[key]
+
+
+def _C():
+    from mamformer_b200.ops._ext import require_native
+    return require_native()
+
+
+def ag_gemm(x_local: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False) -> torch.Tensor:
+    """all_gather_rows(x_local) @ w^T (w (N, K)), or @ w (w (K, N)) with ``b_mn``; x_local (rows, K)."""
+    C = _C()
+    ws = _ws(group)
+    rows, K = x_local.shape
+    N = w.shape[1] if b_mn else w.shape[0]
+    ws.ensure(rows * K, 0 if ws.stage is not None else 64, x_local.device)
+    ws.gather[: rows * K].view(rows, K).copy_(x_local)
+    ws.barrier(C)                                   # every shard written
+    out = torch.empty(ws.P * rows, N, device=x_local.device, dtype=torch.bfloat16)
+    C.gemm_ag(ws.hg.buffer_ptrs, rows, K, ws.rank, w, b_mn, out)
+    ws.barrier(C)                                   # every peer done reading the shards
+    return out
+
+
+def gemm_rs(y: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False) -> torch.Tensor:
+    """reduce_scatter_rows(y @ w^T) over the group: returns this rank's (rows / P, N) block."""
+    C = _C()
+    ws = _ws(group)
+    M, K = y.shape
+    P = ws.P
+    rows = M // P
+    N = w.shape[1] if b_mn else w.shape[0]
+    ws.ensure(64 if ws.gather is None else 0, P * rows * N, y.device)
+    base = [p_ + ws.rank * rows * N * 2 for p_ in ws.hs.buffer_ptrs]   # my slot in every peer's stage
+    C.gemm_rs(y.contiguous(), w, b_mn, base, rows, N, ws.rank)
+    ws.barrier(C)                                   # every partial landed
+    out = torch.empty(rows, N, device=y.device, dtype=torch.bfloat16)
+    stage = ws.stage[: P * rows * N].view(P * rows, N)
+    pos = (torch.arange(P, device=y.device).view(1, P) * rows + torch.arange(rows, device=y.device).view(rows, 1))
+    C.moe_combine(out, [stage.data_ptr()], N, torch.bfloat16, None, pos.reshape(-1), None, P, None)
+    ws.barrier(C)                                   # stage free for the next call
+    return out
+
+
+def gather_rows(x_local: torch.Tensor, group) -> torch.Tensor:
+    """Plain all-gather of row shards (NCCL), for the weight-gradient operands."""
+    P = dist.get_world_size(group)
+    out = torch.empty(P * x_local.shape[0], *x_local.shape[1:], device=x_local.device, dtype=x_local.dtype)
+    dist.all_gather_into_tensor(out, x_local.contiguous(), group=group)
+    return out
+
+
+def _wgrad(w, dy, x):
+    from mamformer_b200.ops import gemm
+    from mamformer_b200.optim import mark_grad_ready
+    mg = getattr(w, "main_grad", None)
+    if mg is not None:
+        gemm.mm_tn_acc(dy, x, mg, accumulate=True)
+        mark_grad_ready(w)
+        return None
+    dw = torch.zeros(w.shape, device=w.device, dtype=torch.float32)
+    gemm.mm_tn_acc(dy, x, dw, accumulate=True)
+    return dw.to(w.dtype)
+
+
+class _AGLinear(torch.autograd.Function):
+    """y (T, n) = all_gather(x) W^T ; x (T/P, K) row shard, W (n, K) column shard."""
+
+    @staticmethod
+    def forward(ctx, x, w, group):
+        ctx.save_for_backward(x, w)
+        ctx.group = group
+        return ag_gemm(x, w, group)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = gemm_rs(dy, w, ctx.group, b_mn=True)            # reduce_scatter(dy W)
+        dw = _wgrad(w, dy, gather_rows(x, ctx.group))
+        return dx, dw, None
+
+
+class _RSLinear(torch.autograd.Function):
+    """z (T/P, d) = reduce_scatter(y W^T) ; y (T, n) full rows of this rank's channel shard."""
+
+    @staticmethod
+    def forward(ctx, y, w, group):
+        ctx.save_for_backward(y, w)
+        ctx.group = group
+        return gemm_rs(y, w, group)
+
+    @staticmethod
+    def backward(ctx, dz):
+        y, w = ctx.saved_tensors
+        dz = dz.contiguous()
+        dy = ag_gemm(dz, w, ctx.group, b_mn=True)            # all_gather(dz) W
+        dw = _wgrad(w, gather_rows(dz, ctx.group), y)
+        return dy, dw, None
+
+
+class SequenceParallelColumnLinear(nn.Module):
+    """Column-parallel linear fed by row-sharded activations (fused all-gather -> GEMM)."""
+
+    def __init__(self, in_features: int, out_features: int, group, init_std: float = 0.02):
+        super().__init__()
+        self.group = group
+        P = dist.get_world_size(group)
+        assert out_features % P == 0
+        self.weight = nn.Parameter(torch.empty(out_features // P, in_features))
+        nn.init.normal_(self.weight, std=init_std)
+
+    def forward(self, x):
+        shp = x.shape
+        y = _AGLinear.apply(x.reshape(-1, shp[-1]), self.weight, self.group)
+        return y.view(-1, *shp[1:-1], self.weight.shape[0]) if x.dim() > 2 else y
+
+
+class SequenceParallelRowLinear(nn.Module):
+    """Row-parallel linear whose output is reduce-scattered by rows (fused GEMM -> RS)."""
+
+    def __init__(self, in_features: int, out_features: int, group, init_std: float = 0.02):
+        super().__init__()
+        self.group = group
+        P = dist.get_world_size(group)
+        assert in_features % P == 0
+        self.weight = nn.Parameter(torch.empty(out_features, in_features // P))
+        nn.init.normal_(self.weight, std=init_std)
+
+    def forward(self, y):
+        return _RSLinear.apply(y.reshape(-1, y.shape[-1]), self.weight, self.group)
+
+
+class SequenceParallelSwiGLU(nn.Module):
+    """SwiGLU FFN in the sequence-parallel TP layout: x (T/P, d) -> (T/P, d)."""
+
+    def __init__(self, d_model: int, d_ff: int, group):
+        super().__init__()
+        self.gate_proj = SequenceParallelColumnLinear(d_model, d_ff, group)
+        self.up_proj = SequenceParallelColumnLinear(d_model, d_ff, group)
+        self.down_proj = SequenceParallelRowLinear(d_ff, d_model, group)
+
+    def forward(self, x):
+        from mamformer_b200 import ops
+        return self.down_proj(ops.swiglu(self.gate_proj(x), self.up_proj(x)))

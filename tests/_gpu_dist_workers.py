@@ -83,3 +83,44 @@ def dp_trainer_worker(rank, world):
         other = p.detach().clone()
         dist.broadcast(other, 0)
         assert torch.equal(other, p.detach()), n
+
+
+def tp_fused_worker(rank, world):
+    """Fused all-gather->GEMM and GEMM->reduce-scatter (and their autograd) against NCCL + torch."""
+    from mamformer_b200.parallel import tp_fused
+    g = dist.group.WORLD
+    torch.manual_seed(0)
+    T, K, N = 512 * world, 1024, 768
+    rows = T // world
+    x_full = (torch.randn(T, K, device="cuda") * 0.5).bfloat16()
+    W = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    x_loc = x_full[rank * rows:(rank + 1) * rows].contiguous()
+    y = tp_fused.ag_gemm(x_loc, W, g)
+    want = (x_full.float() @ W.float().t())
+    assert _rel(y, want) < 1e-2, _rel(y, want)
+    # reduce-scatter: every rank holds a different partial product
+    parts = [(torch.randn(T, K, device="cuda", generator=torch.Generator(device="cuda").manual_seed(10 + r)) * 0.5).bfloat16()
+             for r in range(world)]
+    z = tp_fused.gemm_rs(parts[rank], W, g)
+    full = sum(p_.float() @ W.float().t() for p_ in parts)
+    assert _rel(z, full[rank * rows:(rank + 1) * rows]) < 1e-2
+    # autograd through the sequence-parallel SwiGLU against the unsharded FFN
+    d, ff = 256, 512
+    torch.manual_seed(1)
+    wg, wu, wd = (torch.randn(ff, d, device="cuda") * 0.05, torch.randn(ff, d, device="cuda") * 0.05,
+                  torch.randn(d, ff, device="cuda") * 0.05)
+    m = tp_fused.SequenceParallelSwiGLU(d, ff, g).cuda().bfloat16()
+    sl = slice(rank * ff // world, (rank + 1) * ff // world)
+    with torch.no_grad():
+        m.gate_proj.weight.copy_(wg[sl]); m.up_proj.weight.copy_(wu[sl]); m.down_proj.weight.copy_(wd[:, sl])
+    xs = (torch.randn(T, d, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3)) * 0.5).bfloat16()
+    xl = xs[rank * rows:(rank + 1) * rows].clone().requires_grad_()
+    out = m(xl)
+    xr = xs.float().clone().requires_grad_()
+    ref = (torch.nn.functional.silu(xr @ wg.t()) * (xr @ wu.t())) @ wd.t()
+    assert _rel(out, ref[rank * rows:(rank + 1) * rows]) < 2e-2
+    go = torch.randn(T, d, device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+    out.backward(go[rank * rows:(rank + 1) * rows].bfloat16())
+    ref.backward(go)
+    assert _rel(xl.grad, xr.grad[rank * rows:(rank + 1) * rows]) < 3e-2
+    torch.cuda.synchronize()

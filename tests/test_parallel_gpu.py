@@ -54,3 +54,8 @@ def test_data_parallel_trainer_two_gpus():
 @needs2
 def test_expert_parallel_moe_two_gpus():
     _spawn("ep_moe_worker", 2)
+
+
+@needs2
+def test_tp_fused_gemms_two_gpus():
+    _spawn("tp_fused_worker", 2)
