@@ -79,7 +79,7 @@ class Trainer:
         self.skipped_steps = 0
 
     def train_step(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
-                   sync_loss: bool = False):
+                   sync_loss: bool = False, check_grads: bool = False):
         """One optimizer step.  ``input_ids`` (micro_batch*grad_accum, S) on the device or in
         (pinned) host memory.  Returns the mean loss (device tensor, or float if sync_loss)."""
         cfg = self.cfg
@@ -114,6 +114,18 @@ class Trainer:
                 self.skipped_steps += 1
                 self.optimizer.zero_grad()
                 return loss_val
+        if check_grads:
+            # non-finite gradient: zero and skip (reference train.py:436-447); the flag is
+            # reduced over the data-parallel group so every rank takes the same decision
+            from mamformer_b200.fault import grads_finite
+            self.optimizer.reduce_gradients()
+            ok = torch.tensor([1.0 if grads_finite(self.optimizer) else 0.0], device=self.device)
+            if self.dp_group is not None and dist.is_initialized() and dist.get_world_size(self.dp_group) > 1:
+                dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.dp_group)
+            if float(ok) < 1.0:
+                self.skipped_steps += 1
+                self.optimizer.zero_grad()
+                return loss_val if sync_loss else self._loss_acc
         self.optimizer.step()
         self.scheduler.step()
         self.step_count += 1
