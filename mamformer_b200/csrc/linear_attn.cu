@@ -26,6 +26,7 @@
 // The per-thread work is a 4 x (cols/16) register tile of each 64 x cols product (rows and
 // columns strided by 16 over the threads; shared-memory rows padded by one word).
 #include "common.cuh"
+#include "warp_mma.cuh"
 
 namespace mamf {
 namespace la {
@@ -583,6 +584,529 @@ static void run_states(Params& p) {
   MAMF_LAUNCH_CHECK();
 }
 
+
+// =================================================================================================
+// Tensor-core path (K = HD = 128): the same chunk algorithm with every chunk product on warp-level
+// mma.sync tiles (bf16 operands, fp32 accumulation).  4 warps x 16 rows per 64-row chunk.  The chunk
+// state S (and z as an extra column) enters as a bf16 operand.
+namespace tc {
+constexpr int C = 64, NT = 128, D = 128;
+constexpr int LB = D + 8;          // bf16 tile row stride (elements)
+constexpr int LSX = D + 24;        // state tile [K][D + 16 (z column, zero pad)] + 8
+constexpr int LC = C + 8;          // 64-wide tiles
+
+// rows x 128 bf16 tile of (B, S, heads, 128) into smem (zero past `rows`), phi applied when PHI
+template <bool PHI>
+__device__ __forceinline__ void load_bf(__nv_bfloat16* dst, const __nv_bfloat16* src, int b, int s0, int rows,
+                                        int head, int heads, int S) {
+  for (int i = threadIdx.x; i < C * (D / 8); i += NT) {
+    const int r = i / (D / 8), c = (i % (D / 8)) * 8;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (r < rows) v = *reinterpret_cast<const int4*>(src + (((int64_t)b * S + s0 + r) * heads + head) * D + c);
+    if (PHI) {
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16(r < rows ? phi_f(__bfloat162float(e[k])) : 0.f);
+    }
+    *reinterpret_cast<int4*>(dst + r * LB + c) = v;
+  }
+}
+// fp32 state (K x D) (+ z column) -> bf16 smem [K][LSX]
+__device__ __forceinline__ void load_state(__nv_bfloat16* dst, const float* S, const float* z, bool has) {
+  for (int i = threadIdx.x; i < D * (D + 16); i += NT) {
+    const int r = i / (D + 16), c = i % (D + 16);
+    float v = 0.f;
+    if (has) v = c < D ? S[r * D + c] : (c == D && z ? z[r] : 0.f);
+    dst[r * LSX + c] = __float2bfloat16(v);
+  }
+}
+
+// Q fragments (this warp's 16 rows, K = 128)
+__device__ __forceinline__ void q_frags(uint32_t (&qf)[8][4], const __nv_bfloat16* sQ, int w, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) wm::ldsm_x4(qf[kk], sQ + (w * 16 + wm::a_row(lane)) * LB + kk * 16 + wm::a_col(lane));
+}
+// a (16 x 64) = tril(Q K^T) for this warp's rows
+__device__ __forceinline__ void scores(float (&a)[8][4], const uint32_t (&qf)[8][4], const __nv_bfloat16* sK, int w,
+                                       int lane, int rows) {
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[n][e] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+    for (int n = 0; n < 8; n += 2) {
+      uint32_t bf[4];
+      wm::ldsm_x4(bf, sK + (n * 8 + wm::bn_row(lane)) * LB + kk * 16 + wm::bn_col(lane));
+      wm::mma16816(a[n], qf[kk], bf[0], bf[1]);
+      wm::mma16816(a[n + 1], qf[kk], bf[2], bf[3]);
+    }
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = w * 16 + g + (e >> 1) * 8, j = n * 8 + 2 * t + (e & 1);
+      if (!(j <= i && i < rows && j < rows)) a[n][e] = 0.f;
+    }
+}
+// u (16 x 144) = A V + Q [S | z]; u[:, 128] = Q . z
+__device__ __forceinline__ void numer(float (&u)[18][4], const float (&a)[8][4], const uint32_t (&qf)[8][4],
+                                      const __nv_bfloat16* sV, const __nv_bfloat16* sS, int lane, bool has) {
+#pragma unroll
+  for (int n = 0; n < 18; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) u[n][e] = 0.f;
+  // A enters as hi + lo bf16 parts: the scores of the positive feature map are nearly uniform, so
+  // the two reads' outputs are close and the differential combination (and d lambda) would
+  // otherwise inherit the 2^-9 rounding of A.
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t pa[4], pl[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float x0 = a[2 * j + (e >> 1)][(e & 1) * 2], x1 = a[2 * j + (e >> 1)][(e & 1) * 2 + 1];
+      const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+      const float2 hf = __bfloat1622float2(h);
+      pa[e] = *reinterpret_cast<const uint32_t*>(&h);
+      pl[e] = wm::pack_bf16(x0 - hf.x, x1 - hf.y);
+    }
+#pragma unroll
+    for (int n = 0; n < 16; n += 2) {
+      uint32_t bf[4];
+      wm::ldsm_x4_t(bf, sV + (j * 16 + wm::bt_row(lane)) * LB + n * 8 + wm::bt_col(lane));
+      wm::mma16816(u[n], pa, bf[0], bf[1]);
+      wm::mma16816(u[n + 1], pa, bf[2], bf[3]);
+      wm::mma16816(u[n], pl, bf[0], bf[1]);
+      wm::mma16816(u[n + 1], pl, bf[2], bf[3]);
+    }
+  }
+  if (has) {
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+      for (int n = 0; n < 18; n += 2) {
+        uint32_t bf[4];
+        wm::ldsm_x4_t(bf, sS + (kk * 16 + wm::bt_row(lane)) * LSX + n * 8 + wm::bt_col(lane));
+        wm::mma16816(u[n], qf[kk], bf[0], bf[1]);
+        wm::mma16816(u[n + 1], qf[kk], bf[2], bf[3]);
+      }
+  }
+}
+// per-row denominators of this lane's two rows: rowsum(a) + (Q . z)
+__device__ __forceinline__ void denom(float (&den)[2], const float (&a)[8][4], const float (&u)[18][4], int lane) {
+  float rs[2] = {0.f, 0.f};
+#pragma unroll
+  for (int n = 0; n < 8; ++n) { rs[0] += a[n][0] + a[n][1]; rs[1] += a[n][2] + a[n][3]; }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+    rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+    const float zq = __shfl_sync(0xffffffffu, u[16][2 * r], lane & ~3);   // column 128 sits in lane t = 0
+    den[r] = rs[r] + zq + 1e-8f;
+  }
+}
+
+__global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(smraw);
+  __nv_bfloat16* sV = sK + C * LB;
+  __nv_bfloat16* sQ = sV + C * LB;
+  __nv_bfloat16* sS = sQ + C * LB;     // [D][LSX]
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int g = h / (p.H / p.G);
+  const int s0 = c * C, rows = min(C, p.S - s0);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, gq = lane >> 2, tq = lane & 3;
+  load_bf<true>(sK, p.k, b, s0, rows, g, p.G, p.S);
+  load_bf<false>(sV, p.v, b, s0, rows, g, p.G, p.S);
+  const bool has = c > 0;
+  if (has)
+    load_state(sS, p.st + ((((int64_t)b * p.G + g) * p.NC + c) * D) * D, p.zs + (((int64_t)b * p.G + g) * p.NC + c) * D, true);
+  const float lam = p.lam[h];
+  const float inv = 1.f / (1.f - lam + 1e-8f);
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+  for (int m = 0; m < 2; ++m) {
+    __syncthreads();
+    load_bf<true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, p.S);
+    __syncthreads();
+    uint32_t qf[8][4];
+    q_frags(qf, sQ, w, lane);
+    float a[8][4];
+    scores(a, qf, sK, w, lane, rows);
+    float u[18][4];
+    numer(u, a, qf, sV, sS, lane, has);
+    float den[2];
+    denom(den, a, u, lane);
+    const float cm = (m == 0) ? inv : -lam * inv;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] += cm * u[n][0] / den[0]; o[n][1] += cm * u[n][1] / den[0];
+      o[n][2] += cm * u[n][2] / den[1]; o[n][3] += cm * u[n][3] / den[1];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = w * 16 + gq + 8 * r;
+    if (i >= rows) continue;
+    __nv_bfloat16* dst = p.out + (((int64_t)b * p.S + s0 + i) * p.H + h) * D;
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+      *reinterpret_cast<__nv_bfloat162*>(dst + n * 8 + 2 * tq) = __floats2bfloat162_rn(o[n][2 * r], o[n][2 * r + 1]);
+  }
+}
+
+// Backward part 1 (per b, query head h, chunk c): dN_m = c_m dout / D_m (bf16), dD_m = -(c_m dout . o_m) / D_m,
+// chunk partial of the reverse state R += sum_m Pq_m^T dN_m, r += sum_m Pq_m^T dD_m, and dlam.
+__global__ void __launch_bounds__(NT) dn_kernel(Params p, __nv_bfloat16* dNb) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(smraw);
+  __nv_bfloat16* sV = sK + C * LB;
+  __nv_bfloat16* sQ = sV + C * LB;          // [2][C][LB]
+  __nv_bfloat16* sdN = sQ + 2 * C * LB;     // [2][C][LB]
+  __nv_bfloat16* sS = sdN + 2 * C * LB;     // [D][LSX]
+  float* sdD = reinterpret_cast<float*>(sS + D * LSX);   // [2][C]
+  float* sRed = sdD + 2 * C;                               // [NT / 32]
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int g = h / (p.H / p.G);
+  const int s0 = c * C, rows = min(C, p.S - s0);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, gq = lane >> 2, tq = lane & 3;
+  load_bf<true>(sK, p.k, b, s0, rows, g, p.G, p.S);
+  load_bf<false>(sV, p.v, b, s0, rows, g, p.G, p.S);
+  load_bf<true>(sQ, p.q1, b, s0, rows, h, p.H, p.S);
+  load_bf<true>(sQ + C * LB, p.q2, b, s0, rows, h, p.H, p.S);
+  const bool has = c > 0;
+  if (has)
+    load_state(sS, p.st + ((((int64_t)b * p.G + g) * p.NC + c) * D) * D, p.zs + (((int64_t)b * p.G + g) * p.NC + c) * D, true);
+  __syncthreads();
+  const float lam = p.lam[h];
+  const float inv = 1.f / (1.f - lam + 1e-8f);
+  // dout in the accumulator layout of this warp's rows
+  float dout[16][4];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int i = w * 16 + gq + 8 * r;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      float2 v = make_float2(0.f, 0.f);
+      if (i < rows) v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(
+                          p.dout + (((int64_t)b * p.S + s0 + i) * p.H + h) * D + n * 8 + 2 * tq));
+      dout[n][2 * r] = v.x; dout[n][2 * r + 1] = v.y;
+    }
+  }
+  float dl = 0.f;
+  for (int m = 0; m < 2; ++m) {
+    const __nv_bfloat16* sQm = sQ + m * C * LB;
+    uint32_t qf[8][4];
+    q_frags(qf, sQm, w, lane);
+    float a[8][4];
+    scores(a, qf, sK, w, lane, rows);
+    float u[18][4];
+    numer(u, a, qf, sV, sS, lane, has);
+    float den[2];
+    denom(den, a, u, lane);
+    const float cm = (m == 0) ? inv : -lam * inv;
+    float part[2] = {0.f, 0.f};
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float o = u[n][e] / den[e >> 1];
+        part[e >> 1] += cm * dout[n][e] * o;
+        dl += (m == 0 ? 1.f : -1.f) * dout[n][e] * o;
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      part[r] += __shfl_xor_sync(0xffffffffu, part[r], 1);
+      part[r] += __shfl_xor_sync(0xffffffffu, part[r], 2);
+      const int i = w * 16 + gq + 8 * r;
+      const float dd = (i < rows) ? -part[r] / den[r] : 0.f;
+      if (tq == 0) sdD[m * C + i] = dd;
+      if (tq == 0 && i < rows) p.dD[(((int64_t)b * p.S + s0 + i) * p.H + h) * 2 + m] = dd;
+      __nv_bfloat16* row_s = sdN + (m * C + i) * LB;
+      __nv_bfloat16* row_g = dNb + ((((int64_t)b * p.S + s0 + i) * p.H + h) * 2 + m) * D;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        const float rd = (i < rows) ? cm / den[r] : 0.f;
+        const __nv_bfloat162 v = __floats2bfloat162_rn(dout[n][2 * r] * rd, dout[n][2 * r + 1] * rd);
+        *reinterpret_cast<__nv_bfloat162*>(row_s + n * 8 + 2 * tq) = v;
+        if (i < rows) *reinterpret_cast<__nv_bfloat162*>(row_g + n * 8 + 2 * tq) = v;
+      }
+    }
+  }
+  __syncthreads();
+  // R partial (K x D) = sum_m Pq_m^T dN_m : warp w owns K rows [32w, 32w + 32)
+  {
+    float acc[2][16][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[mt][n][e] = 0.f;
+    for (int m = 0; m < 2; ++m) {
+      const __nv_bfloat16* sQm = sQ + m * C * LB;
+      const __nv_bfloat16* sdNm = sdN + m * C * LB;
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        uint32_t af[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+          wm::ldsm_x4_t(af[mt], sQm + (ks * 16 + wm::at_row(lane)) * LB + w * 32 + mt * 16 + wm::at_col(lane));
+#pragma unroll
+        for (int n = 0; n < 16; n += 2) {
+          uint32_t bf[4];
+          wm::ldsm_x4_t(bf, sdNm + (ks * 16 + wm::bt_row(lane)) * LB + n * 8 + wm::bt_col(lane));
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            wm::mma16816(acc[mt][n], af[mt], bf[0], bf[1]);
+            wm::mma16816(acc[mt][n + 1], af[mt], bf[2], bf[3]);
+          }
+        }
+      }
+    }
+    float* R = p.R + ((((int64_t)b * p.H + h) * p.NC + c) * D) * D;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int k = w * 32 + mt * 16 + gq + 8 * r;
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          *reinterpret_cast<float2*>(R + k * D + n * 8 + 2 * tq) = make_float2(acc[mt][n][2 * r], acc[mt][n][2 * r + 1]);
+      }
+  }
+  {
+    const int k = threadIdx.x;   // 128 threads = K
+    float accr = 0.f;
+    for (int m = 0; m < 2; ++m)
+      for (int i = 0; i < rows; ++i) accr += __bfloat162float(sQ[(m * C + i) * LB + k]) * sdD[m * C + i];
+    p.r[(((int64_t)b * p.H + h) * p.NC + c) * D + k] = accr;
+  }
+  dl = warp_sum(dl);
+  if (lane == 0) sRed[w] = dl;
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(p.dlam + h, (sRed[0] + sRed[1] + sRed[2] + sRed[3]) * inv * inv);
+}
+
+// Backward part 2 (per b, KV head g, chunk c): for each query head of the group and both queries,
+// dq; accumulated dk, dv including the reverse-state terms.
+__global__ void __launch_bounds__(NT) dqkv_kernel(Params p, const __nv_bfloat16* dNb) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(smraw);
+  __nv_bfloat16* sV = sK + C * LB;
+  __nv_bfloat16* sQ = sV + C * LB;
+  __nv_bfloat16* sdN = sQ + C * LB;
+  __nv_bfloat16* sS = sdN + C * LB;       // [D][LB]  state S (no z column)
+  __nv_bfloat16* sR = sS + D * LB;        // [D][LB]  reverse state
+  __nv_bfloat16* sA = sR + D * LB;        // [C][LC]
+  __nv_bfloat16* sdA = sA + C * LC;       // [C][LC]
+  float* sdD = reinterpret_cast<float*>(sdA + C * LC);    // [C]
+  float* sz = sdD + C;                                    // [D]
+  float* srn = sz + D;                                    // [D]
+  const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int groups = p.H / p.G;
+  const int s0 = c * C, rows = min(C, p.S - s0);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, gq = lane >> 2, tq = lane & 3;
+  const bool has = c > 0, hasR = c + 1 < p.NC;
+  load_bf<true>(sK, p.k, b, s0, rows, g, p.G, p.S);
+  load_bf<false>(sV, p.v, b, s0, rows, g, p.G, p.S);
+  {
+    const float* S = p.st + ((((int64_t)b * p.G + g) * p.NC + c) * D) * D;
+    const float* R = p.Rg + ((((int64_t)b * p.G + g) * p.NC + c) * D) * D;
+    for (int i = threadIdx.x; i < D * D; i += NT) {
+      const int r = i / D, col = i % D;
+      sS[r * LB + col] = __float2bfloat16(has ? S[i] : 0.f);
+      sR[r * LB + col] = __float2bfloat16(hasR ? R[i] : 0.f);
+    }
+    sz[threadIdx.x] = has ? p.zs[(((int64_t)b * p.G + g) * p.NC + c) * D + threadIdx.x] : 0.f;
+    srn[threadIdx.x] = hasR ? p.rg[(((int64_t)b * p.G + g) * p.NC + c) * D + threadIdx.x] : 0.f;
+  }
+  float dk[16][4], dv[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { dk[n][e] = 0.f; dv[n][e] = 0.f; }
+  for (int hh = 0; hh < groups; ++hh) {
+    const int h = g * groups + hh;
+    for (int m = 0; m < 2; ++m) {
+      __syncthreads();
+      load_bf<true>(sQ, m == 0 ? p.q1 : p.q2, b, s0, rows, h, p.H, p.S);
+      for (int i = threadIdx.x; i < C * (D / 8); i += NT) {
+        const int r = i / (D / 8), col = (i % (D / 8)) * 8;
+        int4 v = make_int4(0, 0, 0, 0);
+        if (r < rows) v = *reinterpret_cast<const int4*>(dNb + ((((int64_t)b * p.S + s0 + r) * p.H + h) * 2 + m) * D + col);
+        *reinterpret_cast<int4*>(sdN + r * LB + col) = v;
+      }
+      if (threadIdx.x < C)
+        sdD[threadIdx.x] = threadIdx.x < rows ? p.dD[(((int64_t)b * p.S + s0 + threadIdx.x) * p.H + h) * 2 + m] : 0.f;
+      __syncthreads();
+      uint32_t qf[8][4];
+      q_frags(qf, sQ, w, lane);
+      // A (masked) -> smem
+      {
+        float a[8][4];
+        scores(a, qf, sK, w, lane, rows);
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+            *reinterpret_cast<__nv_bfloat162*>(sA + (w * 16 + gq + 8 * r) * LC + n * 8 + 2 * tq) =
+                __floats2bfloat162_rn(a[n][2 * r], a[n][2 * r + 1]);
+      }
+      // dA = tril(dN V^T + dD) -> smem and A fragments
+      uint32_t daf[4][4];
+      {
+        float da[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) da[n][e] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          uint32_t af[4];
+          wm::ldsm_x4(af, sdN + (w * 16 + wm::a_row(lane)) * LB + kk * 16 + wm::a_col(lane));
+#pragma unroll
+          for (int n = 0; n < 8; n += 2) {
+            uint32_t bf[4];
+            wm::ldsm_x4(bf, sV + (n * 8 + wm::bn_row(lane)) * LB + kk * 16 + wm::bn_col(lane));
+            wm::mma16816(da[n], af, bf[0], bf[1]);
+            wm::mma16816(da[n + 1], af, bf[2], bf[3]);
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = w * 16 + gq + (e >> 1) * 8, j = n * 8 + 2 * tq + (e & 1);
+            da[n][e] = (j <= i && i < rows && j < rows) ? da[n][e] + sdD[i] : 0.f;
+          }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          daf[j][0] = wm::pack_bf16(da[2 * j][0], da[2 * j][1]);
+          daf[j][1] = wm::pack_bf16(da[2 * j][2], da[2 * j][3]);
+          daf[j][2] = wm::pack_bf16(da[2 * j + 1][0], da[2 * j + 1][1]);
+          daf[j][3] = wm::pack_bf16(da[2 * j + 1][2], da[2 * j + 1][3]);
+        }
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+            *reinterpret_cast<__nv_bfloat162*>(sdA + (w * 16 + gq + 8 * r) * LC + n * 8 + 2 * tq) =
+                __floats2bfloat162_rn(da[n][2 * r], da[n][2 * r + 1]);
+      }
+      // dPq = dA Pk + dN S^T + dD z  ->  dq
+      {
+        float dq[16][4];
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dq[n][e] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int n = 0; n < 16; n += 2) {
+            uint32_t bf[4];
+            wm::ldsm_x4_t(bf, sK + (j * 16 + wm::bt_row(lane)) * LB + n * 8 + wm::bt_col(lane));
+            wm::mma16816(dq[n], daf[j], bf[0], bf[1]);
+            wm::mma16816(dq[n + 1], daf[j], bf[2], bf[3]);
+          }
+        if (has) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            uint32_t af[4];
+            wm::ldsm_x4(af, sdN + (w * 16 + wm::a_row(lane)) * LB + kk * 16 + wm::a_col(lane));
+#pragma unroll
+            for (int n = 0; n < 16; n += 2) {
+              uint32_t bf[4];     // B[k = d][n = K] = S[K][d]: non-transposed load of S rows
+              wm::ldsm_x4(bf, sS + (n * 8 + wm::bn_row(lane)) * LB + kk * 16 + wm::bn_col(lane));
+              wm::mma16816(dq[n], af, bf[0], bf[1]);
+              wm::mma16816(dq[n + 1], af, bf[2], bf[3]);
+            }
+          }
+        }
+        __nv_bfloat16* dqp = (m == 0) ? p.dq1 : p.dq2;
+        const __nv_bfloat16* qp = (m == 0) ? p.q1 : p.q2;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int i = w * 16 + gq + 8 * r;
+          if (i >= rows) continue;
+          const float ddr = sdD[i];
+          const int64_t base = (((int64_t)b * p.S + s0 + i) * p.H + h) * D;
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            const int col = n * 8 + 2 * tq;
+            const float2 qv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(qp + base + col));
+            const float v0 = (dq[n][2 * r] + ddr * sz[col]) * dphi_f(qv.x);
+            const float v1 = (dq[n][2 * r + 1] + ddr * sz[col + 1]) * dphi_f(qv.y);
+            *reinterpret_cast<__nv_bfloat162*>(dqp + base + col) = __floats2bfloat162_rn(v0, v1);
+          }
+        }
+      }
+      __syncthreads();
+      // dPk (keys w*16..) += dA^T Pq ;  dV += A^T dN
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        uint32_t a1[4], a2[4];
+        wm::ldsm_x4_t(a1, sdA + (ks * 16 + wm::at_row(lane)) * LC + w * 16 + wm::at_col(lane));
+        wm::ldsm_x4_t(a2, sA + (ks * 16 + wm::at_row(lane)) * LC + w * 16 + wm::at_col(lane));
+#pragma unroll
+        for (int n = 0; n < 16; n += 2) {
+          uint32_t bq[4], bn[4];
+          wm::ldsm_x4_t(bq, sQ + (ks * 16 + wm::bt_row(lane)) * LB + n * 8 + wm::bt_col(lane));
+          wm::ldsm_x4_t(bn, sdN + (ks * 16 + wm::bt_row(lane)) * LB + n * 8 + wm::bt_col(lane));
+          wm::mma16816(dk[n], a1, bq[0], bq[1]);
+          wm::mma16816(dk[n + 1], a1, bq[2], bq[3]);
+          wm::mma16816(dv[n], a2, bn[0], bn[1]);
+          wm::mma16816(dv[n + 1], a2, bn[2], bn[3]);
+        }
+      }
+    }
+  }
+  // reverse-state terms: dPk += V R^T + r ;  dV += Pk R
+  if (hasR) {
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t av[4], ak[4];
+      wm::ldsm_x4(av, sV + (w * 16 + wm::a_row(lane)) * LB + kk * 16 + wm::a_col(lane));
+      wm::ldsm_x4(ak, sK + (w * 16 + wm::a_row(lane)) * LB + kk * 16 + wm::a_col(lane));
+#pragma unroll
+      for (int n = 0; n < 16; n += 2) {
+        uint32_t br[4], bt[4];
+        wm::ldsm_x4(br, sR + (n * 8 + wm::bn_row(lane)) * LB + kk * 16 + wm::bn_col(lane));     // R^T
+        wm::ldsm_x4_t(bt, sR + (kk * 16 + wm::bt_row(lane)) * LB + n * 8 + wm::bt_col(lane));   // R
+        wm::mma16816(dk[n], av, br[0], br[1]);
+        wm::mma16816(dk[n + 1], av, br[2], br[3]);
+        wm::mma16816(dv[n], ak, bt[0], bt[1]);
+        wm::mma16816(dv[n + 1], ak, bt[2], bt[3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int j = w * 16 + gq + 8 * r;
+    if (j >= rows) continue;
+    const int64_t base = (((int64_t)b * p.S + s0 + j) * p.G + g) * D;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int col = n * 8 + 2 * tq;
+      const float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p.k + base + col));
+      const float k0 = (dk[n][2 * r] + srn[col]) * dphi_f(kv.x);
+      const float k1 = (dk[n][2 * r + 1] + srn[col + 1]) * dphi_f(kv.y);
+      *reinterpret_cast<__nv_bfloat162*>(p.dk + base + col) = __floats2bfloat162_rn(k0, k1);
+      *reinterpret_cast<__nv_bfloat162*>(p.dv + base + col) = __floats2bfloat162_rn(dv[n][2 * r], dv[n][2 * r + 1]);
+    }
+  }
+}
+
+constexpr int fwd_smem = (3 * C * LB + D * LSX) * 2;
+constexpr int dn_smem = (6 * C * LB + D * LSX) * 2 + (2 * C + NT / 32) * 4;
+constexpr int dqkv_smem = (4 * C * LB + 2 * D * LB + 2 * C * LC) * 2 + (C + 2 * D) * 4;
+}  // namespace tc
 }  // namespace la
 
 static void la_check(const at::Tensor& q1, const at::Tensor& q2, const at::Tensor& k, const at::Tensor& v) {
@@ -630,6 +1154,13 @@ std::vector<at::Tensor> linear_attn_fwd(at::Tensor q1, at::Tensor q2, at::Tensor
   auto lam32 = lam.to(at::kFloat).contiguous();
   la::Params p = la_params(q1, q2, k, v, lam32, Sst, zst);
   p.out = (__nv_bfloat16*)out.data_ptr();
+  if (K == 128 && HD == 128) {
+    la::run_states<128, 128>(p);
+    la::set_smem(la::tc::fwd_kernel, la::tc::fwd_smem);
+    la::tc::fwd_kernel<<<dim3(NC, H, B), la::tc::NT, la::tc::fwd_smem, stream()>>>(p);
+    MAMF_LAUNCH_CHECK();
+    return {out, Sst, zst};
+  }
   la_dispatch(K, HD, [&](auto kc, auto hc) {
     constexpr int KK = decltype(kc)::value, HH = decltype(hc)::value;
     la::run_states<KK, HH>(p);
@@ -652,7 +1183,7 @@ std::vector<at::Tensor> linear_attn_bwd(at::Tensor q1, at::Tensor q2, at::Tensor
   const int NC = (S + la::C - 1) / la::C;
   auto f32 = q1.options().dtype(at::kFloat);
   auto lam32 = lam.to(at::kFloat).contiguous();
-  auto dN = at::empty({B, S, H, 2, HD}, f32);
+  auto dN = (K == 128 && HD == 128) ? at::empty({0}, f32) : at::empty({B, S, H, 2, HD}, f32);
   auto dD = at::empty({B, S, H, 2}, f32);
   auto Rp = at::empty({B, H, NC, K, HD}, f32);
   auto rp = at::empty({B, H, NC, K}, f32);
@@ -668,6 +1199,21 @@ std::vector<at::Tensor> linear_attn_bwd(at::Tensor q1, at::Tensor q2, at::Tensor
   p.dq1 = (__nv_bfloat16*)dq1.data_ptr(); p.dq2 = (__nv_bfloat16*)dq2.data_ptr();
   p.dk = (__nv_bfloat16*)dk.data_ptr(); p.dv = (__nv_bfloat16*)dv.data_ptr();
   p.dlam = dlam.data_ptr<float>();
+  if (K == 128 && HD == 128) {
+    auto dNb = at::empty({B, S, H, 2, HD}, q1.options());
+    la::set_smem(la::tc::dn_kernel, la::tc::dn_smem);
+    la::tc::dn_kernel<<<dim3(NC, H, B), la::tc::NT, la::tc::dn_smem, stream()>>>(p, (__nv_bfloat16*)dNb.data_ptr());
+    MAMF_LAUNCH_CHECK();
+    const int64_t eR = 128 * 128, er = 128;
+    const int grp = H / G;
+    la::la_prefix_kernel<<<dim3((unsigned)((eR + 255) / 256), B * G), 256, 0, stream()>>>(p.Rg, p.R, eR, NC, grp, true, G);
+    la::la_prefix_kernel<<<dim3((unsigned)((er + 255) / 256), B * G), 256, 0, stream()>>>(p.rg, p.r, er, NC, grp, true, G);
+    MAMF_LAUNCH_CHECK();
+    la::set_smem(la::tc::dqkv_kernel, la::tc::dqkv_smem);
+    la::tc::dqkv_kernel<<<dim3(NC, G, B), la::tc::NT, la::tc::dqkv_smem, stream()>>>(p, (const __nv_bfloat16*)dNb.data_ptr());
+    MAMF_LAUNCH_CHECK();
+    return {dq1, dq2, dk, dv, dlam};
+  }
   la_dispatch(K, HD, [&](auto kc, auto hc) {
     constexpr int KK = decltype(kc)::value, HH = decltype(hc)::value;
     constexpr int sm1 = la::dn_smem<KK, HH>();

@@ -75,23 +75,49 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
   MAMF_LAUNCH_CHECK();
 }
 
+// Deterministic sum of squares: every block writes its partial sum, and the last block to finish
+// adds the partials in index order (fixed grid, fixed shuffle tree), so data-parallel replicas that
+// hold bitwise-equal gradients compute bitwise-equal norms and clip factors.
+constexpr int kSqMaxBlocks = 4096;
+__device__ float g_sq_partial[kSqMaxBlocks];
+__device__ unsigned int g_sq_ticket = 0;
+
 __global__ void sq_norm_kernel(const float* __restrict__ g, int64_t n, float* __restrict__ out) {
   float acc = 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float x = g[i];
-    acc += x * x;
+  const int64_t n4 = ((reinterpret_cast<uintptr_t>(g) & 15) == 0) ? n / 4 : 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 x = reinterpret_cast<const float4*>(g)[i];
+    acc = fmaf(x.x, x.x, acc); acc = fmaf(x.y, x.y, acc); acc = fmaf(x.z, x.z, acc); acc = fmaf(x.w, x.w, acc);
   }
+  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) acc = fmaf(g[i], g[i], acc);
   __shared__ float sm[32];
+  __shared__ bool last;
   acc = block_sum(acc, sm);
-  if (threadIdx.x == 0) atomicAdd(out, acc);
+  if (threadIdx.x == 0) {
+    g_sq_partial[blockIdx.x] = acc;
+    __threadfence();
+    last = atomicAdd(&g_sq_ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) s += *reinterpret_cast<volatile float*>(&g_sq_partial[i]);
+  s = block_sum(s, sm);
+  if (threadIdx.x == 0) {
+    *out += s;
+    g_sq_ticket = 0;
+  }
 }
 
 // out (fp32 scalar tensor) += sum(g^2)
 void sq_norm_accumulate(at::Tensor g, at::Tensor out) {
   c10::cuda::CUDAGuard guard(g.device());
+  TORCH_CHECK(g.is_contiguous() && g.scalar_type() == at::kFloat, "sq_norm_accumulate: contiguous fp32");
   const int64_t n = g.numel();
   if (n == 0) return;
-  const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 4);
+  const int blocks = (int)std::min<int64_t>(std::min<int64_t>((n + 1023) / 1024, (int64_t)num_sms() * 4), kSqMaxBlocks);
   sq_norm_kernel<<<blocks, 256, 0, stream()>>>(g.data_ptr<float>(), n, out.data_ptr<float>());
   MAMF_LAUNCH_CHECK();
 }

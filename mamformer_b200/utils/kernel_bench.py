@@ -127,10 +127,32 @@ def case_adamw(n=1 << 28):
     return (lambda: _C.adamw_step(p, g, m, v, low, 1e-4, 0.9, 0.95, 1e-8, 0.1, 1, scale)), 0.0, n * (4 * 7 + 2)
 
 
+def case_flash_attn(B=1, S=4096, H=32, G=8, hd=128, backward=False):
+    """Causal GQA softmax attention of the ultra-7b full-attention layer (32 query / 8 KV heads)."""
+    from mamformer_b200.ops.native import _C
+    mk = lambda h: (torch.randn(B, S, h, hd, device="cuda") * 0.5).bfloat16()
+    q, k, v = mk(H), mk(G), mk(G)
+    lo, hi, scale = -(1 << 30), 0, hd ** -0.5
+    flops = 4.0 * B * H * S * S * hd / 2          # causal: half of the S x S scores
+    if not backward:
+        return (lambda: _C.flash_attn_fwd(q, k, v, lo, hi, scale)), flops, 0
+    out, lse = _C.flash_attn_fwd(q, k, v, lo, hi, scale)
+    dout = torch.randn_like(out)
+    return (lambda: _C.flash_attn_bwd(q, k, v, out, lse, dout, lo, hi, scale)), 2.5 * flops, 0
+
+
+def case_router(T=4096, E=128, k=8):
+    """Router top-k + softmax over the selected scores + per-expert histogram."""
+    from mamformer_b200.ops.native import _C
+    scores = torch.randn(T, E, device="cuda")
+    return (lambda: _C.router_topk(scores, k)), 0.0, T * E * 4 + T * k * 12
+
+
 CASES = {"gemm": case_gemm, "grouped": case_grouped, "scan": case_scan,
          "scan_bwd": lambda: case_scan(backward=True), "linear_attn": case_linear_attn,
          "linear_attn_bwd": lambda: case_linear_attn(backward=True), "ce": case_ce, "moe": case_moe,
-         "adamw": case_adamw}
+         "adamw": case_adamw, "flash_attn": case_flash_attn,
+         "flash_attn_bwd": lambda: case_flash_attn(backward=True), "router": case_router}
 
 
 def run(op: str, iters: int = 20, once: bool = False) -> dict:

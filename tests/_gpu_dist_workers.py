@@ -64,8 +64,11 @@ def ep_moe_worker(rank, world):
 
 
 def dp_trainer_worker(rank, world):
-    """Bucketed, overlapped data-parallel gradient sums on NCCL: every rank ends with the same
-    parameters, equal to a single-GPU step on the concatenated batch."""
+    """Bucketed, overlapped data-parallel gradient sums on NCCL: the reduced gradients equal a
+    single-GPU step on the concatenated batch, and every rank ends with the same parameters.
+    (Parameters after one AdamW step are not compared with the single-GPU run: the first step
+    moves every element by lr * sign(g), so a near-zero gradient element whose sign differs by
+    rounding changes the result by 2 lr.)"""
     from mamformer_b200 import MamformerConfig, MamformerForCausalLM
     from mamformer_b200.engine import Trainer, TrainConfig
     cfg = MamformerConfig.from_preset("debug")
@@ -73,16 +76,25 @@ def dp_trainer_worker(rank, world):
     torch.manual_seed(0)
     ref = Trainer(MamformerForCausalLM(cfg).cuda(), tc)
     ids = torch.randint(0, cfg.vocab_size, (world, 128), generator=torch.Generator().manual_seed(5)).cuda()
-    ref.cfg.micro_batch = 1
     ref.train_step(ids, sync_loss=True)
     torch.manual_seed(0)
     tr = Trainer(MamformerForCausalLM(cfg).cuda(), tc, dp_group=dist.group.WORLD, bucket_mb=1.0)
     tr.train_step(ids[rank:rank + 1], sync_loss=True)
+    torch.cuda.synchronize()
+    bad = []
     for (n, p), (_, q) in zip(tr.model.named_parameters(), ref.model.named_parameters()):
-        assert _rel(p.detach(), q.detach()) < 1e-2, (n, _rel(p.detach(), q.detach()))
         other = p.detach().clone()
-        dist.broadcast(other, 0)
-        assert torch.equal(other, p.detach()), n
+        dist.broadcast(other, 0)                   # every rank takes every collective first
+        og = p.main_grad.clone()
+        dist.broadcast(og, 0)
+        if not torch.equal(other, p.detach()):
+            bad.append(f"{n}: replicas differ by {(other.float() - p.detach().float()).abs().max().item():.3e}, "
+                       f"grads by {(og - p.main_grad).abs().max().item():.3e} (|g| max {og.abs().max().item():.3e}, "
+                       f"dtype {p.dtype}, numel {p.numel()})")
+        g, gr = p.main_grad / world, q.main_grad   # the DP buffer holds sum_r dL_r/dtheta
+        if gr.norm() > 1e-6 and _rel(g, gr) > 3e-2:
+            bad.append(f"{n}: grad rel {_rel(g, gr):.3e}")
+    assert not bad, bad
 
 
 def tp_fused_worker(rank, world):

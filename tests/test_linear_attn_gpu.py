@@ -12,7 +12,7 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("B,S,H,G,hd,K", [(2, 200, 8, 2, 64, 64), (1, 256, 4, 4, 128, 128), (1, 130, 4, 1, 128, 64),
-                                          (1, 1024, 8, 2, 128, 128)])
+                                          (1, 1024, 8, 2, 128, 128), (2, 330, 8, 2, 128, 128)])
 def test_linear_diff_attention_fwd_bwd(B, S, H, G, hd, K):
     from mamformer_b200.ops import native
     torch.manual_seed(0)
