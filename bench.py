@@ -50,6 +50,8 @@ def _args():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-launches", type=int, default=1)
+    ap.add_argument("--dp-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: dense-gradient all-reduce by this repository's NVLink kernels (p2p) or NCCL")
     ap.add_argument("--parallel", default="ep", choices=["ep", "dp"],
                     help="N > 1: ep = routed experts sharded over all N GPUs (EP=N x dense DP=N, the "
                          "BASELINE ultra-7b layout); dp = every GPU holds every expert")
@@ -141,10 +143,12 @@ def run_ours(args, rank, world):
         model = coord.shard_model(model)
         torch.cuda.empty_cache()
         trainer = Trainer(model, tcfg, dp_group=coord.get_group("dense_dp"),
-                          expert_dp_group=coord.get_group("expert_dp"), ep_group=coord.get_group("ep"))
+                          expert_dp_group=coord.get_group("expert_dp"), ep_group=coord.get_group("ep"),
+                          dp_transport=args.dp_transport)
         parallelism = f"ep{world} (routed experts sharded over {world} GPUs; dense weights data-parallel)"
     else:
-        trainer = Trainer(model, tcfg, dp_group=dist.group.WORLD if world > 1 else None)
+        trainer = Trainer(model, tcfg, dp_group=dist.group.WORLD if world > 1 else None,
+                          dp_transport=args.dp_transport)
         parallelism = f"dp{world}"
     n_batches = 2
     g = torch.Generator().manual_seed(1234 + rank)

@@ -42,6 +42,10 @@ void moe_combine_bwd(at::Tensor dout, at::Tensor y, c10::optional<at::Tensor> y_
                      at::Tensor dgate, at::Tensor dy, c10::optional<at::Tensor> dy_idx, int64_t k);
 void ep_pull_runs(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor runs, int64_t max_len);
 void ep_barrier(std::vector<int64_t> signal, int64_t me, int64_t epoch, int64_t slot0);
+int64_t dp_slice(int64_t lo, int64_t hi, int64_t P);
+at::Tensor dp_reduce_scatter(std::vector<int64_t> bufs, int64_t me, int64_t lo, int64_t hi, double scale, bool want_sq);
+void dp_all_gather(std::vector<int64_t> bufs, int64_t me, int64_t lo, int64_t hi);
+at::Tensor dp_allreduce_nvls(int64_t mc_base, int64_t P, int64_t me, int64_t lo, int64_t hi, double scale, bool want_sq);
 int64_t comm_error();
 void comm_clear_error();
 std::vector<at::Tensor> linear_attn_fwd(at::Tensor q1, at::Tensor q2, at::Tensor k, at::Tensor v, at::Tensor lam,
@@ -87,6 +91,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &mamf::moe_combine_bwd);
   m.def("ep_pull_runs", &mamf::ep_pull_runs);
   m.def("ep_barrier", &mamf::ep_barrier);
+  m.def("dp_slice", &mamf::dp_slice);
+  m.def("dp_reduce_scatter", &mamf::dp_reduce_scatter);
+  m.def("dp_all_gather", &mamf::dp_all_gather);
+  m.def("dp_allreduce_nvls", &mamf::dp_allreduce_nvls);
   m.def("comm_error", &mamf::comm_error);
   m.def("comm_clear_error", &mamf::comm_clear_error);
   m.def("linear_attn_fwd", &mamf::linear_attn_fwd);

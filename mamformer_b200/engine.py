@@ -48,7 +48,7 @@ class Trainer:
                  dp_group: Optional[dist.ProcessGroup] = None, expert_params=None,
                  expert_dp_group: Optional[dist.ProcessGroup] = None,
                  ep_group: Optional[dist.ProcessGroup] = None, bucket_mb: float = 64.0,
-                 zero_stage: int = 0):
+                 zero_stage: int = 0, dp_transport: str = "nccl"):
         self.cfg = cfg
         self.model = model
         if cfg.compute_dtype != torch.float32:
@@ -69,7 +69,7 @@ class Trainer:
             weight_decay=cfg.weight_decay, max_grad_norm=cfg.max_grad_norm, dp_group=dp_group,
             no_dp_reduce=expert_params, expert_dp_group=expert_dp_group, ep_group=ep_group,
             bucket_mb=bucket_mb, param_order={id(p): i for i, p in enumerate(model.parameters())},
-            zero_stage=zero_stage)
+            zero_stage=zero_stage, dp_transport=dp_transport)
         self.scheduler = create_lr_scheduler(self.optimizer, cfg.warmup_steps, cfg.max_steps,
                                              cfg.learning_rate, cfg.min_lr_ratio)
         dev = next(model.parameters()).device

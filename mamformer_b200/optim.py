@@ -26,11 +26,19 @@ B200 design:
   the gradient hooks of the last micro-batch, so they overlap the rest of the backward pass;
   buckets are launched in one fixed order on every rank (a bucket waits for its predecessors),
   and whatever did not become ready during the backward is launched by ``step``.
+  ``dp_transport="p2p"`` replaces NCCL on this path: the gradient segments are allocated in
+  symmetric memory and each bucket is summed by the NVLink kernels of ``csrc/dp_grad.cu``
+  (bounded barrier, reduce-scatter by P2P loads in fixed rank order, all-gather; or, with
+  ``MAMF_DP_NVLS=1`` and a multicast object, one switch-side ``multimem`` reduction and
+  multicast store) on a side stream that starts when the bucket's last gradient is in;
+* the squared gradient norm is summed without float atomics (fixed-order partials), so every
+  replica computes the same clip factor and replicas stay bitwise equal.
 """
 
 from __future__ import annotations
 
 import math
+import os
 from typing import Dict, List, Optional, Tuple
 
 import torch
@@ -79,7 +87,7 @@ class _Segment:
     parameter buffer."""
 
     def __init__(self, params: List[torch.nn.Parameter], wd: float, dp_reduce: bool, device,
-                 world: int, shard_group=None):
+                 world: int, shard_group=None, symm_group=None):
         self.params = params
         self.wd = wd
         self.dp_reduce = dp_reduce
@@ -97,7 +105,17 @@ class _Segment:
         self.lo, self.hi = sr * self.numel // sw, (sr + 1) * self.numel // sw
         f32 = dict(device=device, dtype=torch.float32)
         n_local = self.hi - self.lo
-        self.grad = torch.zeros(self.numel, **f32)
+        # with `symm_group` the gradient buffer lives in symmetric memory (every rank of the group
+        # maps it), so the data-parallel reduction can run as this repository's NVLink kernels
+        self.symm = None
+        if symm_group is not None:
+            import torch.distributed._symmetric_memory as symm_mem
+            self.grad = symm_mem.empty(self.numel, dtype=torch.float32, device=device)
+            self.grad.zero_()
+            self.symm = symm_mem.rendezvous(self.grad, symm_group)
+            self.symm_epoch = 0
+        else:
+            self.grad = torch.zeros(self.numel, **f32)
         self.m = torch.zeros(n_local, **f32)
         self.v = torch.zeros(n_local, **f32)
         self.low_flat = torch.zeros(self.numel, device=device, dtype=params[0].dtype) if self.low else None
@@ -188,6 +206,7 @@ class GradReducer:
                 self._of[id(p)] = i
         self.armed = False
         self._next = 0
+        self._side = None
 
     def arm(self) -> None:
         self.armed = True
@@ -208,7 +227,45 @@ class GradReducer:
         self._launch_ready()
 
     def _launch(self, b: _Bucket) -> None:
-        b.work = dist.all_reduce(b.seg.grad[b.lo:b.hi], group=b.group, async_op=True)
+        if b.seg.symm is not None:
+            self._launch_p2p(b)
+        else:
+            b.work = dist.all_reduce(b.seg.grad[b.lo:b.hi], group=b.group, async_op=True)
+
+    def _launch_p2p(self, b: _Bucket) -> None:
+        """Sum the bucket over the group with the NVLink kernels on a side stream: bounded barrier,
+        reduce-scatter (P2P loads) or switch reduction (NVLS multimem), barrier, all-gather,
+        barrier.  The side stream starts after the bucket's last accumulation on this stream."""
+        from mamformer_b200.ops._ext import require_native
+        C = require_native()
+        seg, h = b.seg, b.seg.symm
+        cur = torch.cuda.current_stream()
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=seg.grad.device)
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        self._side.wait_event(ready)
+        P, me = h.world_size, h.rank
+        pads = h.signal_pad_ptrs
+
+        def barrier():
+            seg.symm_epoch += 1
+            C.ep_barrier(pads, me, seg.symm_epoch, _DP_SLOT0)
+
+        with torch.cuda.stream(self._side):
+            barrier()                                   # every rank finished accumulating the bucket
+            mc = int(getattr(h, "multicast_ptr", 0) or 0) if _use_nvls() else 0
+            if mc:
+                C.dp_allreduce_nvls(mc, P, me, b.lo, b.hi, 1.0, False)
+                barrier()                               # every slice stored into every copy
+            else:
+                C.dp_reduce_scatter(h.buffer_ptrs, me, b.lo, b.hi, 1.0, False)
+                barrier()                               # every slice reduced
+                C.dp_all_gather(h.buffer_ptrs, me, b.lo, b.hi)
+                barrier()                               # every peer done reading this rank's slice
+            done = torch.cuda.Event()
+            done.record(self._side)
+        b.work = _StreamWork(done)
 
     def _launch_ready(self) -> None:
         while self._next < len(self.buckets) and self.buckets[self._next].pending == 0:
@@ -226,12 +283,39 @@ class GradReducer:
         self.armed = False
 
 
+_DP_SLOT0 = 640   # signal-pad words used by the data-parallel barrier (after the EP / TP ones)
+
+
+def _use_nvls() -> bool:
+    """NVSwitch multicast reduction for the peer-memory gradient all-reduce (opt-in)."""
+    return os.environ.get("MAMF_DP_NVLS", "0") == "1"
+
+
+class _StreamWork:
+    """Completion of a side-stream reduction, with the ``wait()`` of a collective handle."""
+
+    def __init__(self, event):
+        self.event = event
+
+    def wait(self) -> None:
+        torch.cuda.current_stream().wait_event(self.event)
+
+
 def mark_grad_ready(p: torch.Tensor) -> None:
     """Tell the data-parallel reducer that ``p.main_grad`` is final for this backward (for
     gradients accumulated in place by a kernel instead of through autograd)."""
     red = getattr(p, "_mamf_reducer", None)
     if red is not None:
         red.ready(p)
+
+
+def _p2p_ok(transport: str, group, device) -> bool:
+    """Peer-memory gradient reduction: requested ("p2p"), on CUDA, 2..8 ranks."""
+    if transport != "p2p":
+        return False
+    if torch.device(device).type != "cuda" or group is None:
+        return False
+    return 2 <= _group_size(group) <= 8
 
 
 class MixedPrecisionAdamW(torch.optim.Optimizer):
@@ -245,7 +329,7 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
                  dp_group: Optional[dist.ProcessGroup] = None, no_dp_reduce=None,
                  expert_dp_group: Optional[dist.ProcessGroup] = None,
                  ep_group: Optional[dist.ProcessGroup] = None, bucket_mb: float = 64.0,
-                 param_order=None, zero_stage: int = 0):
+                 param_order=None, zero_stage: int = 0, dp_transport: str = "nccl"):
         defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         super().__init__(params, defaults)
         self.max_grad_norm = max_grad_norm
@@ -264,7 +348,10 @@ class MixedPrecisionAdamW(torch.optim.Optimizer):
             for (dt, is_exp), ps in buckets.items():
                 red = (expert_world > 1) if is_exp else (self.world > 1)
                 shard = dp_group if (zero_stage >= 1 and not is_exp and self.world > 1) else None
-                seg = _Segment(ps, g["weight_decay"], red, dev, self.world, shard_group=shard)
+                grp = expert_dp_group if is_exp else dp_group
+                symm_grp = grp if (red and shard is None and _p2p_ok(dp_transport, grp, dev)) else None
+                seg = _Segment(ps, g["weight_decay"], red, dev, self.world, shard_group=shard,
+                               symm_group=symm_grp)
                 seg.expert = is_exp
                 self.segments.append((gi, seg))
         self.reducer = GradReducer(self.segments, dp_group, expert_dp_group, bucket_mb, param_order)

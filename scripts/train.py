@@ -47,6 +47,8 @@ def build_parser():
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--zero", type=int, default=0, choices=[0, 1],
                    help="1: shard fp32 master weights and Adam moments over the data-parallel ranks")
+    p.add_argument("--dp-transport", default="nccl", choices=["nccl", "p2p"],
+                   help="data-parallel gradient sums: NCCL, or this repository's NVLink peer-memory kernels")
     return p
 
 
@@ -78,7 +80,7 @@ def train(args, parallel=None):
                        gradient_checkpointing=args.gradient_checkpointing)
     trainer = Trainer(model, tcfg, dp_group=coord.get_group("dense_dp") if world > 1 else None,
                       expert_dp_group=coord.get_group("expert_dp"), ep_group=coord.get_group("ep"),
-                      zero_stage=args.zero)
+                      zero_stage=args.zero, dp_transport=args.dp_transport)
     start = 0
     if args.resume:
         start = load_checkpoint(args.resume, trainer.model, trainer.optimizer, trainer.scheduler)

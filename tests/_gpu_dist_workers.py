@@ -97,6 +97,52 @@ def dp_trainer_worker(rank, world):
     assert not bad, bad
 
 
+def dp_p2p_worker(rank, world, nvls=False):
+    """Data-parallel gradient sums by the NVLink kernels (symmetric-memory gradient buffers):
+    reduced gradients equal the single-GPU batch gradient, replicas stay bitwise equal over two
+    steps, and the result matches the NCCL transport."""
+    import os as _os
+    from mamformer_b200 import MamformerConfig, MamformerForCausalLM
+    from mamformer_b200.engine import Trainer, TrainConfig
+    _os.environ["MAMF_DP_NVLS"] = "1" if nvls else "0"
+    cfg = MamformerConfig.from_preset("debug")
+    tc = TrainConfig(learning_rate=1e-3, warmup_steps=1, micro_batch=1)
+    ids = torch.randint(0, cfg.vocab_size, (2, world, 128), generator=torch.Generator().manual_seed(5)).cuda()
+    torch.manual_seed(0)
+    ref = Trainer(MamformerForCausalLM(cfg).cuda(), tc)
+    torch.manual_seed(0)
+    nc = Trainer(MamformerForCausalLM(cfg).cuda(), tc, dp_group=dist.group.WORLD, bucket_mb=1.0)
+    torch.manual_seed(0)
+    tr = Trainer(MamformerForCausalLM(cfg).cuda(), tc, dp_group=dist.group.WORLD, bucket_mb=1.0,
+                 dp_transport="p2p")
+    assert any(seg.symm is not None for _, seg in tr.optimizer.segments), "no symmetric gradient segment"
+    bad = []
+    for step in range(2):
+        ref.train_step(ids[step], sync_loss=True)
+        nc.train_step(ids[step, rank:rank + 1], sync_loss=True)
+        tr.train_step(ids[step, rank:rank + 1], sync_loss=True)
+        torch.cuda.synchronize()
+        for (n, p), (_, q), (_, u) in zip(tr.model.named_parameters(), ref.model.named_parameters(),
+                                          nc.model.named_parameters()):
+            other = p.detach().clone()
+            dist.broadcast(other, 0)
+            if not torch.equal(other, p.detach()):
+                bad.append(f"step {step} {n}: replicas differ")
+            if step == 0:
+                g, gr = p.main_grad / world, q.main_grad
+                if gr.norm() > 1e-6 and _rel(g, gr) > 3e-2:
+                    bad.append(f"{n}: grad rel {_rel(g, gr):.3e}")
+                if _rel(p.main_grad, u.main_grad) > 1e-5:
+                    bad.append(f"{n}: p2p vs nccl grad rel {_rel(p.main_grad, u.main_grad):.3e}")
+    from mamformer_b200.fault import check_device_status
+    check_device_status()
+    assert not bad, bad[:10]
+
+
+def dp_nvls_worker(rank, world):
+    dp_p2p_worker(rank, world, nvls=True)
+
+
 def tp_fused_worker(rank, world):
     """Fused all-gather->GEMM and GEMM->reduce-scatter (and their autograd) against NCCL + torch."""
     from mamformer_b200.parallel import tp_fused

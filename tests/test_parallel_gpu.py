@@ -52,6 +52,16 @@ def test_data_parallel_trainer_two_gpus():
 
 
 @needs2
+def test_data_parallel_p2p_transport_two_gpus():
+    _spawn("dp_p2p_worker", 2)
+
+
+@needs2
+def test_data_parallel_nvls_transport_two_gpus():
+    _spawn("dp_nvls_worker", 2)
+
+
+@needs2
 def test_expert_parallel_moe_two_gpus():
     _spawn("ep_moe_worker", 2)
 
