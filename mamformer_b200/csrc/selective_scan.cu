@@ -8,8 +8,8 @@
 //
 // Work split (sm_100a, 148 SMs): one CTA per (batch, 32-channel block); warp w owns states
 // [16w, 16w+16) of all 32 channels (N/16 warps per CTA); lane = channel.  Each thread keeps
-// its 16 states in registers, so the time recurrence is 16 independent FMA chains per thread
-// and the decay exp2 runs on the MUFU pipe.  Inputs of a 32-step chunk are staged in shared
+// its 16 states in registers as 8 fp32x2 pairs, so the time recurrence is 16 independent chains
+// per thread issued as packed FFMA2/FMUL2 instructions, and the decay exp2 runs on the MUFU pipe.  Inputs of a 32-step chunk are staged in shared
 // memory (B/C rows are broadcast reads); the forward loads the next chunk into registers while
 // the current chunk's recurrence runs.  Reductions over channels (h_states, dB, dC) use an
 // in-warp reduce-scatter after which lanes 2s, 2s+1 hold the 32-channel sum for state 16w+s;
@@ -39,87 +39,61 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// After the call lane l holds sum over the 32 lanes of v[l]; v is destroyed.
-__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const bool up = lane & 16;
-    float send = up ? v[j] : v[j + 16];
-    float keep = up ? v[j + 16] : v[j];
-    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const bool up = lane & 8;
-    float send = up ? v[j] : v[j + 8];
-    float keep = up ? v[j + 8] : v[j];
-    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const bool up = lane & 4;
-    float send = up ? v[j] : v[j + 4];
-    float keep = up ? v[j + 4] : v[j];
-    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const bool up = lane & 2;
-    float send = up ? v[j] : v[j + 2];
-    float keep = up ? v[j + 2] : v[j];
-    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-  {
-    const bool up = lane & 1;
-    float send = up ? v[0] : v[1];
-    float keep = up ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-  }
-  return v[0];
-}
-
-// 16 values per lane: afterwards lanes 2s and 2s+1 both hold sum over the 32 lanes of v[s].
-__device__ __forceinline__ float reduce_scatter16(float (&v)[16], int lane) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const bool up = lane & 16;
-    float send = up ? v[j] : v[j + 8];
-    float keep = up ? v[j + 8] : v[j];
-    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const bool up = lane & 8;
-    float send = up ? v[j] : v[j + 4];
-    float keep = up ? v[j + 4] : v[j];
-    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const bool up = lane & 4;
-    float send = up ? v[j] : v[j + 2];
-    float keep = up ? v[j + 2] : v[j];
-    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  {
-    const bool up = lane & 2;
-    float send = up ? v[0] : v[1];
-    float keep = up ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
-}
-
 constexpr int SW = 16;      // states per warp (lane = channel, 32 channels per CTA)
 
-// 16 consecutive shared-memory floats (16-byte aligned) into registers with 4 vector loads
-__device__ __forceinline__ void ld_row16(float (&r)[16], const float* src) {
+// ---- packed fp32x2 state arithmetic --------------------------------------------------------------
+// sm_100 issues two fp32 FMAs / multiplies / adds per instruction (FFMA2 & co.), which halves the
+// instruction count of the per-state recurrence.  A thread's 16 states are 8 float2 pairs.
+//
+// Register permutation.  Register k of lane l holds state k ^ (qx(l) << 2), qx(l) = (l >> 3) & 3:
+// every group of 4 states (one float4 of a B / C row) is loaded from float4 index q ^ qx.  With
+// this layout the first two rounds of the channel reduce-scatter (partners l ^ 16, l ^ 8) need no
+// lane-dependent selects: every lane keeps registers [0, 8) (then [0, 4)) and adds the partner's
+// registers [8, 16) (then [4, 8)), which hold the same states in the partner's permutation.
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 ex2x2(float2 x) { return make_float2(ex2(x.x), ex2(x.y)); }
+__device__ __forceinline__ int perm_q(int lane) { return (lane >> 3) & 3; }
+__device__ __forceinline__ int state_of(int k, int lane) { return k ^ (perm_q(lane) << 2); }
+
+// 16 consecutive shared-memory floats (16-byte aligned) in the lane's register permutation
+__device__ __forceinline__ void ld_row16p(float2 (&r)[8], const float* src, int qx) {
   const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float4 v = s4[q];
-    r[4 * q] = v.x; r[4 * q + 1] = v.y; r[4 * q + 2] = v.z; r[4 * q + 3] = v.w;
+    const float4 v = s4[q ^ qx];
+    r[2 * q] = make_float2(v.x, v.y);
+    r[2 * q + 1] = make_float2(v.z, v.w);
   }
+}
+// the same for 16 fp32 values in global memory (checkpoint rows)
+__device__ __forceinline__ void ld_state16p(float2 (&r)[8], const float* src, int qx) { ld_row16p(r, src, qx); }
+__device__ __forceinline__ void st_state16p(float* dst, const float2 (&r)[8], int qx) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) d4[q ^ qx] = make_float4(r[2 * q].x, r[2 * q].y, r[2 * q + 1].x, r[2 * q + 1].y);
+}
+
+// Sum over the 32 lanes (channels) of the 16 permuted state values; afterwards lanes 2s and 2s+1
+// hold the sum for state s (s = lane >> 1).  v is destroyed.
+__device__ __forceinline__ float reduce_scatter16p(float2 (&v)[8], int lane) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    v[i] = add2(v[i], make_float2(__shfl_xor_sync(0xffffffffu, v[i + 4].x, 16), __shfl_xor_sync(0xffffffffu, v[i + 4].y, 16)));
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    v[i] = add2(v[i], make_float2(__shfl_xor_sync(0xffffffffu, v[i + 2].x, 8), __shfl_xor_sync(0xffffffffu, v[i + 2].y, 8)));
+  {
+    const bool up = lane & 4;
+    const float2 send = up ? v[0] : v[1], keep = up ? v[1] : v[0];
+    v[0] = add2(keep, make_float2(__shfl_xor_sync(0xffffffffu, send.x, 4), __shfl_xor_sync(0xffffffffu, send.y, 4)));
+  }
+  const bool up = lane & 2;
+  const float send = up ? v[0].x : v[0].y, keep = up ? v[0].y : v[0].x;
+  const float r = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  return r + __shfl_xor_sync(0xffffffffu, r, 1);
 }
 
 struct Params {
@@ -200,7 +174,7 @@ struct Stage {
 };
 
 template <typename T, int NW, bool SOFTPLUS, bool GATE, bool HS>
-__global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
+__global__ void __launch_bounds__(NW * 32, 2) scan_fwd_kernel(Params p) {
   constexpr int NT = NW * 32;
   constexpr int N = NW * SW;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -215,55 +189,49 @@ __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
   float* sDtx = sDt + CK * 32;      // [CK][32]
   float* sYw = sDtx + CK * 32;      // [NW][CK][32] per-warp partial outputs
 
-  float A2[SW];
+  const int qx = perm_q(lane);
+  float2 A2[SW / 2];
 #pragma unroll
   for (int j = 0; j < SW; ++j) {
-    float al = fminf(fmaxf(p.A_log[w * SW + j], -5.f), 5.f);
-    A2[j] = -__expf(al) * LOG2E;
+    const float al = fminf(fmaxf(p.A_log[w * SW + state_of(j, lane)], -5.f), 5.f);
+    const float v = -__expf(al) * LOG2E;
+    if (j & 1) A2[j >> 1].y = v; else A2[j >> 1].x = v;
   }
-  float h[SW];
+  float2 h[SW / 2];
+  if (p.h0 && cvalid) ld_state16p(h, p.h0 + ((int64_t)b * p.Di + c) * N + w * SW, qx);
+  else {
 #pragma unroll
-  for (int j = 0; j < SW; ++j)
-    h[j] = (p.h0 && cvalid) ? p.h0[((int64_t)b * p.Di + c) * N + w * SW + j] : 0.f;
+    for (int j = 0; j < SW / 2; ++j) h[j] = f2(0.f);
+  }
 
   Stage<T, NT, N> st;
   st.load(p, b, cblk, 0, min(CK, p.S));
   for (int t0 = 0, ck = 0; t0 < p.S; t0 += CK, ++ck) {
     const int L = min(CK, p.S - t0);
-    if (p.ckpt && cvalid) {
-      float4* dst = reinterpret_cast<float4*>(p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + c) * N + w * SW);
-#pragma unroll
-      for (int j = 0; j < SW / 4; ++j) dst[j] = make_float4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
-    }
+    if (p.ckpt && cvalid) st_state16p(p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + c) * N + w * SW, h, qx);
     __syncthreads();
     st.template store<SOFTPLUS>(sB, sC, sDt, sDtx);
     __syncthreads();
     if (t0 + CK < p.S) st.load(p, b, cblk, t0 + CK, min(CK, p.S - t0 - CK));   // next chunk in flight
     float* yw = sYw + w * CK * 32;
     for (int tt = 0; tt < L; ++tt) {
-      const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
-      const float4* Bt = reinterpret_cast<const float4*>(sB + tt * N + w * SW);
-      const float4* Ct = reinterpret_cast<const float4*>(sC + tt * N + w * SW);
-      float yq[4] = {0.f, 0.f, 0.f, 0.f};     // 4 independent partial sums (short FMA chains)
+      const float2 dd = f2(sDt[tt * 32 + lane]), dx2 = f2(sDtx[tt * 32 + lane]);
+      float2 Bt[SW / 2], Ct[SW / 2];
+      ld_row16p(Bt, sB + tt * N + w * SW, qx);
+      ld_row16p(Ct, sC + tt * N + w * SW, qx);
+      float2 yq[2] = {f2(0.f), f2(0.f)};        // 4 independent partial sums (short FMA chains)
 #pragma unroll
-      for (int q = 0; q < SW / 4; ++q) {
-        const float4 bq = Bt[q], cq = Ct[q];
-        const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
-        const float cc[4] = {cq.x, cq.y, cq.z, cq.w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int j = 4 * q + r;
-          const float a = ex2(A2[j] * d);
-          h[j] = fmaf(a, h[j], bb[r] * dxv);
-          yq[r] = fmaf(cc[r], h[j], yq[r]);
-        }
+      for (int j = 0; j < SW / 2; ++j) {
+        const float2 a = ex2x2(mul2(A2[j], dd));
+        h[j] = fma2(a, h[j], mul2(Bt[j], dx2));
+        yq[j & 1] = fma2(Ct[j], h[j], yq[j & 1]);
       }
-      yw[tt * 32 + lane] = (yq[0] + yq[1]) + (yq[2] + yq[3]);
+      yw[tt * 32 + lane] = (yq[0].x + yq[0].y) + (yq[1].x + yq[1].y);
       if (HS) {
-        float tmp[SW];
+        float2 tmp[SW / 2];
 #pragma unroll
-        for (int j = 0; j < SW; ++j) tmp[j] = h[j];
-        const float r = reduce_scatter16(tmp, lane);
+        for (int j = 0; j < SW / 2; ++j) tmp[j] = h[j];
+        const float r = reduce_scatter16p(tmp, lane);
         if ((lane & 1) == 0)
           p.hs_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
       }
@@ -281,11 +249,7 @@ __global__ void __launch_bounds__(NW * 32) scan_fwd_kernel(Params p) {
       reinterpret_cast<T*>(p.y)[(int64_t)b * p.y_bs + (int64_t)(t0 + tt) * p.y_ts + cc] = from_f<T>(yv);
     }
   }
-  if (p.final_state && cvalid) {
-    float* dst = p.final_state + ((int64_t)b * p.Di + c) * N + w * SW;
-#pragma unroll
-    for (int j = 0; j < SW; ++j) dst[j] = h[j];
-  }
+  if (p.final_state && cvalid) st_state16p(p.final_state + ((int64_t)b * p.Di + c) * N + w * SW, h, qx);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -321,12 +285,16 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
   if (tid < 32) sDsum[tid] = 0.f;
   float* scratch = p.scratch + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * (CK / SUB) * SW * NT;
 
-  float P[SW], dAacc[SW], A2[SW];
+  const int qx = perm_q(lane);
+  float2 P[SW / 2], dAacc[SW / 2], A2[SW / 2];
 #pragma unroll
-  for (int j = 0; j < SW; ++j) { P[j] = 0.f; dAacc[j] = 0.f; }
+  for (int j = 0; j < SW / 2; ++j) { P[j] = f2(0.f); dAacc[j] = f2(0.f); }
   __syncthreads();
 #pragma unroll
-  for (int j = 0; j < SW; ++j) A2[j] = sA2[w * SW + j];
+  for (int j = 0; j < SW; ++j) {
+    const float v = sA2[w * SW + state_of(j, lane)];
+    if (j & 1) A2[j >> 1].y = v; else A2[j >> 1].x = v;
+  }
 
   for (int ck = p.nck - 1; ck >= 0; --ck) {
     const int t0 = ck * CK;
@@ -355,31 +323,33 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
 
     // ---- phase A: recompute the chunk forward --------------------------------------------
     {
-      float h[SW];
-      const float* src = p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + (cvalid ? c : 0)) * N + w * SW;
+      float2 h[SW / 2];
+      if (cvalid) ld_state16p(h, p.ckpt + (((int64_t)b * p.nck + ck) * p.Di + c) * N + w * SW, qx);
+      else {
 #pragma unroll
-      for (int j = 0; j < SW; ++j) h[j] = cvalid ? src[j] : 0.f;
+        for (int j = 0; j < SW / 2; ++j) h[j] = f2(0.f);
+      }
       for (int tt = 0; tt < L; ++tt) {
         if ((tt % SUB) == 0) {
-          float* dst = scratch + (int64_t)(tt / SUB) * SW * NT;
+          float2* dst = reinterpret_cast<float2*>(scratch + (int64_t)(tt / SUB) * SW * NT);
 #pragma unroll
-          for (int j = 0; j < SW; ++j) dst[j * NT + tid] = h[j];
+          for (int j = 0; j < SW / 2; ++j) dst[j * NT + tid] = h[j];
         }
-        const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
-        float Bt[SW], Ct[SW];
-        ld_row16(Bt, sB + tt * N + w * SW);
-        ld_row16(Ct, sC + tt * N + w * SW);
-        float yq[4] = {0.f, 0.f, 0.f, 0.f};
-        float tmp[SW];
+        const float2 dd = f2(sDt[tt * 32 + lane]), dx2 = f2(sDtx[tt * 32 + lane]), dy2 = f2(sDyp[tt * 32 + lane]);
+        float2 Bt[SW / 2], Ct[SW / 2];
+        ld_row16p(Bt, sB + tt * N + w * SW, qx);
+        ld_row16p(Ct, sC + tt * N + w * SW, qx);
+        float2 yq[2] = {f2(0.f), f2(0.f)};
+        float2 tmp[SW / 2];
 #pragma unroll
-        for (int j = 0; j < SW; ++j) {
-          const float a = ex2(A2[j] * d);
-          h[j] = fmaf(a, h[j], Bt[j] * dxv);
-          yq[j & 3] = fmaf(Ct[j], h[j], yq[j & 3]);
-          tmp[j] = h[j] * dyp;
+        for (int j = 0; j < SW / 2; ++j) {
+          const float2 a = ex2x2(mul2(A2[j], dd));
+          h[j] = fma2(a, h[j], mul2(Bt[j], dx2));
+          yq[j & 1] = fma2(Ct[j], h[j], yq[j & 1]);
+          tmp[j] = mul2(h[j], dy2);
         }
-        atomicAdd(&sY[tt * 32 + lane], (yq[0] + yq[1]) + (yq[2] + yq[3]));
-        const float r = reduce_scatter16(tmp, lane);
+        atomicAdd(&sY[tt * 32 + lane], (yq[0].x + yq[0].y) + (yq[1].x + yq[1].y));
+        const float r = reduce_scatter16p(tmp, lane);
         if ((lane & 1) == 0)
           p.dC_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
       }
@@ -408,59 +378,53 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
       const int s0 = sub * SUB, s1 = min(s0 + SUB, L);
       // B1: G recurrence (reverse)
       for (int tt = s1 - 1; tt >= s0; --tt) {
-        const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane], dyp = sDyp[tt * 32 + lane];
-        float Bt[SW], Ct[SW], Ht[SW];
-        ld_row16(Bt, sB + tt * N + w * SW);
-        ld_row16(Ct, sC + tt * N + w * SW);
-        if (HS) ld_row16(Ht, sDhs + tt * N + w * SW);
-        float duq[4] = {0.f, 0.f, 0.f, 0.f};
-        float gb[SW];
+        const float2 dd = f2(sDt[tt * 32 + lane]), dx2 = f2(sDtx[tt * 32 + lane]), dy2 = f2(sDyp[tt * 32 + lane]);
+        float2 Bt[SW / 2], Ct[SW / 2], Ht[SW / 2];
+        ld_row16p(Bt, sB + tt * N + w * SW, qx);
+        ld_row16p(Ct, sC + tt * N + w * SW, qx);
+        if (HS) ld_row16p(Ht, sDhs + tt * N + w * SW, qx);
+        float2 duq[2] = {f2(0.f), f2(0.f)};
+        float2 gb[SW / 2];
         uint32_t* gdst = reinterpret_cast<uint32_t*>(sG) + (int64_t)(tt - s0) * (SW / 2) * NT + tid;
 #pragma unroll
-        for (int j = 0; j < SW; j += 2) {
-          float G0 = fmaf(Ct[j], dyp, P[j]), G1 = fmaf(Ct[j + 1], dyp, P[j + 1]);
-          if (HS) { G0 += Ht[j]; G1 += Ht[j + 1]; }
-          __nv_bfloat162 gp = __floats2bfloat162_rn(G0, G1);
-          gdst[(j / 2) * NT] = *reinterpret_cast<uint32_t*>(&gp);
-          duq[j & 3] = fmaf(G0, Bt[j], duq[j & 3]);
-          duq[(j + 1) & 3] = fmaf(G1, Bt[j + 1], duq[(j + 1) & 3]);
-          gb[j] = G0 * dxv;
-          gb[j + 1] = G1 * dxv;
-          P[j] = ex2(A2[j] * d) * G0;
-          P[j + 1] = ex2(A2[j + 1] * d) * G1;
+        for (int j = 0; j < SW / 2; ++j) {
+          float2 G = fma2(Ct[j], dy2, P[j]);
+          if (HS) G = add2(G, Ht[j]);
+          __nv_bfloat162 gp = __floats2bfloat162_rn(G.x, G.y);
+          gdst[j * NT] = *reinterpret_cast<uint32_t*>(&gp);
+          duq[j & 1] = fma2(G, Bt[j], duq[j & 1]);
+          gb[j] = mul2(G, dx2);
+          P[j] = mul2(ex2x2(mul2(A2[j], dd)), G);
         }
-        atomicAdd(&sDU[tt * 32 + lane], (duq[0] + duq[1]) + (duq[2] + duq[3]));
-        const float r = reduce_scatter16(gb, lane);
+        atomicAdd(&sDU[tt * 32 + lane], (duq[0].x + duq[0].y) + (duq[1].x + duq[1].y));
+        const float r = reduce_scatter16p(gb, lane);
         if ((lane & 1) == 0)
           p.dB_part[(((int64_t)b * p.G + cblk) * p.S + t0 + tt) * N + w * SW + (lane >> 1)] = r;
       }
       // B2: recompute h over the sub-chunk and form the decay gradients
       {
-        float h[SW];
-        const float* src = scratch + (int64_t)sub * SW * NT;
+        float2 h[SW / 2];
+        const float2* src = reinterpret_cast<const float2*>(scratch + (int64_t)sub * SW * NT);
 #pragma unroll
-        for (int j = 0; j < SW; ++j) h[j] = src[j * NT + tid];
+        for (int j = 0; j < SW / 2; ++j) h[j] = src[j * NT + tid];
         for (int tt = s0; tt < s1; ++tt) {
-          const float d = sDt[tt * 32 + lane], dxv = sDtx[tt * 32 + lane];
-          float Bt[SW];
-          ld_row16(Bt, sB + tt * N + w * SW);
+          const float d = sDt[tt * 32 + lane];
+          const float2 dd = f2(d), mdd = f2(-d), dx2 = f2(sDtx[tt * 32 + lane]);
+          float2 Bt[SW / 2];
+          ld_row16p(Bt, sB + tt * N + w * SW, qx);
           const uint32_t* gsrc = reinterpret_cast<const uint32_t*>(sG) + (int64_t)(tt - s0) * (SW / 2) * NT + tid;
-          float ddq[4] = {0.f, 0.f, 0.f, 0.f};
+          float2 ddq[2] = {f2(0.f), f2(0.f)};
 #pragma unroll
-          for (int j = 0; j < SW; j += 2) {
-            const uint32_t gw = gsrc[(j / 2) * NT];
+          for (int j = 0; j < SW / 2; ++j) {
+            const uint32_t gw = gsrc[j * NT];
             const float2 gf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw));
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const float a = ex2(A2[j + u] * d);
-              const float v = a * h[j + u];
-              h[j + u] = fmaf(Bt[j + u], dxv, v);
-              const float gv = (u == 0 ? gf.x : gf.y) * v;
-              ddq[(j + u) & 3] = fmaf(gv, A2[j + u], ddq[(j + u) & 3]);
-              dAacc[j + u] = fmaf(gv, -d, dAacc[j + u]);
-            }
+            const float2 v = mul2(ex2x2(mul2(A2[j], dd)), h[j]);
+            h[j] = fma2(Bt[j], dx2, v);
+            const float2 gv = mul2(gf, v);
+            ddq[j & 1] = fma2(gv, A2[j], ddq[j & 1]);
+            dAacc[j] = fma2(gv, mdd, dAacc[j]);
           }
-          atomicAdd(&sDD[tt * 32 + lane], (ddq[0] + ddq[1]) + (ddq[2] + ddq[3]));
+          atomicAdd(&sDD[tt * 32 + lane], (ddq[0].x + ddq[0].y) + (ddq[1].x + ddq[1].y));
         }
       }
     }
@@ -483,7 +447,7 @@ __global__ void __launch_bounds__(NW * 32, 2) scan_bwd_kernel(Params p) {
   }
   __syncthreads();
   {
-    const float r = reduce_scatter16(dAacc, lane);
+    const float r = reduce_scatter16p(dAacc, lane);
     if ((lane & 1) == 0) atomicAdd(&p.dA[w * SW + (lane >> 1)], r);
   }
   if (tid < 32 && cvalid) atomicAdd(&p.dD[c], sDsum[tid]);
