@@ -45,8 +45,8 @@ def _args():
     ap.add_argument("--impl", default="mamformer_b200", choices=["mamformer_b200", "reference"])
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--seq", type=int, default=4096)
-    ap.add_argument("--micro-batch", type=int, default=1)
-    ap.add_argument("--grad-accum", type=int, default=16)
+    ap.add_argument("--micro-batch", type=int, default=4)
+    ap.add_argument("--grad-accum", type=int, default=4)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-launches", type=int, default=1)

@@ -27,8 +27,10 @@
 //               M=128 x N=BN x K=16 per instruction, 4 per 64-wide k-block; tcgen05.commit
 //               releases the smem stage and, at tile end, publishes the accumulator.
 //   warps 2..5  epilogue: tcgen05.ld 32x32b.x32 from a double-buffered accumulator (2*BN TMEM
-//               columns), scale, convert, store (bf16 / fp32, or fp32 read-modify-write to
-//               accumulate straight into fp32 gradient buffers).
+//               columns), scale, convert; dense / grouped-K: stage 32 x 128-byte blocks in shared
+//               memory and write them with bulk tensor stores, or bulk tensor reduce-adds that
+//               accumulate straight into fp32 gradient buffers at L2; grouped-M / TP modes:
+//               per-thread stores.
 // Grouped-M launches use an upper bound on the tile count (no host synchronisation); tiles past
 // the device-side tile table are skipped identically by all three roles.
 // Every wait is bounded (clock64); on timeout the CTA records an error code in g_mamf_gemm_err,
@@ -108,6 +110,29 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
 }
+
+// Bulk tensor store / reduce-add from shared memory (epilogue of the dense and grouped-K modes).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // UMMA shared-memory descriptor (sm100 layout: version 1 at bits 46-47, swizzle at 61-63).
 //   K-major SW128 : LBO = 16 B (unused), SBO = 1024 B (8 rows x 128 B); +32 B per K=16 step.
@@ -211,7 +236,19 @@ __device__ __forceinline__ void k_range(const Params& p, const Tile& tl, int& k0
 }
 
 // ---- the kernel -----------------------------------------------------------------------------------
-struct MapSet { CUtensorMap m[8]; };   // mode 3: one A tensor map per rank shard
+struct MapSet { CUtensorMap m[8]; };   // mode 3: one A tensor map per rank shard; modes 0/2: m[0] = D map
+
+// Dense and grouped-K tiles are written by bulk tensor stores (bf16 / fp32) or bulk tensor
+// reduce-adds (fp32 accumulation into gradient buffers, performed at L2 without a round trip
+// through the SM): each epilogue warp stages a 32-row x 128-byte block in shared memory (128-byte
+// swizzle, two buffers per warp) and one lane issues the copy.  Grouped-M tiles (whose rows may
+// end inside the tile) and the tensor-parallel modes keep per-thread stores.
+template <int MODE, typename OutT, bool ACCUM>
+__host__ __device__ constexpr bool tma_epilogue() {
+  return (MODE == 0 || MODE == 2) && !(sizeof(OutT) == 2 && ACCUM);
+}
+constexpr int EPI_BUF_BYTES = 32 * 128;                      // 32 rows x 128 bytes
+constexpr int EPI_STAGE_BYTES = 4 * 2 * EPI_BUF_BYTES;       // 4 epilogue warps x 2 buffers
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, typename OutT, bool ACCUM>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -222,10 +259,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t IDESC = instr_desc(BN, A_MN, B_MN);
   constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  constexpr bool TMA_EPI = tma_epilogue<MODE, OutT, ACCUM>();
+  constexpr int EPI_BYTES = TMA_EPI ? EPI_STAGE_BYTES : 0;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi = smem + STAGES * STAGE_BYTES;                 // epilogue staging (1024-aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;     // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2]
@@ -327,6 +367,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int sub = warp & 3;                  // TMEM lane quarter accessible to this warp
     const int row_in_tile = sub * 32 + lane;
     int local = 0;
+    int epi_buf = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
       const Tile tl = tile_of<MODE>(p, t);
       if (tl.g < 0) continue;
@@ -351,6 +392,54 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         mbar_arrive(&acc_empty[buf]);
         continue;
       }
+      if constexpr (TMA_EPI) {
+        // stage 32 rows x 128 bytes per copy: 32 fp32 columns, or 64 bf16 columns
+        constexpr int COLS = 128 / (int)sizeof(OutT);
+        const int row0 = tl.m0 + sub * 32;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += COLS) {
+          float r[COLS];
+          tmem_ld32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(buf * BN + c),
+                    *reinterpret_cast<float(*)[32]>(&r[0]));
+          if constexpr (COLS == 64)
+            tmem_ld32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(buf * BN + c + 32),
+                      *reinterpret_cast<float(*)[32]>(&r[32]));
+          if (lane == 0) bulk_wait_read<1>();        // the copy that last read this buffer is done
+          __syncwarp();
+          uint8_t* sb = epi + (sub * 2 + epi_buf) * EPI_BUF_BYTES + lane * 128;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            uint4 v;
+            if constexpr (sizeof(OutT) == 4) {
+              v.x = __float_as_uint(p.alpha * r[4 * q]);     v.y = __float_as_uint(p.alpha * r[4 * q + 1]);
+              v.z = __float_as_uint(p.alpha * r[4 * q + 2]); v.w = __float_as_uint(p.alpha * r[4 * q + 3]);
+            } else {
+              __nv_bfloat162 b0 = __floats2bfloat162_rn(p.alpha * r[8 * q], p.alpha * r[8 * q + 1]);
+              __nv_bfloat162 b1 = __floats2bfloat162_rn(p.alpha * r[8 * q + 2], p.alpha * r[8 * q + 3]);
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(p.alpha * r[8 * q + 4], p.alpha * r[8 * q + 5]);
+              __nv_bfloat162 b3 = __floats2bfloat162_rn(p.alpha * r[8 * q + 6], p.alpha * r[8 * q + 7]);
+              v.x = *reinterpret_cast<uint32_t*>(&b0); v.y = *reinterpret_cast<uint32_t*>(&b1);
+              v.z = *reinterpret_cast<uint32_t*>(&b2); v.w = *reinterpret_cast<uint32_t*>(&b3);
+            }
+            *reinterpret_cast<uint4*>(sb + ((q ^ (lane & 7)) << 4)) = v;   // 128-byte swizzle
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const void* src = epi + (sub * 2 + epi_buf) * EPI_BUF_BYTES;
+            const int col = n_base + c;
+            if (MODE == 2) {
+              if (ACCUM) tma_reduce_add_3d(&tmAs.m[0], src, col, row0, tl.g);
+              else tma_store_3d(&tmAs.m[0], src, col, row0, tl.g);
+            } else {
+              if (ACCUM) tma_reduce_add_2d(&tmAs.m[0], src, col, row0);
+              else tma_store_2d(&tmAs.m[0], src, col, row0);
+            }
+            bulk_commit();
+          }
+          epi_buf ^= 1;
+        }
+      } else {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float r[32];
@@ -387,9 +476,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
         }
       }
+      }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
+    if (TMA_EPI && lane == 0) bulk_wait_all();    // every staged block written before exit
   }
 
   __syncwarp();
@@ -440,10 +531,30 @@ static CUtensorMap make_map(const void* base, int rank, const uint64_t* dims, co
   return m;
 }
 
+// Output tensor map for the bulk-store epilogue: box = 128 bytes x 32 rows, 128-byte swizzle.
+// dims/strides innermost first (strides in bytes for dims >= 1).
+static CUtensorMap make_map_d(const at::Tensor& D, int rank, const uint64_t* dims, const uint64_t* strides_bytes) {
+  const bool f32 = D.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || D.scalar_type() == at::kBFloat16, "tcgen05 gemm: bf16 or fp32 output");
+  TORCH_CHECK(aligned16(D.data_ptr()), "tcgen05 gemm: output base must be 16-byte aligned");
+  for (int i = 0; i < rank - 1; ++i) TORCH_CHECK(strides_bytes[i] % 16 == 0, "tcgen05 gemm: output strides must be 16-byte multiples");
+  CUtensorMap m;
+  cuuint64_t gd[3], gs[2];
+  cuuint32_t bx[3] = {f32 ? 32u : 64u, 32u, 1u}, es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) gd[i] = dims[i];
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+  CUresult r = encode_fn()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank,
+                           D.data_ptr(), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output) failed: ", (int)r);
+  return m;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int MODE, typename OutT, bool ACCUM>
 static void launch(const CUtensorMap& a, const CUtensorMap& b, const Params& p, const MapSet& as) {
   auto k = gemm_kernel<BN, STAGES, A_MN, B_MN, MODE, OutT, ACCUM>;
-  const int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  const int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256 +
+                   (tma_epilogue<MODE, OutT, ACCUM>() ? EPI_STAGE_BYTES : 0);
   MAMF_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int grid = std::max(1, std::min(p.total_tiles, num_sms()));
   k<<<grid, NUM_THREADS, smem, stream()>>>(a, b, p, as);
@@ -568,16 +679,26 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
   }
   if (p.total_tiles == 0) return;
   const auto out = D.scalar_type();
+  // dense / grouped-K outputs are written by bulk tensor stores (reduce-adds when accumulating)
+  MapSet dm{};
   if (mode == 0) {
-    if (!a_mn && !b_mn) dispatch_out<false, false, 0>(ma, mb, p, out, accumulate, bn);
-    else if (!a_mn && b_mn) dispatch_out<false, true, 0>(ma, mb, p, out, accumulate, bn);
-    else if (a_mn && b_mn) dispatch_out<true, true, 0>(ma, mb, p, out, accumulate, bn);
-    else dispatch_out<true, false, 0>(ma, mb, p, out, accumulate, bn);
+    uint64_t dims[2] = {(uint64_t)N, (uint64_t)M}, st[1] = {(uint64_t)(p.ldd * esz_d)};
+    dm.m[0] = make_map_d(D, 2, dims, st);
+  } else if (mode == 2) {
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)p.G};
+    uint64_t st[2] = {(uint64_t)(p.ldd * esz_d), (uint64_t)(p.d_gstride * esz_d)};
+    dm.m[0] = make_map_d(D, 3, dims, st);
+  }
+  if (mode == 0) {
+    if (!a_mn && !b_mn) dispatch_out<false, false, 0>(ma, mb, p, out, accumulate, bn, dm);
+    else if (!a_mn && b_mn) dispatch_out<false, true, 0>(ma, mb, p, out, accumulate, bn, dm);
+    else if (a_mn && b_mn) dispatch_out<true, true, 0>(ma, mb, p, out, accumulate, bn, dm);
+    else dispatch_out<true, false, 0>(ma, mb, p, out, accumulate, bn, dm);
   } else if (mode == 1) {
     if (!b_mn) dispatch_out<false, false, 1>(ma, mb, p, out, accumulate, bn);
     else dispatch_out<false, true, 1>(ma, mb, p, out, accumulate, bn);
   } else {
-    dispatch_out<true, true, 2>(ma, mb, p, out, accumulate, bn);
+    dispatch_out<true, true, 2>(ma, mb, p, out, accumulate, bn, dm);
   }
 }
 
