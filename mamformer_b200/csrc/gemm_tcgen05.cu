@@ -27,10 +27,10 @@
 //               M=128 x N=BN x K=16 per instruction, 4 per 64-wide k-block; tcgen05.commit
 //               releases the smem stage and, at tile end, publishes the accumulator.
 //   warps 2..5  epilogue: tcgen05.ld 32x32b.x32 from a double-buffered accumulator (2*BN TMEM
-//               columns), scale, convert; dense / grouped-K: stage 32 x 128-byte blocks in shared
+//               columns), scale, convert; dense / grouped modes: stage 32 x 128-byte blocks in shared
 //               memory and write them with bulk tensor stores, or bulk tensor reduce-adds that
-//               accumulate straight into fp32 gradient buffers at L2; grouped-M / TP modes:
-//               per-thread stores.
+//               accumulate straight into fp32 gradient buffers at L2; TP modes: per-thread
+//               stores.
 // Grouped-M launches use an upper bound on the tile count (no host synchronisation); tiles past
 // the device-side tile table are skipped identically by all three roles.
 // Every wait is bounded (clock64); on timeout the CTA records an error code in g_mamf_gemm_err,
@@ -238,14 +238,16 @@ __device__ __forceinline__ void k_range(const Params& p, const Tile& tl, int& k0
 // ---- the kernel -----------------------------------------------------------------------------------
 struct MapSet { CUtensorMap m[8]; };   // mode 3: one A tensor map per rank shard; modes 0/2: m[0] = D map
 
-// Dense and grouped-K tiles are written by bulk tensor stores (bf16 / fp32) or bulk tensor
-// reduce-adds (fp32 accumulation into gradient buffers, performed at L2 without a round trip
-// through the SM): each epilogue warp stages a 32-row x 128-byte block in shared memory (128-byte
-// swizzle, two buffers per warp) and one lane issues the copy.  Grouped-M tiles (whose rows may
-// end inside the tile) and the tensor-parallel modes keep per-thread stores.
+// Dense, grouped-M and grouped-K tiles are written by bulk tensor stores (bf16 / fp32) or bulk
+// tensor reduce-adds (fp32 accumulation into gradient buffers, performed at L2 without a round
+// trip through the SM): each epilogue warp stages a 32-row x 128-byte block in shared memory
+// (128-byte swizzle, two buffers per warp) and one lane issues the copy.  Grouped-M groups start
+// and end on 64-row boundaries, so a warp's 32 rows lie entirely inside or entirely past its
+// group's end; warps past the end issue nothing.  The tensor-parallel modes keep per-thread
+// stores (their outputs may be peer memory).
 template <int MODE, typename OutT, bool ACCUM>
 __host__ __device__ constexpr bool tma_epilogue() {
-  return (MODE == 0 || MODE == 2) && !(sizeof(OutT) == 2 && ACCUM);
+  return (MODE == 0 || MODE == 1 || MODE == 2) && !(sizeof(OutT) == 2 && ACCUM);
 }
 constexpr int EPI_BUF_BYTES = 32 * 128;                      // 32 rows x 128 bytes
 constexpr int EPI_STAGE_BYTES = 4 * 2 * EPI_BUF_BYTES;       // 4 epilogue warps x 2 buffers
@@ -396,8 +398,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // stage 32 rows x 128 bytes per copy: 32 fp32 columns, or 64 bf16 columns
         constexpr int COLS = 128 / (int)sizeof(OutT);
         const int row0 = tl.m0 + sub * 32;
+        const bool warp_rows = MODE != 1 || row0 < tl.m_end;    // grouped-M: rows of this group
 #pragma unroll 1
-        for (int c = 0; c < BN; c += COLS) {
+        for (int c = 0; c < BN && warp_rows; c += COLS) {
           float r[COLS];
           tmem_ld32(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(buf * BN + c),
                     *reinterpret_cast<float(*)[32]>(&r[0]));
@@ -428,7 +431,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           if (lane == 0) {
             const void* src = epi + (sub * 2 + epi_buf) * EPI_BUF_BYTES;
             const int col = n_base + c;
-            if (MODE == 2) {
+            if constexpr (MODE == 2) {
               if (ACCUM) tma_reduce_add_3d(&tmAs.m[0], src, col, row0, tl.g);
               else tma_store_3d(&tmAs.m[0], src, col, row0, tl.g);
             } else {
@@ -681,7 +684,7 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
   const auto out = D.scalar_type();
   // dense / grouped-K outputs are written by bulk tensor stores (reduce-adds when accumulating)
   MapSet dm{};
-  if (mode == 0) {
+  if (mode == 0 || mode == 1) {
     uint64_t dims[2] = {(uint64_t)N, (uint64_t)M}, st[1] = {(uint64_t)(p.ldd * esz_d)};
     dm.m[0] = make_map_d(D, 2, dims, st);
   } else if (mode == 2) {
@@ -695,8 +698,8 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
     else if (a_mn && b_mn) dispatch_out<true, true, 0>(ma, mb, p, out, accumulate, bn, dm);
     else dispatch_out<true, false, 0>(ma, mb, p, out, accumulate, bn, dm);
   } else if (mode == 1) {
-    if (!b_mn) dispatch_out<false, false, 1>(ma, mb, p, out, accumulate, bn);
-    else dispatch_out<false, true, 1>(ma, mb, p, out, accumulate, bn);
+    if (!b_mn) dispatch_out<false, false, 1>(ma, mb, p, out, accumulate, bn, dm);
+    else dispatch_out<false, true, 1>(ma, mb, p, out, accumulate, bn, dm);
   } else {
     dispatch_out<true, true, 2>(ma, mb, p, out, accumulate, bn, dm);
   }
