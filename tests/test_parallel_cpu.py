@@ -88,3 +88,12 @@ def test_diagnostics_cpu():
     st = mon.end_step(1, 2.0, 1000)
     assert st.loss == 2.0 and "communication" in mon.get_full_report()
     mon.reset()
+
+
+def test_p2p_transport_selection_cpu():
+    """The peer-memory gradient transport is chosen only for CUDA groups of 2..8 ranks; on CPU
+    (or a single rank) the optimizer keeps ordinary buffers and the NCCL/gloo all-reduce."""
+    from mamformer_b200.optim import _p2p_ok
+    assert not _p2p_ok("nccl", object(), "cuda")
+    assert not _p2p_ok("p2p", None, "cuda")
+    assert not _p2p_ok("p2p", object(), "cpu")
