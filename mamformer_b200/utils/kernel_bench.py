@@ -52,6 +52,20 @@ def case_grouped(E=128, k=8, T=4096, d=4096, I=576):
     return (lambda: gemm.grouped_mm(x, w, seg, tile_off, out=out)), 2.0 * T * k * I * d, (rows * d + E * I * d + rows * I) * 2
 
 
+def case_wgrad(E=128, k=8, T=16384, d=4096, I=576):
+    """MoE weight gradient: grouped-K GEMM accumulated into the fp32 optimizer buffer (the
+    epilogue's bulk tensor reduce-add), micro-batch of 4 x 4096 tokens, 128 experts."""
+    from mamformer_b200.ops import gemm
+    from mamformer_b200.ops.moe import plan
+    idx = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)])
+    pos, seg, tile_off, _, rows = plan(idx, E)
+    dy = torch.randn(rows, I, device="cuda").bfloat16()
+    x = torch.randn(rows, d, device="cuda").bfloat16()
+    dw = torch.zeros(E, I, d, device="cuda")
+    return (lambda: gemm.grouped_wgrad(dy, x, seg, dw, accumulate=True)), 2.0 * T * k * I * d, \
+        (rows * (I + d)) * 2 + E * I * d * 4 * 2
+
+
 def case_scan(B=1, S=4096, D=8192, N=128, backward=False):
     """Selective scan (Mamba block of ultra-7b: d_inner 8192, d_state 128), fused gate."""
     from mamformer_b200.ops.native import _C
@@ -148,7 +162,7 @@ def case_router(T=4096, E=128, k=8):
     return (lambda: _C.router_topk(scores, k)), 0.0, T * E * 4 + T * k * 12
 
 
-CASES = {"gemm": case_gemm, "grouped": case_grouped, "scan": case_scan,
+CASES = {"gemm": case_gemm, "grouped": case_grouped, "wgrad": case_wgrad, "scan": case_scan,
          "scan_bwd": lambda: case_scan(backward=True), "linear_attn": case_linear_attn,
          "linear_attn_bwd": lambda: case_linear_attn(backward=True), "ce": case_ce, "moe": case_moe,
          "adamw": case_adamw, "flash_attn": case_flash_attn,
