@@ -21,6 +21,7 @@ import torch.nn.functional as F
 
 from mamformer_b200 import ops
 from mamformer_b200.models.norm import RMSNorm
+from mamformer_b200.ops.linear import linear as _native_linear
 
 
 class ExpertCommunicationLayer(nn.Module):
@@ -86,7 +87,7 @@ class CommunicativeMoE(nn.Module):
             if base.use_balance_lock and self.training:
                 logits, _ = base._apply_balance_lock(logits, spatial)
         else:
-            logits = F.linear(xf, base.router.weight.to(xf.dtype)).float()
+            logits = _native_linear(xf, base.router.weight.to(xf.dtype)).float()
         if base.router_temperature != 1.0:
             logits = logits / base.router_temperature
         gates, idx = base._select(logits)

@@ -20,6 +20,7 @@ from typing import Optional, Tuple
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+from mamformer_b200.ops.linear import linear as _native_linear
 
 
 class DynamicGate(nn.Module):
@@ -49,7 +50,7 @@ class EntropyRouter(nn.Module):
 
     def forward(self, x: torch.Tensor, expert_bias: Optional[torch.Tensor] = None):
         flat = x.reshape(-1, self.d_model)
-        logits = F.linear(flat, self.weight.to(flat.dtype))
+        logits = _native_linear(flat, self.weight.to(flat.dtype))
         if expert_bias is not None:
             logits = logits + expert_bias
         logp = F.log_softmax(logits, dim=-1)

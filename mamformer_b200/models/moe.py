@@ -32,6 +32,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from mamformer_b200 import ops
+from mamformer_b200.ops.linear import linear as _native_linear
 
 
 class _SwiGLUExpert(nn.Module):
@@ -195,7 +196,7 @@ class DeepSeekMoE(nn.Module):
         return out if out is not None else torch.zeros_like(xf)
 
     def _router_logits(self, xf: torch.Tensor) -> torch.Tensor:
-        logits = F.linear(xf, self.router.weight.to(xf.dtype)).float()
+        logits = _native_linear(xf, self.router.weight.to(xf.dtype)).float()
         if self.router_temperature != 1.0:
             logits = logits / self.router_temperature
         return logits
@@ -311,7 +312,7 @@ class MoERouter(nn.Module):
         nn.init.normal_(self.weight, mean=0.0, std=0.02 / n_experts ** 0.5)
 
     def forward(self, x: torch.Tensor, expert_bias: Optional[torch.Tensor] = None):
-        logits = F.linear(x, self.weight.to(x.dtype)).float()
+        logits = _native_linear(x, self.weight.to(x.dtype)).float()
         if self.temperature != 1.0:
             logits = logits / self.temperature
         if expert_bias is not None:
