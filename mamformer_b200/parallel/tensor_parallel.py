@@ -22,6 +22,15 @@ need TP-sharded routed experts is rejected.
 
 Autograd collectives (``f`` / ``g`` of Megatron): ``copy_to_tp`` is identity forward and
 all-reduce backward; ``reduce_from_tp`` is all-reduce forward and identity backward.
+
+On CUDA in bf16 (and when the token count splits into 128-row shards) every TP all-reduce that
+follows a GEMM is fused into it: the row-parallel forward and the column-parallel input-gradient
+run as the tcgen05 GEMM whose epilogue stores each row shard of the partial product straight
+into the owning rank's staging buffer over NVLink (GEMM -> reduce-scatter in one kernel, see
+``tp_fused.gemm_rs``), followed by an all-gather of the reduced shards; the local GEMMs and the
+weight gradients (accumulated into the fp32 optimizer buffer) run on the same kernel.  Elsewhere
+(CPU, fp32, ragged shapes) the layers use the collectives above.  ``shard_model_tp(fused=False)``
+keeps the unfused path everywhere.
 """
 
 from __future__ import annotations
@@ -193,6 +202,71 @@ def _sliced(p: torch.Tensor, dim: int, index: torch.Tensor) -> nn.Parameter:
     return out
 
 
+def _fused_ok(x2: torch.Tensor, w: torch.Tensor, group) -> bool:
+    """The fused GEMM + reduce-scatter applies: CUDA bf16 operands, 16-byte rows, and the token
+    count splits into shards of whole 128-row tiles."""
+    if group is None or not x2.is_cuda or x2.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        return False
+    P = dist.get_world_size(group)
+    T = x2.shape[0]
+    return (P > 1 and T % (P * 128) == 0 and x2.shape[1] % 8 == 0 and w.shape[0] % 8 == 0
+            and w.shape[1] % 8 == 0)
+
+
+def _gather_shards(z: torch.Tensor, group) -> torch.Tensor:
+    P = dist.get_world_size(group)
+    out = torch.empty(P * z.shape[0], z.shape[1], device=z.device, dtype=z.dtype)
+    with _diag("tp_all_gather", z):
+        dist.all_gather_into_tensor(out, z.contiguous(), group=group)
+    return out
+
+
+class _FusedRowLinear(torch.autograd.Function):
+    """y (T, N) = sum_r x_r W_r^T: fused GEMM -> reduce-scatter, then all-gather of the shards.
+    Backward needs no collective: dx_r = dy W_r, dW_r += dy^T x_r."""
+
+    @staticmethod
+    def forward(ctx, x2, w, group):
+        from mamformer_b200.parallel import tp_fused
+        ctx.save_for_backward(x2, w)
+        ctx.group = group
+        return _gather_shards(tp_fused.gemm_rs(x2, w, group), group)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from mamformer_b200.ops import gemm
+        from mamformer_b200.parallel.tp_fused import _wgrad
+        x2, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = gemm.mm_nn(dy, w) if ctx.needs_input_grad[0] else None
+        dw = _wgrad(w, dy, x2) if ctx.needs_input_grad[1] else None
+        return dx, dw, None
+
+
+class _FusedColumnLinear(torch.autograd.Function):
+    """y_r = x W_r^T with x replicated; its input gradient sum_r dy_r W_r is the fused
+    GEMM -> reduce-scatter followed by an all-gather."""
+
+    @staticmethod
+    def forward(ctx, x2, w, group):
+        from mamformer_b200.ops import gemm
+        ctx.save_for_backward(x2, w)
+        ctx.group = group
+        return gemm.mm(x2, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from mamformer_b200.parallel import tp_fused
+        from mamformer_b200.parallel.tp_fused import _wgrad
+        x2, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = _gather_shards(tp_fused.gemm_rs(dy, w, ctx.group, b_mn=True), ctx.group)
+        dw = _wgrad(w, dy, x2) if ctx.needs_input_grad[1] else None
+        return dx, dw, None
+
+
 class ColumnParallelLinear(nn.Module):
     """y_local = x W_local^T (+ b_local); W sharded along its output dimension."""
 
@@ -222,6 +296,11 @@ class ColumnParallelLinear(nn.Module):
         return m
 
     def forward(self, x):
+        if getattr(self, "fused", True) and not self.gather_output and self.bias is None:
+            x2 = x.reshape(-1, x.shape[-1])
+            if _fused_ok(x2, self.weight, self.group):
+                y = _FusedColumnLinear.apply(x2.contiguous(), self.weight, self.group)
+                return y.view(*x.shape[:-1], self.out_local)
         x = copy_to_tp(x, self.group)
         y = F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
         return gather_from_tp(y, self.group) if self.gather_output else y
@@ -261,6 +340,12 @@ class RowParallelLinear(nn.Module):
     def forward(self, x):
         if not self.input_is_parallel:
             x = scatter_to_tp(x, self.group)
+        if getattr(self, "fused", True):
+            x2 = x.reshape(-1, x.shape[-1])
+            if _fused_ok(x2, self.weight, self.group):
+                y = _FusedRowLinear.apply(x2.contiguous(), self.weight, self.group)
+                y = y.view(*x.shape[:-1], self.out_features)
+                return y if self.bias is None else y + self.bias.to(y.dtype)
         y = reduce_from_tp(F.linear(x, self.weight.to(x.dtype)), self.group)
         return y if self.bias is None else y + self.bias.to(y.dtype)
 
@@ -345,9 +430,10 @@ def _shard_ffn(mod, r, n, group):
     _row(mod, "down_proj", rows, group)
 
 
-def shard_model_tp(model: nn.Module, tp_size: int, group=None) -> nn.Module:
+def shard_model_tp(model: nn.Module, tp_size: int, group=None, fused: bool = True) -> nn.Module:
     """Shard every supported block of ``model`` over the TP group, in place.  Must run before
-    the optimizer is built."""
+    the optimizer is built.  ``fused``: fuse the reduce-scatter half of each TP all-reduce into
+    the preceding GEMM where the shapes allow (CUDA, bf16)."""
     group = group if group is not None else _TP_GROUP
     if tp_size <= 1:
         return model
@@ -380,6 +466,8 @@ def shard_model_tp(model: nn.Module, tp_size: int, group=None) -> nn.Module:
     for m in model.modules():
         if hasattr(m, "kv_dim") and hasattr(m, "k_expand"):
             m.kv_dim = m.k_expand.out_local
+        if isinstance(m, (ColumnParallelLinear, RowParallelLinear)):
+            m.fused = fused
     model._mamf_tp = (r, n)
     return model
 

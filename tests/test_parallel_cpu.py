@@ -97,3 +97,13 @@ def test_p2p_transport_selection_cpu():
     assert not _p2p_ok("nccl", object(), "cuda")
     assert not _p2p_ok("p2p", None, "cuda")
     assert not _p2p_ok("p2p", object(), "cpu")
+
+
+def test_fused_tp_path_selection_cpu():
+    """The fused GEMM -> reduce-scatter TP path applies only to CUDA bf16 operands whose token
+    count splits into whole 128-row shards; CPU tensors keep the collective path."""
+    from mamformer_b200.parallel.tensor_parallel import _fused_ok
+    x = torch.zeros(512, 64, dtype=torch.bfloat16)
+    w = torch.zeros(32, 64, dtype=torch.bfloat16)
+    assert not _fused_ok(x, w, None)
+    assert not _fused_ok(x, w, object())          # CPU tensors: never fused

@@ -69,3 +69,8 @@ def test_expert_parallel_moe_two_gpus():
 @needs2
 def test_tp_fused_gemms_two_gpus():
     _spawn("tp_fused_worker", 2)
+
+
+@needs2
+def test_tp_model_fused_matches_unfused_two_gpus():
+    _spawn("tp_model_fused_worker", 2)
