@@ -62,6 +62,20 @@ class _Workspace:
         self.epoch += 1
         C.ep_barrier(self.hg.signal_pad_ptrs, self.rank, self.epoch, _SLOT0)
 
+    def side_stream(self, device):
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=device)
+        return self._side
+
+    def pull_buffer(self, i: int, rows: int, K: int, device) -> torch.Tensor:
+        """Local landing buffer i for a pulled peer shard (grown on demand, kept across calls)."""
+        bufs = self.__dict__.setdefault("_pull", {})
+        b = bufs.get(i)
+        if b is None or b.numel() < rows * K:
+            b = torch.empty(rows * K, device=device, dtype=torch.bfloat16)
+            bufs[i] = b
+        return b[: rows * K].view(rows, K)
+
 
 _WS = {}
 
@@ -78,8 +92,55 @@ def _C():
     return require_native()
 
 
-def ag_gemm(x_local: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False) -> torch.Tensor:
-    """all_gather_rows(x_local) @ w^T (w (N, K)), or @ w (w (K, N)) with ``b_mn``; x_local (rows, K)."""
+# all-gather -> GEMM implementation: "pull" (default) or "kernel"
+_AG_IMPL = "pull"
+
+
+def ag_gemm(x_local: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False, impl: str = None) -> torch.Tensor:
+    """all_gather_rows(x_local) @ w^T (w (N, K)), or @ w (w (K, N)) with ``b_mn``; x_local (rows, K).
+
+    ``impl="pull"``: the copy engines pull every peer's shard from its symmetric buffer into a
+    local buffer (each remote row crosses NVLink once) on a side stream while the tensor cores
+    multiply the local shard; each remote shard's GEMM starts as soon as its copy lands.
+    ``impl="kernel"``: one tcgen05 GEMM whose TMA producer reads the peers' shards directly (no
+    multicast); every output n-tile re-reads its remote A tile over NVLink."""
+    if (impl or _AG_IMPL) == "kernel":
+        return ag_gemm_kernel(x_local, w, group, b_mn)
+    from mamformer_b200.ops import gemm
+    C = _C()
+    ws = _ws(group)
+    rows, K = x_local.shape
+    N = w.shape[1] if b_mn else w.shape[0]
+    P, r = ws.P, ws.rank
+    ws.ensure(rows * K, 0 if ws.stage is not None else 64, x_local.device)
+    ws.gather[: rows * K].view(rows, K).copy_(x_local)
+    ws.barrier(C)                                   # every shard written
+    out = torch.empty(P * rows, N, device=x_local.device, dtype=torch.bfloat16)
+    cur = torch.cuda.current_stream()
+    side = ws.side_stream(x_local.device)
+    start = torch.cuda.Event()
+    start.record(cur)
+    side.wait_event(start)
+    pulled = []
+    with torch.cuda.stream(side):
+        for i in range(1, P):
+            q = (r + i) % P
+            buf = ws.pull_buffer(i - 1, rows, K, x_local.device)
+            buf.copy_(ws.hg.get_buffer(q, (rows, K), torch.bfloat16), non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            pulled.append((q, buf, ev))
+    mm = gemm.mm_nn if b_mn else gemm.mm
+    mm(x_local, w, out=out[r * rows:(r + 1) * rows])
+    for q, buf, ev in pulled:
+        cur.wait_event(ev)
+        mm(buf, w, out=out[q * rows:(q + 1) * rows])
+    ws.barrier(C)                                   # every peer done pulling this rank's shard
+    return out
+
+
+def ag_gemm_kernel(x_local: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False) -> torch.Tensor:
+    """The single-kernel variant of :func:`ag_gemm` (TMA reads of the peers' shards)."""
     C = _C()
     ws = _ws(group)
     rows, K = x_local.shape

@@ -10,8 +10,10 @@ one GPU at the measured peer-copy bandwidth, 770 GB/s per direction).  Each fuse
 compared with the same work done as NCCL collective + this repository's GEMM (the unfused
 baseline).
 
-* ag_gemm  - sequence-parallel column GEMM: all-gather of the row shards fused into the tcgen05
-             GEMM (TMA reads of the peers' shards).  NVLink bytes in: (P-1)/P * T * K * 2.
+* ag_gemm  - sequence-parallel column GEMM on all-gathered row shards: "pull" (copy-engine pulls
+             of the peers' shards overlapped with the local-shard GEMM) and "kernel" (the
+             tcgen05 GEMM's TMA producer reads the peers' shards).  NVLink bytes in:
+             (P-1)/P * T * K * 2.
 * gemm_rs  - row GEMM with the reduce-scatter fused into the epilogue (stores into the owners'
              staging slots) + local sum.  NVLink bytes out: (P-1)/P * T * N * 2.
 * dp_allreduce - 64 MiB fp32 gradient bucket summed by the peer-memory kernels (two-shot:
@@ -85,9 +87,11 @@ def case_ag_gemm(T=16384, K=4096, N=4096):
     def base():
         dist.all_gather_into_tensor(full, x)
         gemm.mm(full, w, out=out)
-    ms = _time(lambda: tp_fused.ag_gemm(x, w, dist.group.WORLD))
     mb = _time(base)
-    _report("ag_gemm", ms, mb, 2.0 * T * N * K, (P - 1) / P * T * K * 2, {"T": T, "K": K, "N": N})
+    for impl in ("pull", "kernel"):
+        ms = _time(lambda: tp_fused.ag_gemm(x, w, dist.group.WORLD, impl=impl))
+        _report("ag_gemm", ms, mb, 2.0 * T * N * K, (P - 1) / P * T * K * 2,
+                {"impl": impl, "T": T, "K": K, "N": N})
 
 
 def case_gemm_rs(T=16384, K=4096, N=4096):
