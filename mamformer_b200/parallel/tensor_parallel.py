@@ -23,15 +23,16 @@ need TP-sharded routed experts is rejected.
 Autograd collectives (``f`` / ``g`` of Megatron): ``copy_to_tp`` is identity forward and
 all-reduce backward; ``reduce_from_tp`` is all-reduce forward and identity backward.
 
-With ``shard_model_tp(fused=True)``, on CUDA in bf16 (and when the token count splits into
+With ``shard_model_tp(fused=True)`` (the default), on CUDA in bf16 (and when the token count splits into
 128-row shards) every TP all-reduce that follows a GEMM is fused into it: the row-parallel
 forward and the column-parallel input-gradient run as the tcgen05 GEMM whose epilogue stores
 each row shard of the partial product straight into the owning rank's staging buffer over
 NVLink (GEMM -> reduce-scatter in one kernel, see ``tp_fused.gemm_rs``), followed by an
 all-gather of the reduced shards; the local GEMMs and the weight gradients (accumulated into the
-fp32 optimizer buffer) run on the same kernel.  The default (``fused=False``) keeps GEMM + NCCL
-all-reduce: on 2 B200s the fused GEMM -> reduce-scatter measured 0.80 ms against 0.56 ms for
-GEMM + NCCL reduce-scatter at T = 16384, K = N = 4096 (``utils/comm_bench.py``).
+fp32 optimizer buffer) run on the same kernel.  ``tp_fused.gemm_rs`` defaults to its overlapped
+form (the other ranks' row blocks first, then copy-engine pulls of the peers' partials while the
+own rows multiply): 0.446 ms against 0.560 ms for GEMM + NCCL reduce-scatter on 2 B200s at
+T = 16384, K = N = 4096 (``utils/comm_bench.py``).  ``fused=False`` keeps GEMM + NCCL all-reduce.
 """
 
 from __future__ import annotations
@@ -431,7 +432,7 @@ def _shard_ffn(mod, r, n, group):
     _row(mod, "down_proj", rows, group)
 
 
-def shard_model_tp(model: nn.Module, tp_size: int, group=None, fused: bool = False) -> nn.Module:
+def shard_model_tp(model: nn.Module, tp_size: int, group=None, fused: bool = True) -> nn.Module:
     """Shard every supported block of ``model`` over the TP group, in place.  Must run before
     the optimizer is built.  ``fused``: fuse the reduce-scatter half of each TP all-reduce into
     the preceding GEMM where the shapes allow (CUDA, bf16)."""

@@ -154,8 +154,59 @@ def ag_gemm_kernel(x_local: torch.Tensor, w: torch.Tensor, group, b_mn: bool = F
     return out
 
 
-def gemm_rs(y: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False) -> torch.Tensor:
-    """reduce_scatter_rows(y @ w^T) over the group: returns this rank's (rows / P, N) block."""
+_RS_IMPL = "pull"
+
+
+def gemm_rs(y: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False, impl: str = None) -> torch.Tensor:
+    """reduce_scatter_rows(y @ w^T) over the group: returns this rank's (rows / P, N) block.
+
+    ``impl="pull"``: each rank first multiplies the row blocks owned by the other ranks into its
+    own symmetric staging buffer, then (bounded barrier) the copy engines pull every peer's
+    partial for this rank's rows into local buffers on a side stream while the tensor cores
+    multiply this rank's own rows; the partials are summed as they land.
+    ``impl="kernel"``: one tcgen05 GEMM whose epilogue stores each row block straight into the
+    owner's staging slot over NVLink, then a local sum of the slots."""
+    if (impl or _RS_IMPL) == "kernel":
+        return gemm_rs_kernel(y, w, group, b_mn)
+    from mamformer_b200.ops import gemm
+    C = _C()
+    ws = _ws(group)
+    M, K = y.shape
+    P, r = ws.P, ws.rank
+    rows = M // P
+    N = w.shape[1] if b_mn else w.shape[0]
+    ws.ensure(64 if ws.gather is None else 0, P * rows * N, y.device)
+    y = y.contiguous()
+    mm = gemm.mm_nn if b_mn else gemm.mm
+    stage = ws.stage[: P * rows * N].view(P * rows, N)
+    for i in range(1, P):                           # the other ranks' row blocks first
+        q = (r + i) % P
+        mm(y[q * rows:(q + 1) * rows], w, out=stage[q * rows:(q + 1) * rows])
+    ws.barrier(C)                                   # every rank's partials for the others are staged
+    cur = torch.cuda.current_stream()
+    side = ws.side_stream(y.device)
+    start = torch.cuda.Event()
+    start.record(cur)
+    side.wait_event(start)
+    pulled = []
+    with torch.cuda.stream(side):
+        for i in range(1, P):
+            q = (r - i) % P
+            buf = ws.pull_buffer(i - 1, rows, N, y.device)
+            buf.copy_(ws.hs.get_buffer(q, (rows, N), torch.bfloat16, r * rows * N), non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            pulled.append((buf, ev))
+    out = mm(y[r * rows:(r + 1) * rows], w)         # this rank's own partial, overlapping the pulls
+    for buf, ev in pulled:
+        cur.wait_event(ev)
+        out.add_(buf)
+    ws.barrier(C)                                   # every peer done pulling from this rank's stage
+    return out
+
+
+def gemm_rs_kernel(y: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False) -> torch.Tensor:
+    """The single-kernel variant of :func:`gemm_rs` (epilogue stores into the peers' staging)."""
     C = _C()
     ws = _ws(group)
     M, K = y.shape

@@ -14,8 +14,10 @@ baseline).
              of the peers' shards overlapped with the local-shard GEMM) and "kernel" (the
              tcgen05 GEMM's TMA producer reads the peers' shards).  NVLink bytes in:
              (P-1)/P * T * K * 2.
-* gemm_rs  - row GEMM with the reduce-scatter fused into the epilogue (stores into the owners'
-             staging slots) + local sum.  NVLink bytes out: (P-1)/P * T * N * 2.
+* gemm_rs  - row GEMM + reduce-scatter of the partial products: "pull" (other ranks' row blocks
+             first, then copy-engine pulls of the peers' partials overlapped with the own-rows
+             GEMM) and "kernel" (epilogue stores into the owners' staging slots + local sum).
+             NVLink bytes: (P-1)/P * T * N * 2.
 * dp_allreduce - 64 MiB fp32 gradient bucket summed by the peer-memory kernels (two-shot:
              reduce-scatter by P2P loads, all-gather by P2P loads).  NVLink bytes in:
              2 (P-1)/P * n * 4.
@@ -107,9 +109,11 @@ def case_gemm_rs(T=16384, K=4096, N=4096):
     def base():
         gemm.mm(y, w, out=part)
         dist.reduce_scatter_tensor(mine, part)
-    ms = _time(lambda: tp_fused.gemm_rs(y, w, dist.group.WORLD))
     mb = _time(base)
-    _report("gemm_rs", ms, mb, 2.0 * T * N * K, (P - 1) / P * T * N * 2, {"T": T, "K": K, "N": N})
+    for impl in ("pull", "kernel"):
+        ms = _time(lambda: tp_fused.gemm_rs(y, w, dist.group.WORLD, impl=impl))
+        _report("gemm_rs", ms, mb, 2.0 * T * N * K, (P - 1) / P * T * N * 2,
+                {"impl": impl, "T": T, "K": K, "N": N})
 
 
 def case_dp_allreduce(mib=64):
