@@ -253,6 +253,12 @@ class GradReducer:
             C.ep_barrier(pads, me, seg.symm_epoch, _DP_SLOT0)
 
         with torch.cuda.stream(self._side):
+            if _DP_IMPL == "pull":
+                dp_pull_allreduce(h, seg.grad, b.lo, b.hi, barrier, self.__dict__.setdefault("_tmp", {}))
+                done = torch.cuda.Event()
+                done.record(self._side)
+                b.work = _StreamWork(done)
+                return
             barrier()                                   # every rank finished accumulating the bucket
             mc = int(getattr(h, "multicast_ptr", 0) or 0) if _use_nvls() else 0
             if mc:
@@ -284,6 +290,43 @@ class GradReducer:
 
 
 _DP_SLOT0 = 640   # signal-pad words used by the data-parallel barrier (after the EP / TP ones)
+_DP_IMPL = "pull"     # peer-memory all-reduce: "pull" (copy engines) or "kernel" (SM P2P loads)
+
+
+def dp_slice_bounds(lo: int, hi: int, P: int, q: int):
+    """Rank q's slice of bucket [lo, hi): whole 16-byte words, as the native kernels use."""
+    sl = ((hi - lo + P - 1) // P + 3) // 4 * 4
+    s0 = min(hi, lo + q * sl)
+    return s0, min(hi, s0 + sl)
+
+
+def dp_pull_allreduce(h, buf: torch.Tensor, lo: int, hi: int, barrier, tmp: dict) -> None:
+    """Sum buf[lo:hi] over the symmetric-memory group on the current stream with the copy
+    engines: barrier; the owner of each slice pulls the peers' copies of it into local buffers
+    and adds them in place (only the owner computes a slice, so every replica ends with the
+    same bits); barrier; every rank pulls the other owners' reduced slices into its own buffer;
+    barrier.  Each remote float crosses NVLink once per phase."""
+    P, r = h.world_size, h.rank
+    s0, s1 = dp_slice_bounds(lo, hi, P, r)
+    barrier()                                       # every rank finished accumulating the bucket
+    if s1 > s0:
+        n = s1 - s0
+        for i in range(1, P):
+            q = (r + i) % P
+            t = tmp.get(i)
+            if t is None or t.numel() < n:
+                t = torch.empty(n, device=buf.device, dtype=torch.float32)
+                tmp[i] = t
+            t = t[:n]
+            t.copy_(h.get_buffer(q, (n,), torch.float32, s0), non_blocking=True)
+            buf[s0:s1].add_(t)
+    barrier()                                       # every slice reduced by its owner
+    for i in range(1, P):
+        q = (r + i) % P
+        q0, q1 = dp_slice_bounds(lo, hi, P, q)
+        if q1 > q0:
+            buf[q0:q1].copy_(h.get_buffer(q, (q1 - q0,), torch.float32, q0), non_blocking=True)
+    barrier()                                       # every peer done reading this rank's slice
 
 
 def _use_nvls() -> bool:

@@ -18,9 +18,9 @@ baseline).
              first, then copy-engine pulls of the peers' partials overlapped with the own-rows
              GEMM) and "kernel" (epilogue stores into the owners' staging slots + local sum).
              NVLink bytes: (P-1)/P * T * N * 2.
-* dp_allreduce - 64 MiB fp32 gradient bucket summed by the peer-memory kernels (two-shot:
-             reduce-scatter by P2P loads, all-gather by P2P loads).  NVLink bytes in:
-             2 (P-1)/P * n * 4.
+* dp_allreduce - 64 MiB fp32 gradient bucket summed over symmetric memory, two-shot:
+             "kernel" (reduce-scatter and all-gather by SM P2P loads) and "pull" (copy-engine
+             pulls, in-place adds by the slice owner).  NVLink bytes in: 2 (P-1)/P * n * 4.
 * ep_moe   - expert-parallel MoE layer forward + backward (T tokens per rank, top-k routing,
              128 experts sharded over P ranks) with the NVLink peer-memory transport vs NCCL
              all-to-all.  Roofline: expert GEMM FLOPs vs dispatch + combine bytes.
@@ -139,10 +139,15 @@ def case_dp_allreduce(mib=64):
         barrier()
         C.dp_all_gather(h.buffer_ptrs, r, 0, n)
         barrier()
-    ms = _time(fused)
+    from mamformer_b200.optim import dp_pull_allreduce
+    tmp = {}
     mb = _time(lambda: dist.all_reduce(plain))
-    C_err = int(C.comm_error())
-    _report("dp_allreduce", ms, mb, 0.0, 2 * (P - 1) / P * n * 4, {"MiB": mib, "comm_error": C_err})
+    ms = _time(fused)
+    _report("dp_allreduce", ms, mb, 0.0, 2 * (P - 1) / P * n * 4,
+            {"impl": "kernel", "MiB": mib, "comm_error": int(C.comm_error())})
+    ms = _time(lambda: dp_pull_allreduce(h, buf, 0, n, barrier, tmp))
+    _report("dp_allreduce", ms, mb, 0.0, 2 * (P - 1) / P * n * 4,
+            {"impl": "pull", "MiB": mib, "comm_error": int(C.comm_error())})
 
 
 def case_ep_moe(T=8192, d=4096, E=128, k=8, I=576):

@@ -143,6 +143,17 @@ def dp_nvls_worker(rank, world):
     dp_p2p_worker(rank, world, nvls=True)
 
 
+def dp_pull_worker(rank, world):
+    """The SM-load ("kernel") form of the peer-memory gradient all-reduce (the copy-engine
+    "pull" form is the default that dp_p2p_worker exercises)."""
+    import mamformer_b200.optim as O
+    O._DP_IMPL = "kernel"
+    try:
+        dp_p2p_worker(rank, world)
+    finally:
+        O._DP_IMPL = "pull"
+
+
 def tp_fused_worker(rank, world):
     """Fused all-gather->GEMM and GEMM->reduce-scatter (and their autograd) against NCCL + torch."""
     from mamformer_b200.parallel import tp_fused

@@ -57,6 +57,11 @@ def test_data_parallel_p2p_transport_two_gpus():
 
 
 @needs2
+def test_data_parallel_kernel_transport_two_gpus():
+    _spawn("dp_pull_worker", 2)
+
+
+@needs2
 def test_data_parallel_nvls_transport_two_gpus():
     _spawn("dp_nvls_worker", 2)
 
