@@ -1,15 +1,20 @@
-"""Sequence-parallel tensor parallelism with the collectives fused into the GEMMs over NVLink.
+"""Sequence-parallel tensor parallelism with the collectives overlapped with the GEMMs over NVLink.
 
 Activations between TP blocks are sharded by rows (tokens) over the TP group.  A column-parallel
-linear needs the full sequence: its all-gather is fused into the GEMM (mode "gathered-A" of the
-tcgen05 kernel: the TMA producer reads every rank's row shard straight from that rank's
-symmetric-memory buffer - plain TMA loads of peer memory, no multicast - starting with the local
-shard so the remote tiles stream in while local tiles compute).  A row-parallel linear produces
-partial sums that must be reduced onto the owning rank: the reduce-scatter is fused into the GEMM
-epilogue (mode "scattered-D": every tile of shard r is stored straight into rank r's staging
-slot for this rank; each rank starts with the next rank's shard), followed by a local sum of the
-P slots.  A bounded signal-pad barrier (the expert-parallel barrier kernel) orders producers and
-consumers; nothing waits on the host.
+linear needs the full sequence (all-gather -> GEMM); a row-parallel linear produces partial sums
+that must be reduced onto the owning rank (GEMM -> reduce-scatter).  Each has two forms:
+
+* "pull" (default): the copy engines move every remote shard / partial once over NVLink from the
+  peer's symmetric-memory buffer into local memory on a side stream, while the tensor cores
+  multiply local rows; each remote block is multiplied (or summed) as soon as it lands.
+* "kernel": one tcgen05 GEMM does both - mode "gathered-A" (the TMA producer reads every rank's
+  row shard straight from that rank's symmetric buffer, plain TMA loads of peer memory, no
+  multicast, local shard first) and mode "scattered-D" (the epilogue stores each tile of shard r
+  into rank r's staging slot, followed by a local sum of the P slots).  Measured slower on 2
+  B200s: the producer re-reads each remote tile once per output n-tile.
+
+A bounded signal-pad barrier (the expert-parallel barrier kernel) orders producers and consumers;
+nothing waits on the host.
 
 Reference: ``mamformer/parallelism/tensor_parallel.py`` (``_tp_all_gather`` 90-103,
 ``_tp_reduce_scatter`` 105-121 - defined there but unused; ``ColumnParallelLinear`` 136-190,
