@@ -107,3 +107,24 @@ def test_fused_tp_path_selection_cpu():
     w = torch.zeros(32, 64, dtype=torch.bfloat16)
     assert not _fused_ok(x, w, None)
     assert not _fused_ok(x, w, object())          # CPU tensors: never fused
+
+
+def test_dp_slice_bounds_partition():
+    """Each rank's slice of a gradient bucket is whole 16-byte words, the slices tile the bucket
+    exactly, and the Python bounds (copy-engine form) match the native kernels' slicing."""
+    from mamformer_b200.optim import dp_slice_bounds
+    try:
+        import mamformer_b200._C as C
+    except ImportError:
+        C = None
+    for lo, hi in ((0, 4), (64, 64 + 4096), (128, 128 + 1000), (0, 262144)):
+        for P in (2, 3, 4, 8):
+            covered = []
+            for q in range(P):
+                s0, s1 = dp_slice_bounds(lo, hi, P, q)
+                assert s0 % 4 == 0 and lo <= s0 <= s1 <= hi
+                covered.extend(range(s0, s1))
+                if C is not None:
+                    sl = C.dp_slice(lo, hi, P)
+                    assert s0 == min(hi, lo + q * sl)
+            assert covered == list(range(lo, hi))
