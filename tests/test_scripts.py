@@ -50,3 +50,26 @@ def test_train_script_gpu_bf16(tmp_path):
     """The pre-training entry point on one GPU in bf16: native kernels, native optimizer."""
     _run(_train_args(tmp_path, ["--bf16"]))
     assert glob.glob(str(tmp_path / "ck" / "checkpoint_*"))
+
+
+def _torchrun(args, nproc=2, timeout=900):
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return _run(["-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
+                 "--master-addr", "127.0.0.1", f"--master-port={port}"] + args, timeout=timeout,
+                env={"CUDA_VISIBLE_DEVICES": "", "OMP_NUM_THREADS": "1"})
+
+
+@pytest.mark.parametrize("layout", [["--tp", "2"], ["--pp", "2"], ["--dp", "2"]])
+def test_train_distributed_script_cpu(tmp_path, layout):
+    """The 4-D entry point under torchrun with two gloo ranks: runs a few steps and writes its
+    per-rank checkpoint shards."""
+    args = ["scripts/train_distributed.py", "--config", "debug", "--data", str(tmp_path / "nodata"),
+            "--max_seq_len", "64", "--batch_size", "1", "--gradient_accumulation_steps", "2",
+            "--max_steps", "2", "--warmup_steps", "1", "--save_every", "2", "--log_every", "1",
+            "--no_gradient_checkpointing", "--output_dir", str(tmp_path / "ck")] + layout
+    _torchrun(args)
+    assert glob.glob(str(tmp_path / "ck" / "**" / "*.pt"), recursive=True), "no checkpoint written"
