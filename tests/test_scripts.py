@@ -132,3 +132,17 @@ def test_profile_model_script_cpu():
     r = _run(["scripts/profile_model.py", "--config", "configs/ultra-7b.yaml", "--seq_len", "4096",
               "--ep", "8"])
     assert (r.stdout + r.stderr).strip() != ""
+
+
+def test_data_pipeline_and_thinking_generation_cpu(tmp_path):
+    """scripts/data_pipeline.py curates a small corpus; scripts/generate.py runs a thinking mode."""
+    import json
+    src = tmp_path / "raw"
+    src.mkdir()
+    (src / "a.jsonl").write_text("\n".join(json.dumps({"text": f"Document {i}. " + "Some prose here. " * 30})
+                                           for i in range(6)))
+    _run(["scripts/data_pipeline.py", "--input", str(src), "--output", str(tmp_path / "out")])
+    assert any((tmp_path / "out").rglob("*")), "data pipeline wrote nothing"
+    r = _run(["scripts/generate.py", "--config", "debug", "--prompt", "2+2?", "--max_new_tokens", "8",
+              "--thinking", "FastThink", "--temperature", "0"])
+    assert r.stdout.strip() != ""
