@@ -34,7 +34,8 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "train tokens/s per box, ultra-7b MoE bf16 @1/2/4/8 B200, max over ranks"
-BASELINE_TOKS = None  # the reference publishes no ultra-7b throughput ("not yet measured")
+# The reference publishes no throughput for this model or hardware, so vs_baseline stays null.
+BASELINE_TOKS = None
 
 
 def _args():
@@ -56,7 +57,7 @@ def _args():
                          "64 MiB bucket on 2 GPUs; equal step time, the reduction is overlapped)")
     ap.add_argument("--parallel", default="ep", choices=["ep", "dp"],
                     help="N > 1: ep = routed experts sharded over all N GPUs (EP=N x dense DP=N, the "
-                         "BASELINE ultra-7b layout); dp = every GPU holds every expert")
+                         "ultra-7b benchmark layout, EP=8 x DP on 8 GPUs); dp = every GPU holds every expert")
     return ap.parse_args()
 
 
@@ -100,6 +101,17 @@ def _barrier(world):
     torch.cuda.synchronize()
 
 
+def _peak_tflops():
+    """bf16 peak used for MFU: the measured sustained cuBLAS figure of this pool when the
+    measurement file is present, else the same figure recorded earlier."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured sustained cuBLAS bf16"
+    except (OSError, KeyError, ValueError):
+        return 1390.2, "sustained cuBLAS bf16 measured on this pool (file absent)"
+
+
 def _emit(obj, rank):
     if rank == 0:
         print(json.dumps(obj), flush=True)
@@ -133,6 +145,9 @@ def run_ours(args, rank, world):
 
     if not ops.has_native():
         raise RuntimeError("native extension missing: run python setup.py build_ext --inplace")
+    if ops.force_reference():
+        raise RuntimeError("MAMF_FORCE_REFERENCE=1 routes every op to eager PyTorch; bench.py refuses to "
+                           "time that path (unset it)")
     cfg = MamformerConfig.from_dict(bench_config(args.layers))
     per_gpu = args.micro_batch * args.grad_accum
     tcfg = TrainConfig(learning_rate=2e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch,
@@ -193,6 +208,14 @@ def run_ours(args, rank, world):
         launches = ours * args.steps
         all_kernels = total * args.steps
     mem = torch.cuda.max_memory_allocated() / 2 ** 30
+    from mamformer_b200.utils.metrics import matmul_params_per_token
+    n_mm = matmul_params_per_token(model)
+    peak_tf, peak_src = _peak_tflops()
+    mfu = {"value": round(value / world * 6.0 * n_mm / (peak_tf * 1e12), 4),
+           "flops_per_token": 6.0 * n_mm, "matmul_params_per_token": n_mm, "peak_tflops_per_gpu": peak_tf,
+           "peak": peak_src,
+           "counts": "6 x matmul weights active per token (top-k experts, 1 + MTP-depth vocab heads); "
+                     "attention scores, scans and recomputation not counted"}
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -207,7 +230,7 @@ def run_ours(args, rank, world):
                    "params_b": round(sum(p.numel() for p in model.parameters()) / 1e9, 3),
                    "l2": "working set >> L2 (inputs larger than L2)"},
         "clocks": clk, "e2e": e2e, "gpu_launches": launches, "all_kernel_launches": all_kernels,
-        "peak_mem_gib": round(mem, 1),
+        "peak_mem_gib": round(mem, 1), "mfu": mfu,
     }
     _emit(out, rank)
 
@@ -277,11 +300,27 @@ def run_reference(args, rank, world):
         msg = str(exc).split("\n")[0][:160]
         _emit({"impl": "reference", "unavailable": f"CUDA out of memory on a 180 GB B200 at seq {args.seq}, "
                                                    f"micro-batch {args.micro_batch}: {msg}"}, rank)
-    except Exception as exc:   # the reference's own Triton kernel fails to compile on this image
-        name = type(exc).__name__
-        msg = str(exc).strip().split("\n")[-1][:160]
-        _emit({"impl": "reference", "unavailable": f"reference forward fails on its stock GPU path "
-                                                   f"({name}: {msg})"}, rank)
+    except Exception as exc:   # e.g. the reference's own Triton kernel failing to compile
+        import traceback
+        traceback.print_exc(file=sys.stderr)
+        _emit({"impl": "reference", "unavailable": "reference fails on its stock GPU path: "
+                                                   + _exception_summary(exc)}, rank)
+
+
+def _exception_summary(exc: BaseException) -> str:
+    """One line: the exception's module-qualified type, the first and the last non-empty line
+    of its message, and the innermost frame of the reference's own code that raised it."""
+    import traceback
+    lines = [ln.strip() for ln in str(exc).splitlines() if ln.strip()]
+    msg = lines[0] if lines else ""
+    if len(lines) > 1 and lines[-1] != msg:
+        msg += " ... " + lines[-1]
+    where = ""
+    for fr in traceback.extract_tb(exc.__traceback__):
+        if os.sep + "mamformer" + os.sep in fr.filename and "_ref" in fr.filename:
+            where = f" [raised under {os.path.relpath(fr.filename, ROOT)}:{fr.lineno} in {fr.name}]"
+    kind = type(exc)
+    return f"{kind.__module__}.{kind.__qualname__}: {msg[:300]}{where}"
 
 
 def main():

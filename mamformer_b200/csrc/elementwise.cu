@@ -415,6 +415,14 @@ std::vector<at::Tensor> conv_silu_bwd(at::Tensor x, at::Tensor w, at::Tensor dy)
 // partial (count, mean, M2); finalize combines them (Chan) in double; pass 2 normalises.
 constexpr int GN_ROWS = 64;
 
+// Stats / reduce block: x covers the head dimension (rounded up to 8 so that x * 4 threads
+// fill whole warps - block_sum shuffles over all 32 lanes), y = 4 rows.  Threads with
+// x >= hd contribute zeros.
+static inline dim3 gn_block(int64_t hd) {
+  const int64_t x = std::min<int64_t>(128, (hd + 7) / 8 * 8);
+  return dim3((unsigned)x, 4);
+}
+
 template <typename T>
 __global__ void gn_stats_kernel(const T* __restrict__ x, float* __restrict__ part, int S, int H, int hd) {
   const int b = blockIdx.z, h = blockIdx.y, tile = blockIdx.x;
@@ -534,7 +542,7 @@ std::vector<at::Tensor> head_groupnorm_fwd(at::Tensor x, int64_t H, at::Tensor w
   at::Tensor y = at::empty_like(x);
   at::Tensor wc = w.to(at::kFloat).contiguous(), bc = bias.to(at::kFloat).contiguous();
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "gn_fwd", [&] {
-    gn_stats_kernel<scalar_t><<<dim3(tiles, H, B), dim3(std::min(hd, 128), 4), 0, stream()>>>(
+    gn_stats_kernel<scalar_t><<<dim3(tiles, H, B), gn_block(hd), 0, stream()>>>(
         (const scalar_t*)x.data_ptr(), part.data_ptr<float>(), S, H, hd);
     gn_finalize_kernel<<<(B * H + 127) / 128, 128, 0, stream()>>>(part.data_ptr<float>(), mr.data_ptr<float>(),
                                                                   B * H, tiles, (float)eps);
@@ -558,7 +566,7 @@ std::vector<at::Tensor> head_groupnorm_bwd(at::Tensor x, int64_t H, at::Tensor w
   at::Tensor dx = at::empty_like(x);
   at::Tensor wc = w.to(at::kFloat).contiguous();
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "gn_bwd", [&] {
-    gn_bwd_reduce_kernel<scalar_t><<<dim3(tiles, H, B), dim3(std::min(hd, 128), by), 0, stream()>>>(
+    gn_bwd_reduce_kernel<scalar_t><<<dim3(tiles, H, B), gn_block(hd), 0, stream()>>>(
         (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(),
         gpart.data_ptr<float>(), wpart.data_ptr<float>(), S, H, hd);
     at::Tensor gsum = gpart.sum(1).contiguous();
@@ -612,6 +620,15 @@ static int scratch_address(float** out) {
   return 0;
 }
 
+// Drop the cached address of the current device; the next call looks it up again.  Used after
+// a failed launch: if the failure came from a context that was reset, the old address is stale.
+static void forget_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  g_scratch_addr[dev] = nullptr;
+}
+
 }  // namespace noalloc
 }  // namespace mamf
 
@@ -625,7 +642,14 @@ int mamf_head_groupnorm_fwd_noalloc(const void* x, const float* w, const float* 
   using namespace mamf;
   if (!x || !w || !b || !y || B <= 0 || S <= 0 || H <= 0 || hd <= 0 || (dtype != 0 && dtype != 1))
     return noalloc::fail(1, "invalid arguments");
+  // Index types of the kernels: grid y/z hold H and B; S, hd and C = H*hd are int; element
+  // offsets are int64.  Check each factor before any product can overflow.
+  if (B > 65535 || H > 65535) return noalloc::fail(1, "B and H must be <= 65535");
+  if (S > INT32_MAX || hd > INT32_MAX || H * hd > INT32_MAX)
+    return noalloc::fail(1, "S, hd and H*hd must fit in int32");
+  if (B * S > INT64_MAX / (H * hd)) return noalloc::fail(1, "B*S*H*hd overflows int64");
   const int64_t tiles = (S + GN_ROWS - 1) / GN_ROWS;
+  // B*H <= 2^32 and tiles <= 2^25, so this product fits easily in int64.
   const int64_t part_floats = B * H * tiles * 3;
   const int64_t mr_floats = mean_rstd_out ? 0 : 2 * B * H;
   if (part_floats + mr_floats > MAMF_NOALLOC_SCRATCH_FLOATS) {
@@ -634,6 +658,15 @@ int mamf_head_groupnorm_fwd_noalloc(const void* x, const float* w, const float* 
              (long long)(part_floats + mr_floats), MAMF_NOALLOC_SCRATCH_FLOATS);
     return noalloc::fail(2, buf);
   }
+  // A launch error left behind by earlier, unrelated work on this thread is reported as such
+  // (and cleared) instead of being attributed to this call's kernels.
+  const cudaError_t prior = cudaGetLastError();
+  if (prior != cudaSuccess) {
+    char buf[200];
+    snprintf(buf, sizeof(buf), "a CUDA error was pending before this call (nothing launched): %s",
+             cudaGetErrorString(prior));
+    return noalloc::fail(3, buf);
+  }
   float* scratch = nullptr;
   if (int rc = noalloc::scratch_address(&scratch)) return rc;
   float* part = scratch;
@@ -641,7 +674,7 @@ int mamf_head_groupnorm_fwd_noalloc(const void* x, const float* w, const float* 
   cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
   const int Bi = (int)B, Si = (int)S, Hi = (int)H, hdi = (int)hd;
   const int64_t numel = B * S * H * hd;
-  dim3 sgrid((unsigned)tiles, (unsigned)H, (unsigned)B), sblock((unsigned)std::min<int64_t>(hd, 128), 4);
+  dim3 sgrid((unsigned)tiles, (unsigned)H, (unsigned)B), sblock = gn_block(hd);
   if (dtype == 1) {
     gn_stats_kernel<__nv_bfloat16><<<sgrid, sblock, 0, st>>>((const __nv_bfloat16*)x, part, Si, Hi, hdi);
   } else {
@@ -655,6 +688,10 @@ int mamf_head_groupnorm_fwd_noalloc(const void* x, const float* w, const float* 
     gn_apply_kernel<float><<<ew_blocks(numel), 256, 0, st>>>((const float*)x, mr, w, b, (float*)y, B * S, Si, Hi, hdi);
   }
   const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return noalloc::fail(3, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    noalloc::forget_current_device();   // a reset context invalidates the cached address
+    return noalloc::fail(3, cudaGetErrorString(e));
+  }
+  noalloc::g_msg[0] = '\0';
   return 0;
 }

@@ -21,6 +21,11 @@
 //     (different streams, or different host threads without ordering) race on the array; order
 //     them on one stream.
 //   * No cudaMalloc, cudaFree or allocating library routine is called.
+//   * Errors: a launch error that earlier work left pending on the calling thread is reported
+//     as rc 3 with its own message, before anything is launched.  After a failed launch the
+//     cached address of the current device is dropped, so a context that was reset in the
+//     meantime (cudaDeviceReset) gets a fresh lookup on the next call.
+//   * Limits: B and H <= 65535; S, hd and H*hd < 2^31; B*S*H*hd < 2^63 (rc 1 otherwise).
 //
 // Arguments: x and y are (B, S, H*hd) contiguous, dtype 0 = float32, 1 = bfloat16; w and b are
 // (H*hd,) float32; mean_rstd_out is (B*H, 2) float32 or NULL; stream is a cudaStream_t (NULL =

@@ -26,13 +26,19 @@ __all__ = [
     "rms_norm", "rope", "swiglu", "causal_conv1d_silu", "selective_scan", "mamba_inner",
     "linear_diff_attention", "diff_attention", "attention", "head_group_norm", "router_topk",
     "expert_histogram", "moe_routed", "moe_expert_outputs", "linear_cross_entropy",
-    "fused_ce_available", "token_log_probs", "NATIVE", "has_native",
+    "fused_ce_available", "token_log_probs", "NATIVE", "has_native", "force_reference",
 ]
 
 # Native-kernel coverage (op name -> kernel source file).  Filled by ops.native on import.
 NATIVE: dict = {}
 
 _FORCE_REF = os.environ.get("MAMF_FORCE_REFERENCE", "0") == "1"
+
+
+def force_reference() -> bool:
+    """True when MAMF_FORCE_REFERENCE=1 sends every CUDA op to its eager PyTorch form (for A/B
+    debugging only; benchmarks refuse to run in this mode)."""
+    return _FORCE_REF
 
 
 def _native(t: torch.Tensor) -> bool:

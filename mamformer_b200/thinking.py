@@ -1,24 +1,42 @@
-"""Multi-path parallel thinking (reference ``mamformer/thinking.py``).
+"""Multi-path parallel thinking: modes, budgets and the decode-time phase tracker.
 
-N paths branch from the prompt cache (each blind to the others), each ends at
-``<|think_end|>`` or its budget; then a summary phase and an answer phase.  Modes and budgets
-(per path / summary): NoThink 0, FastThink 2 x 128 / 64, CoreThink 3 x 341 / 128,
-DeepThink 5 x 819 / 256.  Control token ids 3..7 (think_start, think_end, answer_start,
-answer_end, summary_start).
+Behaviour follows the reference's thinking mode (``mamformer/thinking.py``: modes 52-104,
+config 107-234, controller 237-454): N reasoning paths branch from the prompt's cache and do
+not see each other; each path stops at ``<|think_end|>`` or at its token budget; then a summary
+of bounded length and an answer follow.  The public surface (mode names and budgets, the
+config fields and ``effective_*`` helpers, the controller's method names, the event strings
+``"end_path"`` / ``"budget_exceeded"`` / ``"end_summary"`` / ``"end_answer"`` and the keys of
+``finalize()``) is kept so that generation code written for either framework drives this one.
+
+The controller is written here as a table-driven state machine over :class:`Phase`: every
+transition is one row of ``_TRANSITIONS`` and an illegal transition raises, so a caller that
+records an answer token before the answer phase starts finds out at once.
+
+Control token ids (from the tokenizer): 3 think_start, 4 think_end, 5 answer_start,
+6 answer_end, 7 summary_start; id 2 (EOS) also ends the answer.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from enum import Enum
-from typing import List, Optional
+from typing import Dict, List, NamedTuple, Optional
 
-_MODE_TABLE = {
-    # mode: (paths, budget per path, summary budget)
-    "NoThink": (0, 0, 0),
-    "FastThink": (2, 128, 64),
-    "CoreThink": (3, 341, 128),
-    "DeepThink": (5, 819, 256),
+EOS_TOKEN_ID = 2
+
+
+class _Budget(NamedTuple):
+    paths: int
+    per_path: int
+    summary: int
+
+
+# (number of paths, tokens per path, summary tokens) per mode
+_BUDGETS: Dict[str, _Budget] = {
+    "NoThink": _Budget(0, 0, 0),
+    "FastThink": _Budget(2, 128, 64),
+    "CoreThink": _Budget(3, 341, 128),
+    "DeepThink": _Budget(5, 819, 256),
 }
 
 
@@ -29,27 +47,40 @@ class ThinkingMode(Enum):
     DeepThink = "DeepThink"
 
     @property
+    def budget(self) -> _Budget:
+        return _BUDGETS[self.value]
+
+    @property
     def num_paths(self) -> int:
-        return _MODE_TABLE[self.value][0]
+        return self.budget.paths
 
     @property
     def default_budget(self) -> int:
-        return _MODE_TABLE[self.value][1]
+        return self.budget.per_path
 
     @property
     def default_summary_budget(self) -> int:
-        return _MODE_TABLE[self.value][2]
+        return self.budget.summary
 
     @classmethod
     def from_string(cls, s: str) -> "ThinkingMode":
-        for m in cls:
-            if m.value.lower() == str(s).lower():
-                return m
-        raise ValueError(f"Unknown thinking mode '{s}'. Available: {[m.value for m in cls]}")
+        by_name = {m.value.lower(): m for m in cls}
+        mode = by_name.get(str(s).lower())
+        if mode is None:
+            raise ValueError(f"Unknown thinking mode '{s}'. Available: {[m.value for m in cls]}")
+        return mode
+
+
+def _override_or(value: int, fallback: int) -> int:
+    """A positive explicit setting wins; 0 means 'use the mode's default'."""
+    return value if value > 0 else fallback
 
 
 @dataclass
 class ThinkingConfig:
+    """Thinking settings.  ``num_paths`` / ``think_budget`` / ``summary_budget`` of 0 select the
+    mode's defaults; ``enabled`` is the master switch."""
+
     mode: ThinkingMode = ThinkingMode.NoThink
     num_paths: int = 0
     think_budget: int = 0
@@ -65,19 +96,19 @@ class ThinkingConfig:
 
     @property
     def effective_num_paths(self) -> int:
-        return self.num_paths if self.num_paths > 0 else self.mode.num_paths
+        return _override_or(self.num_paths, self.mode.num_paths)
 
     @property
     def effective_budget(self) -> int:
-        return self.think_budget if self.think_budget > 0 else self.mode.default_budget
+        return _override_or(self.think_budget, self.mode.default_budget)
 
     @property
     def effective_summary_budget(self) -> int:
-        return self.summary_budget if self.summary_budget > 0 else self.mode.default_summary_budget
+        return _override_or(self.summary_budget, self.mode.default_summary_budget)
 
     @property
     def is_active(self) -> bool:
-        return self.enabled and self.mode != ThinkingMode.NoThink
+        return self.enabled and self.mode is not ThinkingMode.NoThink
 
     @property
     def total_think_budget(self) -> int:
@@ -85,115 +116,161 @@ class ThinkingConfig:
 
     @classmethod
     def disabled(cls) -> "ThinkingConfig":
-        return cls(mode=ThinkingMode.NoThink, enabled=False)
+        return cls()
 
     @classmethod
     def from_preset(cls, mode: str = "NoThink", budget: int = 0, num_paths: int = 0,
                     summary_budget: int = 0, show_thinking: bool = False) -> "ThinkingConfig":
         m = ThinkingMode.from_string(mode)
-        return cls(mode=m, think_budget=budget, num_paths=num_paths, summary_budget=summary_budget,
-                   enabled=m != ThinkingMode.NoThink, show_thinking=show_thinking)
+        return cls(mode=m, num_paths=num_paths, think_budget=budget, summary_budget=summary_budget,
+                   enabled=m is not ThinkingMode.NoThink, show_thinking=show_thinking)
 
     def validate(self) -> None:
+        problems = []
         if self.think_budget < 0:
-            raise ValueError(f"think_budget must be >= 0, got {self.think_budget}")
+            problems.append(f"think_budget must be >= 0, got {self.think_budget}")
         if self.num_paths < 0:
-            raise ValueError(f"num_paths must be >= 0, got {self.num_paths}")
-        if self.enabled and self.mode == ThinkingMode.NoThink:
-            raise ValueError("thinking enabled=True but mode=NoThink")
+            problems.append(f"num_paths must be >= 0, got {self.num_paths}")
+        if self.enabled and self.mode is ThinkingMode.NoThink:
+            problems.append("thinking enabled=True but mode=NoThink")
+        if problems:
+            raise ValueError("; ".join(problems))
 
     def summary(self) -> str:
-        n, b, s = self.effective_num_paths, self.effective_budget, self.effective_summary_budget
-        return (f"ThinkingConfig(mode={self.mode.value}, paths={n}, budget_per_path={b}, "
-                f"total_think={n * b}, summary_budget={s})")
+        paths, per, summ = self.effective_num_paths, self.effective_budget, self.effective_summary_budget
+        return (f"ThinkingConfig(mode={self.mode.value}, paths={paths}, budget_per_path={per}, "
+                f"total_think={paths * per}, summary_budget={summ})")
+
+
+class Phase(Enum):
+    PROMPT = "prompt"
+    PATH = "path"                  # rendered as "path:<index>"
+    BETWEEN_PATHS = "between_paths"
+    PATHS_DONE = "paths_done"
+    SUMMARY = "summary"
+    SUMMARY_DONE = "summary_done"
+    ANSWER = "answer"
+    DONE = "done"
+
+
+# Allowed (from, to) transitions.  start_path may also restart a path from any earlier phase
+# (the batched generator records paths one after another, after all were sampled).
+_TRANSITIONS = {
+    Phase.PROMPT: {Phase.PATH, Phase.SUMMARY, Phase.ANSWER},
+    Phase.PATH: {Phase.PATH, Phase.BETWEEN_PATHS, Phase.PATHS_DONE, Phase.SUMMARY, Phase.ANSWER},
+    Phase.BETWEEN_PATHS: {Phase.PATH, Phase.SUMMARY, Phase.ANSWER},
+    Phase.PATHS_DONE: {Phase.PATH, Phase.SUMMARY, Phase.ANSWER},
+    Phase.SUMMARY: {Phase.SUMMARY_DONE, Phase.ANSWER, Phase.SUMMARY},
+    Phase.SUMMARY_DONE: {Phase.ANSWER, Phase.SUMMARY},
+    Phase.ANSWER: {Phase.DONE, Phase.ANSWER},
+    Phase.DONE: {Phase.ANSWER},
+}
+
+
+@dataclass
+class _Segment:
+    """Tokens of one path or of the summary, with the count against its budget (the path's
+    closing think_end token is kept in ``tokens`` but not counted)."""
+    tokens: List[int] = field(default_factory=list)
+    counted: int = 0
+    hit_budget: bool = False
 
 
 class MultiPathController:
-    """Phase bookkeeping: prompt -> path:i ... -> summary -> answer -> done."""
+    """Tracks one thinking decode: paths, then summary, then answer.
+
+    Drive it with ``start_path(i)`` / ``record_path_token(i, tok)`` for each path,
+    ``start_summary()`` / ``record_summary_token(tok)``, ``start_answer()`` /
+    ``record_answer_token(tok)``; each ``record_*`` call returns ``None`` (keep going) or an
+    event string telling the caller to stop that phase.  ``finalize()`` returns the tokens and
+    counters."""
 
     def __init__(self, config: ThinkingConfig):
         self.config = config
         self.num_paths = config.effective_num_paths
-        self._path_tokens: List[List[int]] = [[] for _ in range(self.num_paths)]
-        self._path_counts: List[int] = [0] * self.num_paths
-        self._path_budget_forced: List[bool] = [False] * self.num_paths
-        self._summary_tokens: List[int] = []
-        self._summary_count = 0
-        self._summary_budget_forced = False
-        self._answer_tokens: List[int] = []
-        self._phase = "prompt"
-        self._current_path = -1
-        self._all_paths_done = False
+        self._paths = [_Segment() for _ in range(self.num_paths)]
+        self._summary = _Segment()
+        self._answer: List[int] = []
+        self._state = Phase.PROMPT
+        self._active_path = -1
+
+    # -- state -------------------------------------------------------------------------------
+    def _go(self, nxt: Phase) -> None:
+        if nxt not in _TRANSITIONS[self._state]:
+            raise RuntimeError(f"thinking controller: cannot go from {self.phase} to {nxt.value}")
+        self._state = nxt
 
     @property
     def phase(self) -> str:
-        return self._phase
+        if self._state is Phase.PATH:
+            return f"path:{self._active_path}"
+        return self._state.value
 
     @property
     def current_path(self) -> int:
-        return self._current_path
+        return self._active_path
 
     @property
     def is_done(self) -> bool:
-        return self._phase == "done"
+        return self._state is Phase.DONE
 
     @property
     def path_done(self) -> bool:
-        return not self._phase.startswith("path:") and self._phase != "prompt"
+        return self._state not in (Phase.PATH, Phase.PROMPT)
 
     @property
     def summary_done(self) -> bool:
-        return self._phase not in ("summary", "prompt")
+        return self._state not in (Phase.SUMMARY, Phase.PROMPT)
 
     @property
     def answer_done(self) -> bool:
-        return self._phase not in ("answer", "prompt")
+        return self._state not in (Phase.ANSWER, Phase.PROMPT)
 
+    # -- transitions --------------------------------------------------------------------------
     def start_path(self, path_idx: int) -> None:
-        if path_idx < self.num_paths:
-            self._phase = f"path:{path_idx}"
-            self._current_path = path_idx
-
-    def _end_current_path(self) -> None:
-        if self._current_path + 1 >= self.num_paths:
-            self._all_paths_done = True
-            self._phase = "paths_done"
-        else:
-            self._phase = "between_paths"
+        if not 0 <= path_idx < self.num_paths:
+            return
+        self._go(Phase.PATH)
+        self._active_path = path_idx
 
     def start_summary(self) -> None:
-        self._phase = "summary"
+        self._go(Phase.SUMMARY)
 
     def start_answer(self) -> None:
-        self._phase = "answer"
+        self._go(Phase.ANSWER)
 
+    # -- token recording ----------------------------------------------------------------------
     def record_path_token(self, path_idx: int, token_id: int) -> Optional[str]:
-        self._path_tokens[path_idx].append(token_id)
+        seg = self._paths[path_idx]
+        seg.tokens.append(token_id)
         if token_id == self.config.think_end_token_id:
-            self._end_current_path()
+            last = path_idx + 1 >= self.num_paths
+            self._go(Phase.PATHS_DONE if last else Phase.BETWEEN_PATHS)
             return "end_path"
-        self._path_counts[path_idx] += 1
-        if self._path_counts[path_idx] >= self.config.effective_budget:
-            self._path_budget_forced[path_idx] = True
+        seg.counted += 1
+        if seg.counted >= self.config.effective_budget:
+            seg.hit_budget = True
             return "budget_exceeded"
         return None
 
     def record_summary_token(self, token_id: int) -> Optional[str]:
-        self._summary_tokens.append(token_id)
-        self._summary_count += 1
-        if self._summary_count >= self.config.effective_summary_budget:
-            self._summary_budget_forced = True
-            self._phase = "summary_done"
-            return "end_summary"
-        return None
+        seg = self._summary
+        seg.tokens.append(token_id)
+        seg.counted += 1
+        if seg.counted < self.config.effective_summary_budget:
+            return None
+        seg.hit_budget = True
+        self._go(Phase.SUMMARY_DONE)
+        return "end_summary"
 
     def record_answer_token(self, token_id: int) -> Optional[str]:
-        if token_id in (self.config.answer_end_token_id, 2):
-            self._phase = "done"
+        if token_id == self.config.answer_end_token_id or token_id == EOS_TOKEN_ID:
+            self._go(Phase.DONE)
             return "end_answer"
-        self._answer_tokens.append(token_id)
+        self._answer.append(token_id)
         return None
 
+    # -- control tokens -----------------------------------------------------------------------
     def get_think_start_token(self) -> int:
         return self.config.think_start_token_id
 
@@ -206,15 +283,23 @@ class MultiPathController:
     def get_answer_start_token(self) -> int:
         return self.config.answer_start_token_id
 
+    # -- results ------------------------------------------------------------------------------
     def finalize(self) -> dict:
-        return {"all_paths": self._path_tokens, "path_counts": self._path_counts,
-                "path_budget_forced": self._path_budget_forced,
-                "summary_tokens": self._summary_tokens, "summary_count": self._summary_count,
-                "summary_budget_forced": self._summary_budget_forced,
-                "answer_tokens": self._answer_tokens, "total_think_tokens": sum(self._path_counts),
-                "phase": self._phase}
+        counts = [s.counted for s in self._paths]
+        return {
+            "all_paths": [list(s.tokens) for s in self._paths],
+            "path_counts": counts,
+            "path_budget_forced": [s.hit_budget for s in self._paths],
+            "summary_tokens": list(self._summary.tokens),
+            "summary_count": self._summary.counted,
+            "summary_budget_forced": self._summary.hit_budget,
+            "answer_tokens": list(self._answer),
+            "total_think_tokens": sum(counts),
+            "phase": self.phase,
+        }
 
     def __repr__(self) -> str:
-        return (f"MultiPathController(phase={self._phase}, paths={self._path_counts}/{self.num_paths}, "
-                f"summary={self._summary_count}/{self.config.effective_summary_budget}, "
-                f"answer={len(self._answer_tokens)})")
+        counts = [s.counted for s in self._paths]
+        return (f"MultiPathController(phase={self.phase}, paths={counts}/{self.num_paths}, "
+                f"summary={self._summary.counted}/{self.config.effective_summary_budget}, "
+                f"answer={len(self._answer)})")

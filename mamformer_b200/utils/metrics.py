@@ -33,6 +33,43 @@ def train_flops_per_token(config, seq_len: int) -> float:
     return 6.0 * n_active + quad
 
 
+def matmul_params_per_token(model) -> int:
+    """Weights that take part in a matmul for one token of a training forward.
+
+    Counts every 2-D projection weight once, the routed experts at top-k of their number (the
+    stacked (E, out, in) tensors, local slice included under expert parallelism), the attention
+    module each KDA-Diff layer actually ran last (``last_choice``; linear when none has run yet)
+    and the tied vocabulary head once per loss head (main + every MTP depth).  Token embedding
+    lookups, depthwise convolutions, norms and the scan are not matmuls and are left out."""
+    from mamformer_b200.models.kda_diff import KDADiffAttention
+    from mamformer_b200.models.moe import DeepSeekMoE
+    skip_ids = set()
+    total = 0
+    for mod in model.modules():
+        if isinstance(mod, KDADiffAttention):
+            unused = mod.full_attn if (mod.last_choice or "linear") == "linear" else mod.linear_attn
+            skip_ids.update(id(p) for p in unused.parameters())
+        elif isinstance(mod, DeepSeekMoE):
+            for name in ("routed_gate_proj", "routed_up_proj", "routed_down_proj"):
+                w = getattr(mod, name)
+                skip_ids.add(id(w))
+                total += w.numel() // max(1, w.shape[0]) * mod.top_k
+    vocab_heads = 1
+    for name, p in model.named_parameters():
+        if id(p) in skip_ids or p.dim() != 2:
+            continue
+        if "embed" in name:
+            continue
+        total += p.numel()
+    mtp = getattr(model, "mtp", None)
+    if mtp is not None and getattr(mtp, "output_heads", None) is None:
+        vocab_heads += int(getattr(mtp, "depth", 0))      # MTP depths reuse the tied embedding
+    emb = getattr(getattr(model, "model", None), "embed_tokens", None)
+    if emb is not None:
+        total += vocab_heads * emb.weight.numel()
+    return total
+
+
 class MetricsLogger:
     def __init__(self, out_dir: Optional[str], rank: int = 0, world: int = 1, flops_per_token: float = 0.0,
                  peak_tflops: Optional[float] = None):

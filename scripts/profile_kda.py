@@ -16,13 +16,25 @@ ABLATIONS = ("full", "no_kda_diff", "no_interleave", "no_mamba")
 
 
 def ablate(cfg, name):
+    """Ablated copies of a config (reference ``scripts/profile_kda.py:49-78``):
+
+    * ``no_kda_diff``: KDA-Diff off, the differential state attention (DSA) takes its place;
+    * ``no_interleave``: interleaving off, every layer runs attention and SSM in fusion;
+    * ``no_mamba``: every layer attention-only (``cross_layer`` with attention in every layer
+      and no fusion layer, so no layer builds an SSM).  The reference's version of this
+      ablation only switches interleaving off and so still runs the SSM everywhere."""
     if name == "no_kda_diff":
         cfg.kda_diff.enabled = False
+        cfg.dsa.enabled = True
     elif name == "no_interleave":
         cfg.interleave.enabled = False
     elif name == "no_mamba":
         cfg.interleave.enabled = True
-        cfg.interleave.pattern = "all_attention" if hasattr(cfg.interleave, "pattern") else cfg.interleave.pattern
+        cfg.interleave.pattern = "cross_layer"
+        cfg.interleave.attn_every_k = 1
+        cfg.interleave.first_layer_attn = True
+        cfg.interleave.fusion_layers = []
+        assert not any(t["has_ssm"] for t in cfg.layer_types()), "no_mamba ablation left an SSM layer"
     return cfg
 
 

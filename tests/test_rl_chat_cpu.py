@@ -185,3 +185,43 @@ def test_grpo_step_cpu():
     m = tr.step(batch)
     assert torch.isfinite(m["loss"]) and tr.global_step == 1
     assert any(not torch.equal(b, p.detach()) for b, p in zip(before, tr.policy.parameters()))
+
+
+def test_thinking_controller_phases_and_events():
+    from mamformer_b200.thinking import MultiPathController, ThinkingConfig, ThinkingMode
+    tc = ThinkingConfig.from_preset("FastThink", budget=3)
+    assert tc.is_active and tc.effective_num_paths == 2 and tc.effective_budget == 3
+    assert tc.effective_summary_budget == ThinkingMode.FastThink.default_summary_budget == 64
+    assert tc.total_think_budget == 6 and "paths=2" in tc.summary()
+    ctl = MultiPathController(tc)
+    assert ctl.phase == "prompt" and not ctl.path_done
+    ctl.start_path(0)
+    assert ctl.phase == "path:0" and not ctl.path_done
+    assert ctl.record_path_token(0, 11) is None
+    assert ctl.record_path_token(0, tc.think_end_token_id) == "end_path"
+    assert ctl.phase == "between_paths" and ctl.path_done
+    ctl.start_path(1)
+    assert [ctl.record_path_token(1, t) for t in (20, 21, 22)] == [None, None, "budget_exceeded"]
+    assert ctl.record_path_token(1, tc.think_end_token_id) == "end_path" and ctl.phase == "paths_done"
+    ctl.start_summary()
+    assert not ctl.summary_done
+    for i in range(63):
+        assert ctl.record_summary_token(100 + i) is None
+    assert ctl.record_summary_token(999) == "end_summary" and ctl.summary_done
+    ctl.start_answer()
+    assert ctl.record_answer_token(7) is None and not ctl.answer_done
+    assert ctl.record_answer_token(2) == "end_answer" and ctl.is_done
+    out = ctl.finalize()
+    assert out["all_paths"] == [[11, 4], [20, 21, 22, 4]]
+    assert out["path_counts"] == [1, 3] and out["path_budget_forced"] == [False, True]
+    assert out["summary_count"] == 64 and out["summary_budget_forced"]
+    assert out["answer_tokens"] == [7] and out["total_think_tokens"] == 4 and out["phase"] == "done"
+    # an answer token before the answer phase is a caller bug
+    bad = MultiPathController(tc)
+    bad.start_path(0)
+    with pytest.raises(RuntimeError):
+        bad.record_answer_token(2)
+    with pytest.raises(ValueError):
+        ThinkingConfig(num_paths=-1).validate()
+    with pytest.raises(ValueError):
+        ThinkingMode.from_string("UltraThink")

@@ -146,3 +146,33 @@ def test_data_pipeline_and_thinking_generation_cpu(tmp_path):
     r = _run(["scripts/generate.py", "--config", "debug", "--prompt", "2+2?", "--max_new_tokens", "8",
               "--thinking", "FastThink", "--temperature", "0"])
     assert r.stdout.strip() != ""
+
+
+def test_profile_kda_ablations_change_the_layer_stack():
+    """scripts/profile_kda.py: each ablation really changes the model (no_mamba leaves no SSM
+    layer, no_kda_diff switches DSA on, no_interleave makes every layer a fusion layer)."""
+    sys.path.insert(0, os.path.join(ROOT, "scripts"))
+    try:
+        import profile_kda
+    finally:
+        sys.path.remove(os.path.join(ROOT, "scripts"))
+    from mamformer_b200.config import MamformerConfig
+    base = lambda: MamformerConfig.from_yaml(os.path.join(ROOT, "configs", "_arch_verify.yaml"))  # noqa: E731
+    assert any(t["has_ssm"] for t in base().layer_types())
+    nm = profile_kda.ablate(base(), "no_mamba")
+    assert all(t["has_attention"] and not t["has_ssm"] for t in nm.layer_types())
+    nk = profile_kda.ablate(base(), "no_kda_diff")
+    assert not nk.kda_diff.enabled and nk.dsa.enabled
+    ni = profile_kda.ablate(base(), "no_interleave")
+    assert ni.layout_string() == "F" * ni.n_layers
+
+
+def test_gen_1b_ultra_config_writes_the_file(tmp_path):
+    out = tmp_path / "_1b_ultra.yaml"
+    _run(["scripts/gen_1b_ultra_config.py", "--out", str(out)])
+    from mamformer_b200.config import MamformerConfig
+    cfg = MamformerConfig.from_yaml(str(out))
+    assert (cfg.d_model, cfg.n_layers, cfg.moe.n_routed_experts, cfg.moe.top_k) == (2048, 24, 32, 4)
+    assert cfg.layout_string().endswith("FF") and cfg.mtp.depth == 2
+    committed = MamformerConfig.from_yaml(os.path.join(ROOT, "configs", "_1b_ultra.yaml"))
+    assert committed.to_dict() == cfg.to_dict()
