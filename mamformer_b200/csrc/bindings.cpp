@@ -42,6 +42,16 @@ void moe_combine_bwd(at::Tensor dout, at::Tensor y, c10::optional<at::Tensor> y_
                      at::Tensor dgate, at::Tensor dy, c10::optional<at::Tensor> dy_idx, int64_t k);
 void ep_pull_runs(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor runs, int64_t max_len);
 void ep_barrier(std::vector<int64_t> signal, int64_t me, int64_t epoch, int64_t slot0);
+std::vector<at::Tensor> moe_sort_plan(at::Tensor idx, int64_t E, bool padded);
+int64_t plan_error();
+void ep_exchange_counts(std::vector<int64_t> mats, std::vector<int64_t> signal, at::Tensor counts, int64_t me,
+                        int64_t epoch, int64_t slot0);
+void ep_layout(at::Tensor C, int64_t me, int64_t cap, at::Tensor plan, at::Tensor status);
+void ep_positions(at::Tensor idx, at::Tensor srow, at::Tensor start, at::Tensor plan, int64_t P, int64_t cap,
+                  at::Tensor pos, at::Tensor owner);
+void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor plan, int64_t P);
+int64_t ep_plan_size(int64_t P, int64_t El);
+void moe_bias_update(at::Tensor counts, double n_assign, int64_t E, double speed, at::Tensor bias, at::Tensor ema);
 int64_t dp_slice(int64_t lo, int64_t hi, int64_t P);
 at::Tensor dp_reduce_scatter(std::vector<int64_t> bufs, int64_t me, int64_t lo, int64_t hi, double scale, bool want_sq);
 void dp_all_gather(std::vector<int64_t> bufs, int64_t me, int64_t lo, int64_t hi);
@@ -91,6 +101,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &mamf::moe_combine_bwd);
   m.def("ep_pull_runs", &mamf::ep_pull_runs);
   m.def("ep_barrier", &mamf::ep_barrier);
+  m.def("moe_sort_plan", &mamf::moe_sort_plan);
+  m.def("plan_error", &mamf::plan_error);
+  m.def("ep_exchange_counts", &mamf::ep_exchange_counts);
+  m.def("ep_layout", &mamf::ep_layout);
+  m.def("ep_positions", &mamf::ep_positions);
+  m.def("ep_pull_rows", &mamf::ep_pull_rows);
+  m.def("ep_plan_size", &mamf::ep_plan_size);
+  m.def("moe_bias_update", &mamf::moe_bias_update);
   m.def("dp_slice", &mamf::dp_slice);
   m.def("dp_reduce_scatter", &mamf::dp_reduce_scatter);
   m.def("dp_all_gather", &mamf::dp_all_gather);

@@ -317,4 +317,381 @@ void comm_clear_error() {
   MAMF_CUDA_CHECK(cudaMemcpyToSymbol(g_mamf_comm_err, &z, sizeof(int)));
 }
 
+
+// =================================================================================================
+// Device-side routing plans (no host round trip)
+//
+//   moe_sort_plan   counting sort of the T*k top-k assignments by expert, stable in assignment
+//                   order: per-warp histograms (shared-memory atomics) -> one block turns them into
+//                   per-warp base offsets -> every warp ranks its assignments again in order with
+//                   __match_any_sync.  Gives srow[q] (position in the expert-sorted order), the
+//                   per-expert counts and exclusive starts, and - for the single-GPU layout - the
+//                   64-aligned segment table, the GEMM tile table and pos[q] in the padded buffer.
+//   ep_exchange     pushes this rank's per-expert counts into row `me` of every peer's count matrix
+//                   (P2P stores into symmetric memory), then runs the bounded signal-pad barrier, so
+//                   each rank holds the full (P, E) matrix locally.
+//   ep_layout       one block: from the count matrix, every owner's 64-aligned segments (so each
+//                   rank knows where its rows land in every owner's buffer), this rank's owner
+//                   tables (segments, GEMM tiles, per-(sender, expert) offsets) and the capacity
+//                   check.  A problem larger than the fixed capacity sets a status word and is
+//                   clamped so that every access stays inside the buffers; the host reads the status
+//                   once per optimizer step and reruns that step with a larger capacity.
+//   ep_pos          pos[q] / owner[q] of every assignment in the owners' buffers (for the combine).
+//   ep_pull_rows    owner side: one warp per destination row of the expert-grouped GEMM operand,
+//                   read with 16-byte loads from the sender's stage over NVLink; pad rows are
+//                   written as zeros (the weight-gradient GEMM contracts over them).
+// =================================================================================================
+constexpr int SORT_WARPS = 8;
+constexpr int SORT_MAXE = 256;
+
+__device__ int g_mamf_plan_err = 0;     // sort saw an expert id < 0 (1) or >= E (2); 0 = none
+
+__global__ void sort_hist_kernel(const int64_t* __restrict__ idx, int64_t Q, int E, int64_t chunk,
+                                 int* __restrict__ hist) {
+  __shared__ int cnt[SORT_WARPS][SORT_MAXE];
+  const int lw = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < SORT_WARPS * SORT_MAXE; i += blockDim.x) (&cnt[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t w = (int64_t)blockIdx.x * SORT_WARPS + lw;
+  const int64_t q0 = w * chunk, q1 = min(Q, q0 + chunk);
+  for (int64_t q = q0 + lane; q < q1; q += 32) {
+    const int64_t e = idx[q];
+    if (e < 0 || e >= E) { atomicCAS(&g_mamf_plan_err, 0, e < 0 ? 1 : 2); continue; }
+    atomicAdd(&cnt[lw][e], 1);
+  }
+  __syncwarp();
+  for (int e = lane; e < E; e += 32) hist[w * E + e] = cnt[lw][e];
+}
+
+// hist (W, E): per-warp counts in, per-warp base offsets out.  counts (E), start (E+1).
+// seg / tile_off (E+1) are written when non-null (single-GPU padded layout, 128-row GEMM tiles).
+__global__ void sort_scan_kernel(int* __restrict__ hist, int W, int E, int* __restrict__ counts,
+                                 int* __restrict__ start, int* __restrict__ seg, int* __restrict__ tile_off) {
+  __shared__ int tot[SORT_MAXE];
+  __shared__ int st[SORT_MAXE + 1];
+  const int e = threadIdx.x;
+  if (e < E) {
+    int run = 0;
+    for (int w = 0; w < W; ++w) {
+      const int c = hist[(int64_t)w * E + e];
+      hist[(int64_t)w * E + e] = run;
+      run += c;
+    }
+    tot[e] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0, sp = 0, sT = 0;
+    for (int i = 0; i < E; ++i) {
+      st[i] = s;
+      start[i] = s;
+      counts[i] = tot[i];
+      if (seg) { seg[i] = sp; tile_off[i] = sT; }
+      const int pad = (tot[i] + 63) / 64 * 64;
+      s += tot[i];
+      sp += pad;
+      sT += (pad + 127) / 128;
+    }
+    st[E] = s;
+    start[E] = s;
+    if (seg) { seg[E] = sp; tile_off[E] = sT; }
+  }
+  __syncthreads();
+  if (e < E) {
+    const int b = st[e];
+    for (int w = 0; w < W; ++w) hist[(int64_t)w * E + e] += b;
+  }
+}
+
+// srow[q]: stable position of assignment q in the expert-sorted order.  pos[q] (optional):
+// seg[e] + rank of q inside expert e (single-GPU padded layout).
+__global__ void sort_rank_kernel(const int64_t* __restrict__ idx, int64_t Q, int E, int64_t chunk,
+                                 const int* __restrict__ base, const int* __restrict__ start,
+                                 const int* __restrict__ seg, int64_t* __restrict__ srow,
+                                 int64_t* __restrict__ pos) {
+  __shared__ int cnt[SORT_WARPS][SORT_MAXE];
+  const int lw = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t w = (int64_t)blockIdx.x * SORT_WARPS + lw;
+  for (int e = lane; e < E; e += 32) cnt[lw][e] = base[w * E + e];
+  __syncwarp();
+  const int64_t q0 = w * chunk, q1 = min(Q, q0 + chunk);
+  for (int64_t b0 = q0; b0 < q1; b0 += 32) {
+    const int64_t q = b0 + lane;
+    int e = q < q1 ? (int)idx[q] : -1;
+    if (e < 0 || e >= E) e = -1 - lane;              // unmatched key: the lane takes no part
+    const unsigned mask = __match_any_sync(0xffffffffu, e);
+    const int r = __popc(mask & ((1u << lane) - 1u));
+    const int b = e >= 0 ? cnt[lw][e] : 0;
+    __syncwarp();
+    if (e >= 0) {
+      const int row = b + r;
+      srow[q] = row;
+      if (pos) pos[q] = (int64_t)seg[e] + (row - start[e]);
+      if (r == 0) cnt[lw][e] = b + __popc(mask);
+    } else if (q < q1) {
+      srow[q] = 0;                                   // bad id (recorded by the histogram pass):
+      if (pos) pos[q] = 0;                           // keep every later access in bounds
+    }
+    __syncwarp();
+  }
+}
+
+// idx (Q,) int64 expert ids -> srow (Q,) int64, counts (E,) int32, start (E+1) int32 and, with
+// `padded`, seg (E+1) int32, tile_off (E+1) int32, pos (Q,) int64.
+std::vector<at::Tensor> moe_sort_plan(at::Tensor idx, int64_t E, bool padded) {
+  c10::cuda::CUDAGuard guard(idx.device());
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kLong, "moe_sort_plan: int64 CUDA expert ids");
+  TORCH_CHECK(E >= 1 && E <= SORT_MAXE, "moe_sort_plan: 1 <= E <= 256");
+  auto ic = idx.contiguous().view({-1});
+  const int64_t Q = ic.numel();
+  auto i32 = idx.options().dtype(at::kInt);
+  const int64_t want_warps = std::max<int64_t>(1, std::min<int64_t>(1024, (Q + 255) / 256));
+  const int64_t blocks = (want_warps + SORT_WARPS - 1) / SORT_WARPS;
+  const int64_t W = blocks * SORT_WARPS;
+  const int64_t chunk = std::max<int64_t>(1, (Q + W - 1) / W);
+  auto hist = at::empty({W, E}, i32);
+  auto counts = at::empty({E}, i32);
+  auto start = at::empty({E + 1}, i32);
+  auto srow = at::empty({Q}, idx.options());
+  at::Tensor seg, tile_off, pos;
+  if (padded) {
+    seg = at::empty({E + 1}, i32);
+    tile_off = at::empty({E + 1}, i32);
+    pos = at::empty({Q}, idx.options());
+  }
+  sort_hist_kernel<<<(unsigned)blocks, SORT_WARPS * 32, 0, stream()>>>(ic.data_ptr<int64_t>(), Q, (int)E, chunk,
+                                                                       hist.data_ptr<int>());
+  MAMF_LAUNCH_CHECK();
+  sort_scan_kernel<<<1, SORT_MAXE, 0, stream()>>>(hist.data_ptr<int>(), (int)W, (int)E, counts.data_ptr<int>(),
+                                                   start.data_ptr<int>(), padded ? seg.data_ptr<int>() : nullptr,
+                                                   padded ? tile_off.data_ptr<int>() : nullptr);
+  MAMF_LAUNCH_CHECK();
+  sort_rank_kernel<<<(unsigned)blocks, SORT_WARPS * 32, 0, stream()>>>(
+      ic.data_ptr<int64_t>(), Q, (int)E, chunk, hist.data_ptr<int>(), start.data_ptr<int>(),
+      padded ? seg.data_ptr<int>() : nullptr, srow.data_ptr<int64_t>(), padded ? pos.data_ptr<int64_t>() : nullptr);
+  MAMF_LAUNCH_CHECK();
+  if (padded) return {srow, counts, start, seg, tile_off, pos};
+  return {srow, counts, start};
+}
+
+int64_t plan_error() {
+  int v = 0;
+  MAMF_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_mamf_plan_err, sizeof(int)));
+  if (v) {
+    int z = 0;
+    MAMF_CUDA_CHECK(cudaMemcpyToSymbol(g_mamf_plan_err, &z, sizeof(int)));
+  }
+  return v;
+}
+
+// ---- expert parallelism: count exchange, layout, positions, row pull -----------------------------
+constexpr int EP_MAXP = MAX_PEERS;
+
+__device__ __forceinline__ void signal_wait_all(PtrTable sig, int me, int P, uint32_t epoch, int slot0) {
+  const int p = threadIdx.x;
+  if (p < P) {
+    uint32_t* remote = static_cast<uint32_t*>(const_cast<void*>(sig.p[p])) + slot0 + me;
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(remote), "r"(epoch) : "memory");
+    const uint32_t* mine = static_cast<const uint32_t*>(sig.p[me]) + slot0 + p;
+    const long long t0 = clock64();
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if (clock64() - t0 > BARRIER_WAIT_CYCLES) { atomicExch(&g_mamf_comm_err, 100 + p); break; }
+      if (*((volatile int*)&g_mamf_comm_err) != 0) break;
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+
+// Push counts into row `me` of every peer's (P, E) matrix, then the barrier.
+__global__ void ep_exchange_kernel(PtrTable mats, PtrTable sig, const int* __restrict__ counts, int me, int P, int E,
+                                   uint32_t epoch, int slot0) {
+  for (int i = threadIdx.x; i < P * E; i += blockDim.x) {
+    const int p = i / E, e = i - p * E;
+    static_cast<int*>(const_cast<void*>(mats.p[p]))[me * E + e] = counts[e];
+  }
+  __syncthreads();
+  signal_wait_all(sig, me, P, epoch, slot0);
+}
+
+void ep_exchange_counts(std::vector<int64_t> mats, std::vector<int64_t> signal, at::Tensor counts, int64_t me,
+                        int64_t epoch, int64_t slot0) {
+  c10::cuda::CUDAGuard guard(counts.device());
+  const int P = (int)mats.size();
+  TORCH_CHECK(P >= 1 && P <= EP_MAXP && (int)signal.size() == P && me >= 0 && me < P, "ep_exchange: 1..8 ranks");
+  TORCH_CHECK(counts.scalar_type() == at::kInt && counts.is_contiguous(), "ep_exchange: int32 counts");
+  PtrTable m{}, sg{};
+  for (int i = 0; i < P; ++i) {
+    m.p[i] = reinterpret_cast<const void*>(mats[i]);
+    sg.p[i] = reinterpret_cast<const void*>(signal[i]);
+  }
+  ep_exchange_kernel<<<1, 256, 0, stream()>>>(m, sg, counts.data_ptr<int>(), (int)me, P, (int)counts.numel(),
+                                              (uint32_t)epoch, (int)slot0);
+  MAMF_LAUNCH_CHECK();
+}
+
+// Plan buffer (int32) of one EP layer, offsets for El local experts, P ranks, E = P * El:
+//   [0, El]            seg   (this rank's 64-aligned expert segments; seg[El] = rows used)
+//   [El+1, 2El+1]      tile  (cumulative 128-row GEMM tiles)
+//   [2El+2, 3El+1]     tot   (rows per local expert, all senders)
+//   next P*El          before[s][le]  rows of senders < s for local expert le
+//   next P*El          src[s][le]     first row of expert me*El+le in sender s's sorted stage
+//   next E             base[e]        where this rank's rows of expert e start in its owner's buffer
+struct PlanOff {
+  int seg, tile, tot, before, src, base, total;
+  __host__ __device__ PlanOff(int P, int El) {
+    seg = 0; tile = El + 1; tot = 2 * El + 2; before = 3 * El + 2; src = before + P * El; base = src + P * El;
+    total = base + P * El;
+  }
+};
+
+// status[0]: 1 if some owner needs more rows than `cap`;  status[1]: max rows any owner needs.
+__global__ void ep_layout_kernel(const int* __restrict__ C, int P, int El, int me, int cap, int* __restrict__ plan,
+                                 int* __restrict__ status) {
+  const int E = P * El;
+  const PlanOff o(P, El);
+  __shared__ int tot[SORT_MAXE];
+  __shared__ int segall[EP_MAXP][SORT_MAXE + 1];
+  const int e = threadIdx.x;
+  if (e < E) {
+    int t = 0;
+    for (int s = 0; s < P; ++s) t += C[s * E + e];
+    tot[e] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < P) {                          // owner r = threadIdx.x: its segments
+    const int r = threadIdx.x;
+    int sp = 0;
+    for (int le = 0; le < El; ++le) { segall[r][le] = sp; sp += (tot[r * El + le] + 63) / 64 * 64; }
+    segall[r][El] = sp;
+    if (sp > cap) atomicExch(status, 1);
+    atomicMax(status + 1, sp);
+  }
+  __syncthreads();
+  if (e < E) {
+    // this rank as a sender: rows of expert e start at owner segment + rows of lower senders
+    const int r = e / El, le = e - r * El;
+    int before_me = 0;
+    for (int s = 0; s < me; ++s) before_me += C[s * E + e];
+    plan[o.base + e] = segall[r][le] + before_me;
+  }
+  if (e < El) {                                   // this rank as owner
+    const int ge = me * El + e;
+    const int t = tot[ge];
+    plan[o.tot + e] = t;
+    int run = 0;
+    for (int s = 0; s < P; ++s) {
+      plan[o.before + s * El + e] = run;
+      run += C[s * E + ge];
+      int sstart = 0;                             // sender s's sorted start of expert ge
+      for (int x = 0; x < ge; ++x) sstart += C[s * E + x];
+      plan[o.src + s * El + e] = sstart;
+    }
+  }
+  if (threadIdx.x == 0) {
+    int tiles = 0;
+    for (int le = 0; le <= El; ++le) {
+      const int sg = min(segall[me][le], cap);   // clamped: an overflowing step is discarded
+      plan[o.seg + le] = sg;
+      plan[o.tile + le] = tiles;
+      if (le < El) tiles += (min(segall[me][le + 1], cap) - sg + 127) / 128;
+    }
+  }
+}
+
+// C (P, E) int32 (this rank's copy after the exchange) -> plan (int32, PlanOff(P, El).total).
+void ep_layout(at::Tensor C, int64_t me, int64_t cap, at::Tensor plan, at::Tensor status) {
+  c10::cuda::CUDAGuard guard(C.device());
+  const int P = (int)C.size(0), E = (int)C.size(1);
+  TORCH_CHECK(P >= 1 && P <= EP_MAXP && E % P == 0 && E <= SORT_MAXE && C.scalar_type() == at::kInt, "ep_layout: C");
+  const int El = E / P;
+  TORCH_CHECK(plan.scalar_type() == at::kInt && plan.numel() >= PlanOff(P, El).total, "ep_layout: plan buffer");
+  TORCH_CHECK(status.scalar_type() == at::kInt && status.numel() >= 2, "ep_layout: status");
+  TORCH_CHECK(cap > 0 && cap < (1LL << 30), "ep_layout: capacity");
+  ep_layout_kernel<<<1, SORT_MAXE, 0, stream()>>>(C.data_ptr<int>(), P, El, (int)me, (int)cap, plan.data_ptr<int>(),
+                                                  status.data_ptr<int>());
+  MAMF_LAUNCH_CHECK();
+}
+
+// pos[q] = base[e] + srow[q] - start[e] (clamped into the owner's capacity), owner[q] = e / El.
+__global__ void ep_pos_kernel(const int64_t* __restrict__ idx, const int64_t* __restrict__ srow,
+                              const int* __restrict__ start, const int* __restrict__ base, int64_t Q, int El, int E,
+                              int cap, int64_t* __restrict__ pos, int32_t* __restrict__ owner) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < Q; q += (int64_t)gridDim.x * blockDim.x) {
+    int64_t e = idx[q];
+    if (e < 0 || e >= E) e = 0;
+    const int64_t p = (int64_t)base[e] + srow[q] - start[e];
+    pos[q] = p < 0 ? 0 : (p >= cap ? (int64_t)cap - 1 : p);
+    owner[q] = (int32_t)(e / El);
+  }
+}
+
+void ep_positions(at::Tensor idx, at::Tensor srow, at::Tensor start, at::Tensor plan, int64_t P, int64_t cap,
+                  at::Tensor pos, at::Tensor owner) {
+  c10::cuda::CUDAGuard guard(idx.device());
+  const int64_t Q = idx.numel();
+  const int E = (int)start.numel() - 1, El = E / (int)P;
+  if (Q == 0) return;
+  TORCH_CHECK(idx.is_contiguous() && srow.numel() == Q && pos.numel() == Q && owner.numel() == Q &&
+              owner.scalar_type() == at::kInt && pos.scalar_type() == at::kLong, "ep_positions: shapes");
+  const PlanOff o((int)P, El);
+  ep_pos_kernel<<<(unsigned)std::min<int64_t>((Q + 255) / 256, 4 * num_sms()), 256, 0, stream()>>>(
+      idx.data_ptr<int64_t>(), srow.data_ptr<int64_t>(), start.data_ptr<int>(), plan.data_ptr<int>() + o.base, Q, El,
+      E, (int)cap, pos.data_ptr<int64_t>(), owner.data_ptr<int32_t>());
+  MAMF_LAUNCH_CHECK();
+}
+
+// Owner pull: dst rows [0, seg[El]) of the expert-grouped operand, one warp per row.
+__global__ void ep_pull_rows_kernel(__nv_bfloat16* __restrict__ dst, int64_t ld_dst, int64_t dst_rows, PtrTable tab,
+                                    int64_t ld_src, const int* __restrict__ plan, int P, int El, int64_t d) {
+  const PlanOff o(P, El);
+  __shared__ int seg[SORT_MAXE + 1], tot[SORT_MAXE], before[SORT_MAXE], src[SORT_MAXE];
+  for (int i = threadIdx.x; i <= El; i += blockDim.x) seg[i] = plan[o.seg + i];
+  for (int i = threadIdx.x; i < El; i += blockDim.x) tot[i] = plan[o.tot + i];
+  for (int i = threadIdx.x; i < P * El; i += blockDim.x) { before[i] = plan[o.before + i]; src[i] = plan[o.src + i]; }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t rows = (int64_t)seg[El] < dst_rows ? (int64_t)seg[El] : dst_rows;
+  const int64_t nv = d / 8;
+  for (int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < rows; i += warps) {
+    int lo = 0, hi = El;
+    while (hi - lo > 1) { const int mid = (lo + hi) >> 1; if (seg[mid] <= i) lo = mid; else hi = mid; }
+    const int le = lo, j = (int)i - seg[le];
+    int4* out = reinterpret_cast<int4*>(dst + i * ld_dst);
+    if (j >= tot[le]) {
+      for (int64_t v = lane; v < nv; v += 32) out[v] = make_int4(0, 0, 0, 0);
+      continue;
+    }
+    int s = 0;
+    while (s + 1 < P && before[(s + 1) * El + le] <= j) ++s;
+    const int64_t row = (int64_t)src[s * El + le] + (j - before[s * El + le]);
+    const int4* in = reinterpret_cast<const int4*>(static_cast<const __nv_bfloat16*>(tab.p[s]) + row * ld_src);
+    for (int64_t v = lane; v < nv; v += 32) out[v] = in[v];
+  }
+}
+
+// dst (>= seg[El] rows, bf16); table: every rank's stage base (row stride ld_src); plan from ep_layout.
+void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor plan, int64_t P) {
+  c10::cuda::CUDAGuard guard(dst.device());
+  const int64_t d = dst.size(1);
+  TORCH_CHECK(dst.scalar_type() == at::kBFloat16 && d % 8 == 0 && (dst.stride(0) * 2) % 16 == 0 && (ld_src * 2) % 16 == 0,
+              "ep_pull_rows: bf16 16-byte aligned rows");
+  TORCH_CHECK((int)table.size() == P && P >= 1 && P <= EP_MAXP, "ep_pull_rows: 1..8 peers");
+  TORCH_CHECK(plan.scalar_type() == at::kInt && plan.is_contiguous(), "ep_pull_rows: int32 plan");
+  PtrTable tab{};
+  for (int i = 0; i < (int)P; ++i) tab.p[i] = reinterpret_cast<const void*>(table[i]);
+  const int el = (int)((plan.numel() - 2) / (3 + 3 * P));      // total = 3*El + 2 + 3*P*El
+  TORCH_CHECK(el >= 1 && PlanOff((int)P, el).total == plan.numel(), "ep_pull_rows: plan size");
+  ep_pull_rows_kernel<<<4 * num_sms(), 256, 0, stream()>>>((__nv_bfloat16*)dst.data_ptr(), dst.stride(0), dst.size(0),
+                                                           tab, ld_src, plan.data_ptr<int>(), (int)P, el, d);
+  MAMF_LAUNCH_CHECK();
+}
+
+int64_t ep_plan_size(int64_t P, int64_t El) { return PlanOff((int)P, (int)El).total; }
+
 }  // namespace mamf

@@ -132,4 +132,31 @@ at::Tensor expert_histogram(at::Tensor idx, int64_t E) {
   return counts.to(at::kLong);
 }
 
+
+// ---- aux-loss-free expert-bias update ---------------------------------------------------------
+// Reference moe.py:335-347 (and the DeepSeekMoE forward):  load = counts / (tokens * k + 1e-8),
+// bias -= speed * sign(load - 1/E),  ema = 0.99 * ema + 0.01 * load.  Each product and sum is
+// rounded separately (no FMA contraction) so the result matches the eager float32 ops bit for bit.
+__global__ void bias_update_kernel(const int64_t* __restrict__ counts, int E, float denom, float inv_e, float speed,
+                                   float* __restrict__ bias, float* __restrict__ ema) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= E) return;
+  const float load = __fdiv_rn((float)counts[e], denom);
+  const float dlt = __fsub_rn(load, inv_e);
+  const float sg = dlt > 0.f ? 1.f : (dlt < 0.f ? -1.f : 0.f);
+  bias[e] = __fsub_rn(bias[e], __fmul_rn(speed, sg));
+  ema[e] = __fadd_rn(__fmul_rn(ema[e], 0.99f), __fmul_rn(0.01f, load));
+}
+
+void moe_bias_update(at::Tensor counts, double n_assign, int64_t E, double speed, at::Tensor bias, at::Tensor ema) {
+  c10::cuda::CUDAGuard guard(counts.device());
+  TORCH_CHECK(counts.scalar_type() == at::kLong && counts.numel() == E && counts.is_contiguous(), "bias_update: counts");
+  TORCH_CHECK(bias.scalar_type() == at::kFloat && ema.scalar_type() == at::kFloat && bias.numel() == E &&
+              ema.numel() == E && bias.is_contiguous() && ema.is_contiguous(), "bias_update: fp32 bias / ema");
+  bias_update_kernel<<<(unsigned)((E + 127) / 128), 128, 0, stream()>>>(
+      counts.data_ptr<int64_t>(), (int)E, (float)(n_assign + 1e-8), (float)(1.0 / (double)E), (float)speed,
+      bias.data_ptr<float>(), ema.data_ptr<float>());
+  MAMF_LAUNCH_CHECK();
+}
+
 }  // namespace mamf

@@ -89,16 +89,27 @@ class Trainer:
                 labels = labels.to(self.device, non_blocking=True)
         labels = input_ids if labels is None else labels
         n_micro = max(1, input_ids.shape[0] // cfg.micro_batch)
+        eng = getattr(self.model, "_mamf_ep_engine", None)
         self.optimizer.zero_grad()
         self._loss_acc.zero_()
+        if eng is not None:
+            eng.begin_step(self.model)
         for i in range(n_micro):
             sl = slice(i * cfg.micro_batch, (i + 1) * cfg.micro_batch)
             out = self.model(input_ids[sl], labels=labels[sl])
             loss = out["loss"]
             if i == n_micro - 1:
+                if eng is not None:
+                    eng.record_status()           # expert-parallel capacity check of this step
                 self.optimizer.reducer.arm()      # overlap the gradient all-reduce with this backward
             (loss / n_micro).backward()
             self._loss_acc += loss.detach().float() / n_micro
+        if eng is not None and eng.step_overflowed():
+            # some expert owner needed more rows than its fixed capacity: discard and rerun the
+            # step with the larger capacity the engine has just set (identically on every rank)
+            self.optimizer.reduce_gradients()
+            self.optimizer.zero_grad()
+            return self.train_step(input_ids, labels, sync_loss=sync_loss, check_grads=check_grads)
         loss_val = None
         if sync_loss:
             self.optimizer.reduce_gradients()

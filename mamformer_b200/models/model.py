@@ -28,6 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint as activation_checkpoint
 
+from mamformer_b200.utils.nvtx import rng as nvtx_rng
 from mamformer_b200 import ops
 from mamformer_b200.config import MamformerConfig
 from mamformer_b200.generation import GenerationMixin
@@ -183,14 +184,15 @@ class MamformerModel(nn.Module):
                 kw["ssm_h_states"] = pending
             if rope_offset:
                 kw["rope_offset"] = rope_offset
-            if (self.gradient_checkpointing and self.training and layer.has_attention
-                    and _is_full_attention_checkpointable(layer)):
-                def run(hs, am, _layer=layer, _kw=kw):
-                    return _layer(hs, attention_mask=am, use_cache=False, cache=None, **_kw)[0]
-                h = activation_checkpoint(run, h, attention_mask, use_reentrant=False)
-                entry = None
-            else:
-                h, entry = layer(h, attention_mask=attention_mask, use_cache=use_cache, cache=lc, **kw)
+            with nvtx_rng(f"layer{idx}"):
+                if (self.gradient_checkpointing and self.training and layer.has_attention
+                        and _is_full_attention_checkpointable(layer)):
+                    def run(hs, am, _layer=layer, _kw=kw):
+                        return _layer(hs, attention_mask=am, use_cache=False, cache=None, **_kw)[0]
+                    h = activation_checkpoint(run, h, attention_mask, use_reentrant=False)
+                    entry = None
+                else:
+                    h, entry = layer(h, attention_mask=attention_mask, use_cache=use_cache, cache=lc, **kw)
             if not layer.has_attention and layer.has_ssm and entry is not None and "ssm_h_states" in entry:
                 pending = entry["ssm_h_states"]
             if attn_only and kw.get("ssm_h_states") is not None:

@@ -285,6 +285,16 @@ class DeepSeekMoE(nn.Module):
 
 def _update_expert_bias(counts: torch.Tensor, n_tokens: int, n_experts: int, top_k: int,
                         speed: float, expert_bias: torch.Tensor, load_ema: torch.Tensor) -> None:
+    """bias -= speed * sign(load - 1/E), load EMA; one native kernel on CUDA (bitwise equal to
+    the eager float32 ops below, which are the CPU path)."""
+    if counts.is_cuda and expert_bias.dtype == torch.float32 and load_ema.dtype == torch.float32 \
+            and expert_bias.is_contiguous() and load_ema.is_contiguous():
+        from mamformer_b200.ops._ext import ext
+        C = ext()
+        if C is not None and not ops.force_reference():
+            C.moe_bias_update(counts.long().contiguous(), float(n_tokens * top_k), n_experts, float(speed),
+                              expert_bias, load_ema)
+            return
     with torch.no_grad():
         load = counts.float() / (n_tokens * top_k + 1e-8)
         expert_bias -= speed * torch.sign(load - 1.0 / n_experts)

@@ -33,22 +33,33 @@ def plan(idx: torch.Tensor, n_experts: int):
     """Counting-sort plan for the (T, k) expert indices.
 
     Returns (pos (T*k,) int64 row of each assignment in the permuted buffer, seg (E+1,) int32,
-    tile_off (E+1,) int32, counts (E,) int64, rows (int, upper bound of the buffer size))."""
+    tile_off (E+1,) int32, counts (E,) int32/int64, rows (int, upper bound of the buffer size)).
+    On CUDA one native counting sort (``csrc/moe_rows.cu`` ``moe_sort_plan``) builds the plan on
+    the device; the eager form below is the CPU path and the oracle of its test."""
     flat = idx.reshape(-1).long()
+    rows = (flat.numel() + ALIGN * n_experts + ALIGN - 1) // ALIGN * ALIGN
+    if flat.is_cuda and n_experts <= 256:
+        from mamformer_b200.ops._ext import require_native
+        srow, counts, start, seg, tile_off, pos = require_native().moe_sort_plan(flat, n_experts, True)
+        return pos, seg, tile_off, counts, rows
+    return plan_eager(flat, n_experts) + (rows,)
+
+
+def plan_eager(flat: torch.Tensor, n_experts: int):
+    """Eager counting sort: (pos, seg int32, tile_off int32, counts int64)."""
     counts = torch.bincount(flat, minlength=n_experts)
     padded = (counts + ALIGN - 1) // ALIGN * ALIGN
-    seg = torch.zeros(n_experts + 1, dtype=torch.int64, device=idx.device)
+    seg = torch.zeros(n_experts + 1, dtype=torch.int64, device=flat.device)
     seg[1:] = torch.cumsum(padded, 0)
-    start = torch.zeros(n_experts, dtype=torch.int64, device=idx.device)
+    start = torch.zeros(n_experts, dtype=torch.int64, device=flat.device)
     start[1:] = torch.cumsum(counts, 0)[:-1]
     order = torch.sort(flat, stable=True).indices
     sorted_e = flat[order]
-    rank = torch.arange(flat.numel(), device=idx.device) - start[sorted_e]
+    rank = torch.arange(flat.numel(), device=flat.device) - start[sorted_e]
     pos = torch.empty_like(flat)
     pos[order] = seg[sorted_e] + rank
     seg32 = seg.to(torch.int32)
-    rows = (flat.numel() + ALIGN * n_experts + ALIGN - 1) // ALIGN * ALIGN
-    return pos, seg32, gemm.tile_offsets(seg32), counts, rows
+    return pos, seg32, gemm.tile_offsets(seg32), counts
 
 
 def _grad_sink(w: torch.Tensor):

@@ -227,10 +227,12 @@ class GradReducer:
         self._launch_ready()
 
     def _launch(self, b: _Bucket) -> None:
-        if b.seg.symm is not None:
-            self._launch_p2p(b)
-        else:
-            b.work = dist.all_reduce(b.seg.grad[b.lo:b.hi], group=b.group, async_op=True)
+        from mamformer_b200.utils.nvtx import rng
+        with rng(f"dp.bucket[{b.lo}:{b.hi}]"):
+            if b.seg.symm is not None:
+                self._launch_p2p(b)
+            else:
+                b.work = dist.all_reduce(b.seg.grad[b.lo:b.hi], group=b.group, async_op=True)
 
     def _launch_p2p(self, b: _Bucket) -> None:
         """Sum the bucket over the group with the NVLink kernels on a side stream: bounded barrier,

@@ -9,18 +9,18 @@ implemented) and its ``EPMoE`` sends every top-k slot through its own padded all
 slots of all tokens at once.  Two transports:
 
 * ``"p2p"`` (CUDA, EP group inside one NVSwitch domain): symmetric-memory stages and the kernels
-  of ``csrc/moe_rows.cu``.  Per layer and direction the sender writes its rows once, already
-  sorted by expert, into its own stage; after a signal-pad barrier each owner pulls its runs
-  straight into its 64-aligned, expert-grouped GEMM operand (no all-to-all buffer, no local
-  re-permutation), the down-projection GEMM writes its output into the owner's stage, and each
+  of ``csrc/moe_rows.cu``, planned entirely on the device.  Per layer the sender sorts its
+  top-k assignments by expert (native counting sort) and writes its rows once, sorted, into its
+  own stage; it pushes its per-expert counts into every peer's count matrix with P2P stores,
+  and that exchange doubles as the barrier that publishes the stage.  Every rank then lays out
+  every owner's 64-aligned expert segments from the same matrix, so it knows where each of its
+  rows lands; each owner pulls its rows straight into its expert-grouped GEMM operand (one warp
+  per row, pad rows zeroed), the down-projection GEMM writes into the owner's stage, and each
   sender's combine kernel reads its k rows per token from the owners over NVLink and sums them
-  with the gates in fp32.  The backward is the mirror image (gate-scaled gradient rows pulled
-  by the owners, fp32 input-gradient rows gathered and summed by the senders).
+  with the gates in fp32.  The backward is the mirror image.  The owners' buffers have a fixed
+  capacity, so the host never waits inside the forward or backward; see :class:`EPEngine`.
 * ``"nccl"`` (any device, also gloo on CPU): one variable-size ``all_to_all_single`` per
   direction (autograd-aware), then the same grouped expert computation.
-
-The per-expert token counts are exchanged once per layer with one small collective and read on
-the host (the sizes of the owner's buffers depend on them).
 
 Gradient bookkeeping: routed-expert weights are tagged ``_mamf_expert``; the optimizer reduces
 them over the ``expert_dp`` group (replicas of the same shard) instead of ``dense_dp``.
@@ -28,10 +28,10 @@ them over the ``expert_dp`` group (replicas of the same shard) instead of ``dens
 
 from __future__ import annotations
 
+import math
 import os
 from typing import List, Optional, Tuple
 
-import numpy as np
 import torch
 import torch.distributed as dist
 import torch.nn as nn
@@ -128,49 +128,72 @@ def expert_combine(expert_outputs: torch.Tensor, sort_order: torch.Tensor, token
 
 # ---------------------------------------------------------------------------------------------
 class _SymStage:
-    """Symmetric-memory stages of one EP group (grown collectively, never shrunk)."""
+    """Symmetric-memory buffers of one EP group (grown collectively, never shrunk):
 
-    def __init__(self, group, device, d):
-        self.group = group
-        self.device = device
-        self.d = d
-        self.rows_x = 0
-        self.rows_y = 0
+    * ``x``  (Q rows, bf16): this rank's token rows sorted by expert (forward), or its
+      gate-scaled output-gradient rows (backward); owners pull from it;
+    * ``y``  (capacity rows, bf16): expert outputs of this rank's experts; senders gather from it;
+    * ``dx`` (capacity rows, fp32): input-gradient rows of this rank's experts;
+    * ``cnt`` (P, E) int32: row s holds sender s's per-expert counts (pushed by s)."""
+
+    def __init__(self, group, device, d, P, E):
+        self.group, self.device, self.d, self.P, self.E = group, device, d, P, E
+        self.rows_x = self.rows_y = 0
         self.x = self.y = self.dx = None
         self.hx = self.hy = self.hdx = None
+        self.cnt, self.hcnt = self._alloc((P, E), torch.int32)
 
-    def _alloc(self, rows, dtype):
+    def _alloc(self, shape, dtype):
         import torch.distributed._symmetric_memory as symm
-        t = symm.empty((max(rows, 1), self.d), dtype=dtype, device=self.device)
+        t = symm.empty(shape, dtype=dtype, device=self.device)
         return t, symm.rendezvous(t, self.group)
 
     def ensure(self, rows_x: int, rows_y: int) -> None:
-        """Every rank calls this with the same sizes (derived from the all-gathered counts)."""
+        """Collective: every rank calls this with the same sizes (fixed by T*k and the capacity,
+        never by the routing), so it only allocates on first use or after a capacity increase."""
         if rows_x <= self.rows_x and rows_y <= self.rows_y:
             return
         torch.cuda.current_stream(self.device).synchronize()   # old stages may still be read
         if rows_x > self.rows_x:
-            self.rows_x = (rows_x * 5 // 4 + ALIGN - 1) // ALIGN * ALIGN
-            self.x, self.hx = self._alloc(self.rows_x, torch.bfloat16)
+            self.rows_x = rows_x
+            self.x, self.hx = self._alloc((rows_x, self.d), torch.bfloat16)
         if rows_y > self.rows_y:
-            self.rows_y = (rows_y * 5 // 4 + ALIGN - 1) // ALIGN * ALIGN
-            self.y, self.hy = self._alloc(self.rows_y, torch.bfloat16)
-            self.dx, self.hdx = self._alloc(self.rows_y, torch.float32)
+            self.rows_y = rows_y
+            self.y, self.hy = self._alloc((rows_y, self.d), torch.bfloat16)
+            self.dx, self.hdx = self._alloc((rows_y, self.d), torch.float32)
 
 
 class EPEngine:
-    """Installed as ``DeepSeekMoE.ep_engine`` by :func:`shard_experts_ep`."""
+    """Installed as ``DeepSeekMoE.ep_engine`` by :func:`shard_experts_ep`.
+
+    Peer-memory transport without host round trips: the routing plan (counting sort, count
+    exchange, owner layout) is built on the device.  Each owner's expert-grouped buffers have a
+    fixed capacity of ``min(P, capacity_factor) * T * k + 64 * E/P`` rows (T tokens per rank);
+    a step whose routing needs more rows at some owner sets a device status word, is discarded
+    by :meth:`step_overflowed` (read once per optimizer step, while the GPU still runs the last
+    backward) and is rerun by the trainer with a larger capacity.  With ``capacity_factor >= P``
+    no step can overflow and nothing is checked."""
 
     def __init__(self, ep_group: ExpertParallelGroup, dense_dp_group=None, dp_factor: Optional[int] = None,
-                 backend: str = "auto"):
+                 backend: str = "auto", capacity_factor: Optional[float] = None):
         self.ep = ep_group
         self.dense_dp_group = dense_dp_group if dense_dp_group is not None else ep_group.group
         if dp_factor is None:
             dp_factor = dist.get_world_size(self.dense_dp_group) if self.dense_dp_group is not None else ep_group.ep_size
         self.dp_factor = int(dp_factor)
         self.backend = os.environ.get("MAMF_EP_BACKEND", backend)
+        if capacity_factor is None:
+            capacity_factor = float(os.environ.get("MAMF_EP_CAPACITY", "2.0"))
+        self.capacity_factor = float(capacity_factor)
         self._stage = None
         self._epoch = 0
+        self.status = None            # device int32 [overflow flag, max rows any owner needed]
+        self._status_host = None
+        self._status_event = None
+        self._snapshot = None
+        self.overflow_steps = 0
+        from mamformer_b200.utils.nvtx import PhaseTimer
+        self.timer = PhaseTimer(os.environ.get("MAMF_EP_PROFILE", "0") == "1")
 
     # -- helpers used by DeepSeekMoE ------------------------------------------------------------
     def global_counts(self, counts: torch.Tensor) -> torch.Tensor:
@@ -191,7 +214,7 @@ class EPEngine:
 
     def routed(self, m, xf: torch.Tensor, idx: torch.Tensor, gates: torch.Tensor) -> torch.Tensor:
         from mamformer_b200.ops import moe as moe_ops
-        if self._use_p2p(xf) and moe_ops.supported(xf, m.routed_gate_proj):
+        if self._use_p2p(xf) and moe_ops.supported(xf, m.routed_gate_proj) and m.n_routed_experts <= 256:
             return _P2PRouted.apply(xf.contiguous(), gates, idx, m.routed_gate_proj, m.routed_up_proj,
                                     m.routed_down_proj, self, m)
         y = self._exchange_nccl(m, xf, idx)
@@ -210,6 +233,61 @@ class EPEngine:
             if err:
                 C.comm_clear_error()
                 raise RuntimeError(f"expert-parallel barrier timed out waiting for EP rank {err - 100}")
+            bad = int(C.plan_error())
+            if bad:
+                raise RuntimeError("routing plan saw an expert id outside [0, E)")
+
+    # -- capacity and the once-per-step overflow check ------------------------------------------
+    def capacity(self, q_rows: int, n_local: int) -> int:
+        f = min(float(self.ep.ep_size), self.capacity_factor)
+        rows = int(math.ceil(f * q_rows)) + ALIGN * n_local
+        return (rows + 127) // 128 * 128
+
+    @property
+    def can_overflow(self) -> bool:
+        return self.capacity_factor < self.ep.ep_size
+
+    def _ensure_status(self, device) -> None:
+        if self.status is None:
+            self.status = torch.zeros(2, dtype=torch.int32, device=device)
+            self._status_host = torch.zeros(2, dtype=torch.int32).pin_memory()
+            self._status_event = torch.cuda.Event()
+
+    def begin_step(self, model: nn.Module) -> None:
+        """Start of an optimizer step: clear the status word and keep a copy of the MoE routing
+        state (biases, load EMA, counters) so that a discarded step leaves no trace."""
+        dev = next(model.parameters()).device
+        if not self.can_overflow or dev.type != "cuda":
+            return
+        self._ensure_status(dev)
+        self.status.zero_()
+        self._snapshot = [(b, b.detach().clone()) for mod in _moe_modules(model) for b in mod.buffers()]
+
+    def record_status(self) -> None:
+        """After the step's last forward: make the status identical on every data-parallel
+        replica and start its copy to the host (read by :meth:`step_overflowed`)."""
+        if not self.can_overflow or self.status is None:
+            return
+        if self.dense_dp_group is not None and dist.get_world_size(self.dense_dp_group) > self.ep.ep_size:
+            dist.all_reduce(self.status, op=dist.ReduceOp.MAX, group=self.dense_dp_group)
+        self._status_host.copy_(self.status, non_blocking=True)
+        self._status_event.record()
+
+    def step_overflowed(self) -> bool:
+        """True when some owner needed more rows than the capacity in this step.  Then the
+        routing state is restored and the capacity raised; the caller reruns the step."""
+        if not self.can_overflow or self._status_event is None:
+            return False
+        self._status_event.synchronize()
+        if int(self._status_host[0]) == 0:
+            return False
+        need = int(self._status_host[1])
+        self.overflow_steps += 1
+        for buf, saved in self._snapshot or []:
+            buf.copy_(saved)
+        q_rows = max(1, self._stage.rows_x if self._stage is not None else 1)
+        self.capacity_factor = max(self.capacity_factor * 1.5, 1.25 * need / q_rows)
+        return True
 
     # -- nccl / gloo transport -----------------------------------------------------------------
     def _exchange_nccl(self, m, xf, idx):
@@ -236,89 +314,76 @@ class EPEngine:
     # -- p2p transport ---------------------------------------------------------------------------
     def barrier(self, C) -> None:
         self._epoch += 1
-        C.ep_barrier(self._stage.hx.signal_pad_ptrs, self.ep.ep_rank, self._epoch, _SIGNAL_SLOT0)
+        C.ep_barrier(self._stage.hcnt.signal_pad_ptrs, self.ep.ep_rank, self._epoch, _SIGNAL_SLOT0)
 
-    def plan_p2p(self, m, idx: torch.Tensor, d: int):
-        """Exchange per-expert counts (one all-gather + one host read) and derive: this rank's
-        slot positions in the owners' grouped buffers, its pull runs as an owner, its segment
-        table, and the stage sizes (identical on every rank)."""
+    def plan_device(self, m, x: torch.Tensor, idx: torch.Tensor):
+        """Routing plan on the device (no host synchronisation): sort this rank's assignments
+        by expert and write its rows, sorted, into its stage; exchange the counts through peer
+        memory (the exchange is also the barrier that publishes the stage); lay out every
+        owner's buffer; locate each assignment's row in its owner's buffer."""
+        from mamformer_b200.ops.native import _C as C
+        T, d = x.shape
+        k = idx.shape[1]
+        Q = T * k
         E, El, P, me = m.n_routed_experts, m.n_local_experts, self.ep.ep_size, self.ep.ep_rank
-        dev = idx.device
-        flat = idx.reshape(-1).long()
-        Q = flat.numel()
-        order = torch.argsort(flat, stable=True)
-        send_e = torch.bincount(flat, minlength=E)
-        allc = torch.empty(P, E, dtype=send_e.dtype, device=dev)
-        dist.all_gather_into_tensor(allc, send_e, group=self.ep.group)
-        Ch = allc.cpu().numpy().astype(np.int64)                      # (P, E)
-        tot = Ch.sum(0)                                                # per expert, all sources
-        loc = tot.reshape(P, El)
-        pad = (loc + ALIGN - 1) // ALIGN * ALIGN
-        seg_all = np.zeros((P, El + 1), np.int64)
-        seg_all[:, 1:] = np.cumsum(pad, 1)                             # owner r's segments
-        src_start = np.zeros((P, E), np.int64)
-        src_start[:, 1:] = np.cumsum(Ch, 1)[:, :-1]                    # sorted position per source
-        before = np.cumsum(Ch, 0) - Ch                                 # rows of sources s' < s
-        owner_e = np.arange(E) // El
-        base = seg_all[owner_e, np.arange(E) % El] + before[me]
-        runs = []
-        for le in range(El):
-            e = me * El + le
-            for s in range(P):
-                n = int(Ch[s, e])
-                if n:
-                    runs.append((int(seg_all[me, le] + before[s, e]), s, int(src_start[s, e]), n))
-        rows_me = int(seg_all[me, -1])
-        rows_y = int(seg_all[:, -1].max())
-        rows_x = int(Ch.sum(1).max())
-        tabs = torch.from_numpy(np.stack([base, src_start[me]])).to(dev)
-        e_sorted = flat[order]
-        q = torch.arange(Q, device=dev)
-        pos_sorted = tabs[0][e_sorted] + q - tabs[1][e_sorted]
-        pos = torch.empty_like(pos_sorted)
-        pos[order] = pos_sorted
-        inv = torch.empty_like(order)
-        inv[order] = q
-        owner = (flat // El).to(torch.int32)
-        seg = torch.from_numpy(seg_all[me]).to(dev, torch.int32)
-        runs_t = torch.tensor(runs if runs else [[0, 0, 0, 0]], dtype=torch.long, device=dev)
-        max_len = max((r[3] for r in runs), default=0)
+        dev = x.device
+        flat = idx.reshape(-1).long().contiguous()
+        srow, counts, start = C.moe_sort_plan(flat, E, False)
+        cap = self.capacity(Q, El)
         if self._stage is None:
-            self._stage = _SymStage(self.ep.group, dev, d)
-        self._stage.ensure(max(rows_x, Q), rows_y)
-        return dict(pos=pos, inv=inv, owner=owner, seg=seg, runs=runs_t, n_runs=len(runs), max_len=max_len,
-                    rows=rows_me)
+            self._stage = _SymStage(self.ep.group, dev, d, P, E)
+        st = self._stage
+        st.ensure(Q, cap)
+        self._ensure_status(dev)
+        C.moe_scatter_rows(st.x, srow, x, k)
+        self._epoch += 1
+        C.ep_exchange_counts(st.hcnt.buffer_ptrs, st.hcnt.signal_pad_ptrs, counts, me, self._epoch, _SIGNAL_SLOT0)
+        plan = torch.empty(C.ep_plan_size(P, El), dtype=torch.int32, device=dev)
+        C.ep_layout(st.cnt, me, cap, plan, self.status)
+        pos = torch.empty(Q, dtype=torch.int64, device=dev)
+        owner = torch.empty(Q, dtype=torch.int32, device=dev)
+        C.ep_positions(flat, srow, start, plan, P, cap, pos, owner)
+        return dict(srow=srow, plan=plan, seg=plan[: El + 1], tile_off=plan[El + 1: 2 * El + 2], pos=pos,
+                    owner=owner, cap=cap)
 
 
 class _P2PRouted(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, gates, idx, w_gate, w_up, w_down, eng: EPEngine, m):
-        from mamformer_b200.ops import gemm, moe as moe_ops
+        from mamformer_b200.ops import moe as moe_ops
         from mamformer_b200.ops.native import _C
+        from mamformer_b200.utils.nvtx import rng
         T, d = x.shape
         k = idx.shape[1]
-        pl = eng.plan_p2p(m, idx, d)
+        P = eng.ep.ep_size
+        tm = eng.timer
+        tm.mark("begin_fwd")
+        with rng("ep.plan_dispatch"):
+            pl = eng.plan_device(m, x, idx)
+        tm.mark("fwd.plan+exchange")
         st = eng._stage
-        Q = T * k
-        tile_off = gemm.tile_offsets(pl["seg"])
-        # dispatch: sorted rows into my stage, owners pull their runs
-        _C.moe_scatter_rows(st.x, pl["inv"], x, k)
-        eng.barrier(_C)
-        xp = torch.zeros(pl["rows"], d, device=x.device, dtype=x.dtype)
-        if pl["n_runs"]:
-            _C.ep_pull_runs(xp, st.hx.buffer_ptrs, d, pl["runs"][: pl["n_runs"]], pl["max_len"])
-        eng.barrier(_C)
-        hg, hu, act, yp = moe_ops.mlp_forward(xp, pl["seg"], tile_off, w_gate, w_up, w_down,
-                                              y_out=st.y[: pl["rows"]])
-        eng.barrier(_C)
-        g32 = gates.float().reshape(-1).contiguous()
-        out = torch.empty(T, d, device=x.device, dtype=x.dtype)
-        y_rows = torch.empty(Q, d, device=x.device, dtype=x.dtype)
-        _C.moe_combine(out, st.hy.buffer_ptrs, d, torch.bfloat16, pl["owner"], pl["pos"], g32, k, y_rows)
-        eng.barrier(_C)
-        ctx.save_for_backward(xp, hg, hu, act, y_rows, pl["pos"], pl["inv"], pl["owner"], pl["seg"], tile_off,
-                              pl["runs"], g32, w_gate, w_up, w_down)
-        ctx.meta = (T, k, d, pl["n_runs"], pl["max_len"], pl["rows"], gates.dtype)
+        cap = pl["cap"]
+        # owners pull their rows (already expert-sorted by each sender) into the grouped operand
+        xp = torch.empty(cap, d, device=x.device, dtype=x.dtype)
+        with rng("ep.pull"):
+            _C.ep_pull_rows(xp, st.hx.buffer_ptrs, d, pl["plan"], P)
+            eng.barrier(_C)                              # every stage read: stages reusable
+        tm.mark("fwd.pull")
+        with rng("ep.expert_gemms"):
+            hg, hu, act, yp = moe_ops.mlp_forward(xp, pl["seg"], pl["tile_off"], w_gate, w_up, w_down,
+                                                  y_out=st.y[:cap])
+        tm.mark("fwd.gemm")
+        with rng("ep.combine"):
+            eng.barrier(_C)                              # every owner's outputs complete
+            g32 = gates.float().reshape(-1).contiguous()
+            out = torch.empty(T, d, device=x.device, dtype=x.dtype)
+            y_rows = torch.empty(T * k, d, device=x.device, dtype=x.dtype)
+            _C.moe_combine(out, st.hy.buffer_ptrs, d, torch.bfloat16, pl["owner"], pl["pos"], g32, k, y_rows)
+            eng.barrier(_C)                              # every output read: y stage reusable
+        tm.mark("fwd.combine")
+        ctx.save_for_backward(xp, hg, hu, act, y_rows, pl["pos"], pl["srow"], pl["owner"], pl["plan"], g32,
+                              w_gate, w_up, w_down)
+        ctx.meta = (T, k, d, cap, m.n_local_experts, gates.dtype)
         ctx.eng = eng
         return out
 
@@ -326,25 +391,35 @@ class _P2PRouted(torch.autograd.Function):
     def backward(ctx, dout):
         from mamformer_b200.ops import moe as moe_ops
         from mamformer_b200.ops.native import _C
-        (xp, hg, hu, act, y_rows, pos, inv, owner, seg, tile_off, runs, g32, w_gate, w_up,
-         w_down) = ctx.saved_tensors
-        T, k, d, n_runs, max_len, rows, gdt = ctx.meta
+        from mamformer_b200.utils.nvtx import rng
+        (xp, hg, hu, act, y_rows, pos, srow, owner, plan, g32, w_gate, w_up, w_down) = ctx.saved_tensors
+        T, k, d, cap, El, gdt = ctx.meta
         eng = ctx.eng
         st = eng._stage
+        P = eng.ep.ep_size
+        tm = eng.timer
+        tm.mark("begin_bwd")
         dout = dout.to(xp.dtype).contiguous()
         dg = torch.empty(T * k, device=xp.device, dtype=torch.float32)
-        _C.moe_combine_bwd(dout, y_rows, None, g32, dg, st.x, inv, k)
-        eng.barrier(_C)
-        dyp = torch.zeros(rows, d, device=xp.device, dtype=xp.dtype)
-        if n_runs:
-            _C.ep_pull_runs(dyp, st.hx.buffer_ptrs, d, runs[:n_runs], max_len)
-        eng.barrier(_C)
-        dxp, (gw_g, gw_u, gw_d) = moe_ops.mlp_backward(dyp, xp, hg, hu, act, seg, tile_off, w_gate, w_up, w_down,
-                                                      dx_out=st.dx[:rows])
-        eng.barrier(_C)
-        dx = torch.empty(T, d, device=xp.device, dtype=xp.dtype)
-        _C.moe_combine(dx, st.hdx.buffer_ptrs, d, torch.float32, owner, pos, None, k, None)
-        eng.barrier(_C)
+        with rng("ep.bwd_dispatch"):
+            # gate-scaled gradient rows, expert-sorted, into this rank's stage; owners pull them
+            _C.moe_combine_bwd(dout, y_rows, None, g32, dg, st.x, srow, k)
+            eng.barrier(_C)
+            dyp = torch.empty(cap, d, device=xp.device, dtype=xp.dtype)
+            _C.ep_pull_rows(dyp, st.hx.buffer_ptrs, d, plan, P)
+            eng.barrier(_C)
+        tm.mark("bwd.pull")
+        seg, tile_off = plan[: El + 1], plan[El + 1: 2 * El + 2]
+        with rng("ep.expert_gemms_bwd"):
+            dxp, (gw_g, gw_u, gw_d) = moe_ops.mlp_backward(dyp, xp, hg, hu, act, seg, tile_off, w_gate, w_up,
+                                                          w_down, dx_out=st.dx[:cap])
+        tm.mark("bwd.gemm")
+        with rng("ep.bwd_combine"):
+            eng.barrier(_C)
+            dx = torch.empty(T, d, device=xp.device, dtype=xp.dtype)
+            _C.moe_combine(dx, st.hdx.buffer_ptrs, d, torch.float32, owner, pos, None, k, None)
+            eng.barrier(_C)
+        tm.mark("bwd.combine")
         return dx, dg.view(T, k).to(gdt), None, gw_g, gw_u, gw_d, None, None
 
 
@@ -355,14 +430,16 @@ def _moe_modules(model: nn.Module):
 
 
 def shard_experts_ep(model: nn.Module, ep_group: ExpertParallelGroup, dp_factor: Optional[int] = None,
-                     dense_dp_group=None, backend: str = "auto") -> nn.Module:
+                     dense_dp_group=None, backend: str = "auto",
+                     capacity_factor: Optional[float] = None) -> nn.Module:
     """Keep this rank's slice of every MoE layer's routed experts and install the EP engine.
 
     Must run before the optimizer is built (the optimizer's flat buffers take the sliced
     parameters).  The number of routed experts must be divisible by the EP size."""
     if ep_group.ep_size <= 1:
         return model
-    eng = EPEngine(ep_group, dense_dp_group=dense_dp_group, dp_factor=dp_factor, backend=backend)
+    eng = EPEngine(ep_group, dense_dp_group=dense_dp_group, dp_factor=dp_factor, backend=backend,
+                   capacity_factor=capacity_factor)
     for mod in _moe_modules(model):
         E = mod.n_routed_experts
         if E % ep_group.ep_size:

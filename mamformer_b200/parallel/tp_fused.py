@@ -32,6 +32,8 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
+from mamformer_b200.utils.nvtx import ranged
+
 _SLOT0 = 320      # signal-pad words used by this module's barrier (after the expert-parallel ones)
 
 
@@ -101,6 +103,7 @@ def _C():
 _AG_IMPL = "pull"
 
 
+@ranged("tp.ag_gemm")
 def ag_gemm(x_local: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False, impl: str = None) -> torch.Tensor:
     """all_gather_rows(x_local) @ w^T (w (N, K)), or @ w (w (K, N)) with ``b_mn``; x_local (rows, K).
 
@@ -162,6 +165,7 @@ def ag_gemm_kernel(x_local: torch.Tensor, w: torch.Tensor, group, b_mn: bool = F
 _RS_IMPL = "pull"
 
 
+@ranged("tp.gemm_rs")
 def gemm_rs(y: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False, impl: str = None) -> torch.Tensor:
     """reduce_scatter_rows(y @ w^T) over the group: returns this rank's (rows / P, N) block.
 

@@ -63,6 +63,45 @@ def ep_moe_worker(rank, world):
     torch.cuda.synchronize()
 
 
+def _tiny_moe_model():
+    from mamformer_b200.config import MamformerConfig
+    from mamformer_b200.models.model import MamformerForCausalLM
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    d = MamformerConfig.from_yaml(os.path.join(root, "configs", "ultra-7b.yaml")).to_dict()
+    d.update(d_model=256, n_heads=2, n_kv_heads=1, head_dim=128, n_layers=2, vocab_size=512,
+             interleave_fusion_layers=[1], interleave_last_layers_dense=1, moe_n_routed_experts=16,
+             moe_top_k=4, moe_expert_intermediate_dim=64, moe_shared_expert_intermediate_dim=128,
+             kda_diff_kernel_dim=128, kda_diff_latent_dim=64, d_ff=512, mtp_enabled=False)
+    torch.manual_seed(0)
+    return MamformerForCausalLM(MamformerConfig.from_dict(d)).cuda()
+
+
+def ep_capacity_rerun_worker(rank, world):
+    """Expert parallelism with a deliberately small capacity: steps whose routing overflows an
+    owner are discarded and rerun with a larger capacity, so the result is bitwise equal to a
+    run whose capacity can never overflow."""
+    from mamformer_b200.engine import TrainConfig, Trainer
+    from mamformer_b200.parallel.expert_parallel import ExpertParallelGroup, shard_experts_ep
+    g = torch.Generator().manual_seed(7 + rank)
+    ids = [torch.randint(0, 512, (2, 128), generator=g).cuda() for _ in range(3)]
+    results = []
+    for cf in (float(world), 0.3):
+        model = _tiny_moe_model()
+        shard_experts_ep(model, ExpertParallelGroup(group=dist.group.WORLD), backend="p2p", capacity_factor=cf)
+        tr = Trainer(model, TrainConfig(learning_rate=1e-3, warmup_steps=1, micro_batch=1), dp_group=dist.group.WORLD,
+                     expert_dp_group=None, ep_group=dist.group.WORLD)
+        losses = [tr.train_step(x, sync_loss=True) for x in ids]
+        eng = model._mamf_ep_engine
+        results.append((losses, {n: p.detach().clone() for n, p in model.named_parameters()}, eng.overflow_steps))
+        del tr, model
+    (l_big, p_big, o_big), (l_small, p_small, o_small) = results
+    assert o_big == 0 and o_small >= 1, (o_big, o_small)
+    assert l_big == l_small, (l_big, l_small)
+    for n in p_big:
+        assert torch.equal(p_big[n], p_small[n]), n
+    torch.cuda.synchronize()
+
+
 def dp_trainer_worker(rank, world):
     """Bucketed, overlapped data-parallel gradient sums on NCCL: the reduced gradients equal a
     single-GPU step on the concatenated batch, and every rank ends with the same parameters.

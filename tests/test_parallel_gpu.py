@@ -42,40 +42,51 @@ def _spawn(fn, world, timeout=240):
     assert not bad, "\n".join(f"rank {r}:\n{m}" for r, m in bad.items())
 
 
-needs2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                            reason="needs 2 GPUs")
+def _worlds(*sizes):
+    """World sizes of a multi-GPU test: every one this box has GPUs for (2 and up)."""
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    return [pytest.param(w, marks=pytest.mark.skipif(n < w, reason=f"needs {w} GPUs")) for w in sizes]
 
 
-@needs2
-def test_data_parallel_trainer_two_gpus():
-    _spawn("dp_trainer_worker", 2)
+ALL = _worlds(2, 4, 8)
 
 
-@needs2
-def test_data_parallel_p2p_transport_two_gpus():
-    _spawn("dp_p2p_worker", 2)
+@pytest.mark.parametrize("world", ALL)
+def test_data_parallel_trainer(world):
+    _spawn("dp_trainer_worker", world)
 
 
-@needs2
-def test_data_parallel_kernel_transport_two_gpus():
-    _spawn("dp_pull_worker", 2)
+@pytest.mark.parametrize("world", ALL)
+def test_data_parallel_p2p_transport(world):
+    """Copy-engine pull form: replicas bitwise equal, gradients equal to NCCL's (rel 1e-5)."""
+    _spawn("dp_p2p_worker", world)
 
 
-@needs2
-def test_data_parallel_nvls_transport_two_gpus():
-    _spawn("dp_nvls_worker", 2)
+@pytest.mark.parametrize("world", ALL)
+def test_data_parallel_kernel_transport(world):
+    _spawn("dp_pull_worker", world)
 
 
-@needs2
-def test_expert_parallel_moe_two_gpus():
-    _spawn("ep_moe_worker", 2)
+@pytest.mark.parametrize("world", _worlds(2))
+def test_data_parallel_nvls_transport(world):
+    _spawn("dp_nvls_worker", world)
 
 
-@needs2
-def test_tp_fused_gemms_two_gpus():
-    _spawn("tp_fused_worker", 2)
+@pytest.mark.parametrize("world", ALL)
+def test_expert_parallel_moe(world):
+    _spawn("ep_moe_worker", world)
 
 
-@needs2
-def test_tp_model_fused_matches_unfused_two_gpus():
-    _spawn("tp_model_fused_worker", 2)
+@pytest.mark.parametrize("world", ALL)
+def test_expert_parallel_capacity_overflow_reruns_the_step(world):
+    _spawn("ep_capacity_rerun_worker", world)
+
+
+@pytest.mark.parametrize("world", _worlds(2, 8))
+def test_tp_fused_gemms(world):
+    _spawn("tp_fused_worker", world)
+
+
+@pytest.mark.parametrize("world", _worlds(2))
+def test_tp_model_fused_matches_unfused(world):
+    _spawn("tp_model_fused_worker", world)
