@@ -55,6 +55,20 @@ def _args():
                     help="N > 1: dense-gradient all-reduce by NCCL (default; validated up to 8 ranks) or "
                          "by this repository's peer-memory path (p2p: 0.145 ms vs 0.155 ms for NCCL per "
                          "64 MiB bucket on 2 GPUs; equal step time, the reduction is overlapped)")
+    ap.add_argument("--profile-table", type=int, default=0,
+                    help="print the top-N kernels of one extra step by device time (torch profiler, for "
+                         "ranking only; never a timed number) to stderr")
+    ap.add_argument("--breakdown", type=int, default=1,
+                    help="after the timed steps, one extra step with CUDA-event marks: forward, backward, "
+                         "exposed gradient reduction, optimizer and the expert-parallel phases (max over ranks)")
+    ap.add_argument("--checkpoint", default="none", choices=["none", "attention", "all"],
+                    help="activation recomputation: none, the reference's selective form (full-attention "
+                         "layers), or every layer (needed by the full 32-layer model)")
+    ap.add_argument("--zero", type=int, default=0, choices=[0, 1],
+                    help="1: shard the dense weights' fp32 masters and Adam moments over the data-parallel group")
+    ap.add_argument("--build", default="auto", choices=["auto", "host", "device"],
+                    help="device: construct on the GPU, each rank allocating only its routed-expert slice "
+                         "(auto: device when the model has more than 8 layers)")
     ap.add_argument("--parallel", default="ep", choices=["ep", "dp"],
                     help="N > 1: ep = routed experts sharded over all N GPUs (EP=N x dense DP=N, the "
                          "ultra-7b benchmark layout, EP=8 x DP on 8 GPUs); dp = every GPU holds every expert")
@@ -112,6 +126,49 @@ def _peak_tflops():
         return 1390.2, "sustained cuBLAS bf16 measured on this pool (file absent)"
 
 
+def _breakdown(trainer, model, batch, world):
+    """One extra (untimed) step with CUDA-event marks; milliseconds per phase, max over ranks.
+    The expert-parallel phases are also contained in forward / backward."""
+    import torch
+    eng = getattr(model, "_mamf_ep_engine", None)
+    trainer.timer.enabled = True
+    trainer.timer.reset()
+    if eng is not None:
+        eng.timer.enabled = True
+        eng.timer.reset()
+    _barrier(world)
+    trainer.train_step(batch)
+    torch.cuda.synchronize()
+    out = trainer.timer.summary()
+    if eng is not None:
+        out.update({"ep." + k: v for k, v in eng.timer.summary().items()})
+        eng.timer.enabled = False
+    trainer.timer.enabled = False
+    keys = sorted(out)
+    vals = [_max_over_ranks(out[k], world) for k in keys]
+    return {k: round(v, 2) for k, v in zip(keys, vals)}
+
+
+def _kernel_table(step_fn, top):
+    """Device time per kernel name over one step (torch profiler; ranking only)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    agg = {}
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            a = agg.setdefault(ev.name, [0.0, 0])
+            a[0] += ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
+            a[1] += 1
+    total = sum(v[0] for v in agg.values()) or 1.0
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][0])[:top]
+    print(f"# kernel device time over one step (total {total / 1e3:.1f} ms, profiler)", file=sys.stderr)
+    for name, (us, n) in rows:
+        print(f"{us / 1e3:9.2f} ms {100 * us / total:5.1f}% {n:6d}x  {name[:140]}", file=sys.stderr)
+
+
 def _emit(obj, rank):
     if rank == 0:
         print(json.dumps(obj), flush=True)
@@ -153,7 +210,17 @@ def run_ours(args, rank, world):
     tcfg = TrainConfig(learning_rate=2e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch,
                        grad_accum=args.grad_accum)
     torch.manual_seed(0)
-    model = MamformerForCausalLM(cfg).cuda()
+    on_device = args.build == "device" or (args.build == "auto" and args.layers > 8)
+    if on_device:
+        import contextlib
+        from mamformer_b200.models.moe import build_expert_slice
+        sl = build_expert_slice(rank, world) if (world > 1 and args.parallel == "ep") else contextlib.nullcontext()
+        with torch.device("cuda"), sl:
+            model = MamformerForCausalLM(cfg)
+    else:
+        model = MamformerForCausalLM(cfg).cuda()
+    if args.checkpoint != "none":
+        model.model.enable_gradient_checkpointing(all_layers=args.checkpoint == "all")
     if world > 1 and args.parallel == "ep":
         from mamformer_b200.parallel import DistributedCoordinator, ParallelConfig
         coord = DistributedCoordinator(ParallelConfig(ep_size=world)).initialize()
@@ -161,11 +228,11 @@ def run_ours(args, rank, world):
         torch.cuda.empty_cache()
         trainer = Trainer(model, tcfg, dp_group=coord.get_group("dense_dp"),
                           expert_dp_group=coord.get_group("expert_dp"), ep_group=coord.get_group("ep"),
-                          dp_transport=args.dp_transport)
+                          dp_transport=args.dp_transport, zero_stage=args.zero)
         parallelism = f"ep{world} (routed experts sharded over {world} GPUs; dense weights data-parallel)"
     else:
         trainer = Trainer(model, tcfg, dp_group=dist.group.WORLD if world > 1 else None,
-                          dp_transport=args.dp_transport)
+                          dp_transport=args.dp_transport, zero_stage=args.zero)
         parallelism = f"dp{world}"
     n_batches = 2
     g = torch.Generator().manual_seed(1234 + rank)
@@ -202,6 +269,11 @@ def run_ours(args, rank, world):
                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(),
                "d2h_bytes_per_step": 4, "last_loss": loss}
 
+    breakdown = _breakdown(trainer, model, dev[0], world) if args.breakdown else None
+    if args.profile_table and rank == 0:
+        _kernel_table(lambda: trainer.train_step(dev[0]), args.profile_table)
+    elif args.profile_table:
+        trainer.train_step(dev[0])                 # every rank takes the same collective steps
     launches = all_kernels = None
     if args.profile_launches:
         ours, total = _count_launches(lambda: trainer.train_step(dev[0]))
@@ -226,11 +298,12 @@ def run_ours(args, rank, world):
                             f"({cfg.layout_string()}), same per-layer shapes",
                    "global_batch": world * per_gpu, "seq_len": args.seq,
                    "micro_batch": args.micro_batch, "grad_accum": args.grad_accum,
-                   "parallelism": parallelism,
+                   "parallelism": parallelism, "checkpoint": args.checkpoint, "zero": args.zero,
+                   "dp_transport": args.dp_transport if world > 1 else None,
                    "params_b": round(sum(p.numel() for p in model.parameters()) / 1e9, 3),
                    "l2": "working set >> L2 (inputs larger than L2)"},
         "clocks": clk, "e2e": e2e, "gpu_launches": launches, "all_kernel_launches": all_kernels,
-        "peak_mem_gib": round(mem, 1), "mfu": mfu,
+        "peak_mem_gib": round(mem, 1), "mfu": mfu, "breakdown_ms": breakdown,
     }
     _emit(out, rank)
 

@@ -35,9 +35,9 @@ void ce_stats(at::Tensor logits, at::Tensor labels, int64_t ignore_index, at::Te
 void ce_grad_inplace(at::Tensor logits, at::Tensor labels, int64_t ignore_index, at::Tensor lse,
                      at::Tensor scale, at::Tensor n_valid);
 void moe_scatter_rows(at::Tensor dst, at::Tensor dst_idx, at::Tensor src, int64_t k);
-void moe_combine(at::Tensor out, std::vector<int64_t> table, int64_t ld_src, at::ScalarType src_dtype,
-                 c10::optional<at::Tensor> owner, at::Tensor pos, c10::optional<at::Tensor> w, int64_t k,
-                 c10::optional<at::Tensor> rows_out);
+void moe_combine(at::Tensor out, std::vector<int64_t> table, int64_t ld_src, int64_t src_rows,
+                 at::ScalarType src_dtype, c10::optional<at::Tensor> owner, at::Tensor pos,
+                 c10::optional<at::Tensor> w, int64_t k, c10::optional<at::Tensor> rows_out);
 void moe_combine_bwd(at::Tensor dout, at::Tensor y, c10::optional<at::Tensor> y_idx, at::Tensor gate,
                      at::Tensor dgate, at::Tensor dy, c10::optional<at::Tensor> dy_idx, int64_t k);
 void ep_pull_runs(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor runs, int64_t max_len);
@@ -49,7 +49,11 @@ void ep_exchange_counts(std::vector<int64_t> mats, std::vector<int64_t> signal, 
 void ep_layout(at::Tensor C, int64_t me, int64_t cap, at::Tensor plan, at::Tensor status);
 void ep_positions(at::Tensor idx, at::Tensor srow, at::Tensor start, at::Tensor plan, int64_t P, int64_t cap,
                   at::Tensor pos, at::Tensor owner);
-void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor plan, int64_t P);
+void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, int64_t src_rows, at::Tensor plan,
+                  int64_t P);
+int64_t bounds_error_moe_rows();
+int64_t bounds_error_ce();
+bool bounds_check_built();
 int64_t ep_plan_size(int64_t P, int64_t El);
 void moe_bias_update(at::Tensor counts, double n_assign, int64_t E, double speed, at::Tensor bias, at::Tensor ema);
 int64_t dp_slice(int64_t lo, int64_t hi, int64_t P);
@@ -108,6 +112,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_positions", &mamf::ep_positions);
   m.def("ep_pull_rows", &mamf::ep_pull_rows);
   m.def("ep_plan_size", &mamf::ep_plan_size);
+  m.def("bounds_error_moe_rows", &mamf::bounds_error_moe_rows);
+  m.def("bounds_error_ce", &mamf::bounds_error_ce);
+  m.def("bounds_check_built", &mamf::bounds_check_built);
   m.def("moe_bias_update", &mamf::moe_bias_update);
   m.def("dp_slice", &mamf::dp_slice);
   m.def("dp_reduce_scatter", &mamf::dp_reduce_scatter);

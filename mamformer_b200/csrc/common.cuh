@@ -98,6 +98,35 @@ __device__ __forceinline__ void st16(T* p, const Vec16<T>& r) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// ---- debug bounds checks ----------------------------------------------------------------------
+// In a build with MAMF_BOUNDS_CHECK defined, MAMF_BOUND(cond, code) evaluates `cond`; when it is
+// false it records `code` in this file's error word (the first failure wins) and returns false,
+// and the caller skips the access.  Nothing traps, so a bad index leaves the context usable.
+// Without the flag MAMF_BOUND is the constant `true` and compiles away.  A file that uses it
+// defines its reader with MAMF_BOUNDS_READER(name) (read-and-clear of its own word).
+static __device__ int g_mamf_bounds_err = 0;
+#ifdef MAMF_BOUNDS_CHECK
+__device__ __forceinline__ bool mamf_bound(bool ok, int code) {
+  if (!ok) atomicCAS(&g_mamf_bounds_err, 0, code);
+  return ok;
+}
+#define MAMF_BOUND(cond, code) ::mamf::mamf_bound((cond), (code))
+#define MAMF_BOUNDS_BUILT 1
+#else
+#define MAMF_BOUND(cond, code) true
+#define MAMF_BOUNDS_BUILT 0
+#endif
+#define MAMF_BOUNDS_READER(fn)                                                        \
+  int64_t fn() {                                                                      \
+    int v = 0;                                                                        \
+    MAMF_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_mamf_bounds_err, sizeof(int)));        \
+    if (v) {                                                                          \
+      int z = 0;                                                                      \
+      MAMF_CUDA_CHECK(cudaMemcpyToSymbol(g_mamf_bounds_err, &z, sizeof(int)));        \
+    }                                                                                 \
+    return v;                                                                         \
+  }
+
 }  // namespace mamf
 
 #define MAMF_DISPATCH_FLOAT_BF16(dtype, NAME, ...)                                      \

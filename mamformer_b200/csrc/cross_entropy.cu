@@ -62,7 +62,9 @@ __global__ void __launch_bounds__(CE_THREADS) ce_stats_kernel(const T* __restric
       const float lse = m + __logf(s);
       lse_out[row] = lse;
       const int64_t lab = labels[row];
-      loss[row] = (lab == ignore_index || lab < 0 || lab >= V) ? 0.f : lse - to_f(lr[lab]);
+      const bool valid = lab >= 0 && lab < V;
+      (void)MAMF_BOUND(valid || lab == ignore_index, 1201);    // a label outside the vocabulary
+      loss[row] = (lab == ignore_index || !valid) ? 0.f : lse - to_f(lr[lab]);
     }
   }
 }
@@ -127,5 +129,7 @@ void ce_grad_inplace(at::Tensor logits, at::Tensor labels, int64_t ignore_index,
   });
   MAMF_LAUNCH_CHECK();
 }
+
+MAMF_BOUNDS_READER(bounds_error_ce)
 
 }  // namespace mamf

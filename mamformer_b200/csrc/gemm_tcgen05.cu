@@ -569,7 +569,8 @@ static void dispatch_out(const CUtensorMap& a, const CUtensorMap& b, const Param
                          bool accum, int bn, const MapSet& as = MapSet{}) {
   auto run = [&](auto bnc) {
     constexpr int BNV = decltype(bnc)::value;
-    constexpr int ST = BNV == 256 ? 4 : 6;
+    // stages: as many A + B k-blocks as fit next to the 32 KB epilogue staging in 227 KB
+    constexpr int ST = BNV == 256 ? 4 : (BNV == 192 ? 4 : 6);
     if (MODE >= 3) {
       TORCH_CHECK(out == at::kBFloat16 && !accum, "tensor-parallel gemm: bf16 output without accumulation");
       return launch<BNV, ST, A_MN, B_MN, MODE, __nv_bfloat16, false>(a, b, p, as);
@@ -581,6 +582,7 @@ static void dispatch_out(const CUtensorMap& a, const CUtensorMap& b, const Param
     TORCH_CHECK(false, "tcgen05 gemm: unsupported output configuration");
   };
   if (bn == 256) run(std::integral_constant<int, 256>{});
+  else if (bn == 192) run(std::integral_constant<int, 192>{});
   else run(std::integral_constant<int, 128>{});
 }
 
@@ -634,9 +636,15 @@ void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, boo
   const int64_t esz_d = D.element_size();
   TORCH_CHECK(aligned16(D.data_ptr()) && (p.ldd * esz_d) % 16 == 0 && (p.d_gstride * esz_d) % 16 == 0,
               "gemm: D must be 16-byte aligned with 16-byte-multiple row strides");
-  // tile width: the one that pads N least (ties -> 256); grouped-K keeps 128 (more tiles per group)
-  const int pad128 = (N + 127) / 128 * 128, pad256 = (N + 255) / 256 * 256;
-  const int bn = (mode != 2 && N >= 256 && pad256 <= pad128) ? 256 : 128;
+  // tile width: the one of 128 / 192 / 256 that pads N least (ties -> the wider tile, which reads
+  // fewer A bytes per FLOP); grouped-K keeps 128 (more tiles per group).  192 serves the MoE expert
+  // width 576 and the MTP FFN width 1152 without a padded tail.
+  const int pad128 = (N + 127) / 128 * 128, pad192 = (N + 191) / 192 * 192, pad256 = (N + 255) / 256 * 256;
+  int bn = 128;
+  if (mode != 2 && N >= 192) {
+    if (N >= 256 && pad256 <= pad192 && pad256 <= pad128) bn = 256;
+    else if (pad192 <= pad128) bn = 192;
+  }
   p.n_tiles_n = (N + bn - 1) / bn;
   if (!a_mn) {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, st[1] = {(uint64_t)A.stride(0) * esz};

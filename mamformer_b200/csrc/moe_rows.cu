@@ -76,12 +76,15 @@ static int row_threads(int64_t d) { return (int)std::min<int64_t>(256, std::max<
 
 // ---- dispatch scatter -------------------------------------------------------------------------
 template <typename T>
-__global__ void scatter_rows_kernel(T* __restrict__ dst, int64_t ld_dst, const int64_t* __restrict__ dst_idx,
-                                    const T* __restrict__ src, int64_t ld_src, int k, int64_t d) {
+__global__ void scatter_rows_kernel(T* __restrict__ dst, int64_t ld_dst, int64_t dst_rows,
+                                    const int64_t* __restrict__ dst_idx, const T* __restrict__ src, int64_t ld_src,
+                                    int k, int64_t d) {
   const int64_t q = blockIdx.x;
   const int64_t t = q / k;
+  const int64_t r = dst_idx[q];
+  if (!MAMF_BOUND(r >= 0 && r < dst_rows, 1101)) return;
   const int4* s = reinterpret_cast<const int4*>(src + t * ld_src);
-  int4* o = reinterpret_cast<int4*>(dst + dst_idx[q] * ld_dst);
+  int4* o = reinterpret_cast<int4*>(dst + r * ld_dst);
   const int64_t nv = d * (int64_t)sizeof(T) / 16;
   for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) o[i] = s[i];
 }
@@ -97,23 +100,25 @@ void moe_scatter_rows(at::Tensor dst, at::Tensor dst_idx, at::Tensor src, int64_
               "scatter_rows: 16-byte aligned rows");
   MAMF_DISPATCH_FLOAT_BF16(src.scalar_type(), "scatter_rows", [&] {
     scatter_rows_kernel<scalar_t><<<(unsigned)Q, row_threads(d), 0, stream()>>>(
-        (scalar_t*)dst.data_ptr(), dst.stride(0), dst_idx.data_ptr<int64_t>(), (const scalar_t*)src.data_ptr(),
-        src.stride(0), (int)k, d);
+        (scalar_t*)dst.data_ptr(), dst.stride(0), dst.size(0), dst_idx.data_ptr<int64_t>(),
+        (const scalar_t*)src.data_ptr(), src.stride(0), (int)k, d);
   });
   MAMF_LAUNCH_CHECK();
 }
 
 // ---- combine: out[t] = sum_j w[q] * row(q) ---------------------------------------------------------
 template <typename S, typename O>
-__global__ void combine_kernel(O* __restrict__ out, PtrTable tab, int64_t ld_src, const int32_t* __restrict__ owner,
-                               const int64_t* __restrict__ pos, const float* __restrict__ w, int k, int64_t d,
-                               S* __restrict__ rows_out) {
+__global__ void combine_kernel(O* __restrict__ out, PtrTable tab, int n_tab, int64_t ld_src, int64_t src_rows,
+                               const int32_t* __restrict__ owner, const int64_t* __restrict__ pos,
+                               const float* __restrict__ w, int k, int64_t d, S* __restrict__ rows_out) {
   const int64_t t = blockIdx.x;
   for (int64_t c = (int64_t)threadIdx.x * 8; c < d; c += (int64_t)blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < k; ++j) {
       const int64_t q = t * k + j;
-      const S* base = static_cast<const S*>(tab.p[owner ? owner[q] : 0]);
+      const int o = owner ? owner[q] : 0;
+      if (!MAMF_BOUND(o >= 0 && o < n_tab && pos[q] >= 0 && pos[q] < src_rows, 1102)) continue;
+      const S* base = static_cast<const S*>(tab.p[o]);
       float f[8];
       Chunk<S>::load(base + pos[q] * ld_src + c, f);
       const float g = w ? w[q] : 1.f;
@@ -125,11 +130,12 @@ __global__ void combine_kernel(O* __restrict__ out, PtrTable tab, int64_t ld_src
   }
 }
 
-// table: up to 8 base pointers (int64) of row arrays with row stride ld_src (elements) and dtype
-// `src_dtype`; owner (Q,) int32 or None (all rows in table[0]); pos (Q,) int64; w (Q,) fp32 or None.
-void moe_combine(at::Tensor out, std::vector<int64_t> table, int64_t ld_src, at::ScalarType src_dtype,
-                 c10::optional<at::Tensor> owner, at::Tensor pos, c10::optional<at::Tensor> w, int64_t k,
-                 c10::optional<at::Tensor> rows_out) {
+// table: up to 8 base pointers (int64) of row arrays with row stride ld_src (elements), src_rows
+// rows each and dtype `src_dtype`; owner (Q,) int32 or None (all rows in table[0]); pos (Q,)
+// int64; w (Q,) fp32 or None.
+void moe_combine(at::Tensor out, std::vector<int64_t> table, int64_t ld_src, int64_t src_rows,
+                 at::ScalarType src_dtype, c10::optional<at::Tensor> owner, at::Tensor pos,
+                 c10::optional<at::Tensor> w, int64_t k, c10::optional<at::Tensor> rows_out) {
   c10::cuda::CUDAGuard guard(out.device());
   const int64_t T = out.size(0), d = out.size(1);
   if (T == 0) return;
@@ -155,7 +161,8 @@ void moe_combine(at::Tensor out, std::vector<int64_t> table, int64_t ld_src, at:
       ro = (S*)rows_out->data_ptr();
     }
     combine_kernel<S, O><<<(unsigned)T, thr, 0, stream()>>>(
-        (O*)out.data_ptr(), tab, ld_src, owner ? owner->data_ptr<int32_t>() : nullptr, pos.data_ptr<int64_t>(),
+        (O*)out.data_ptr(), tab, (int)table.size(), ld_src, src_rows,
+        owner ? owner->data_ptr<int32_t>() : nullptr, pos.data_ptr<int64_t>(),
         w ? w->data_ptr<float>() : nullptr, (int)k, d, ro);
   };
   const bool o_bf = out.scalar_type() == at::kBFloat16;
@@ -173,8 +180,9 @@ void moe_combine(at::Tensor out, std::vector<int64_t> table, int64_t ld_src, at:
 constexpr int CB_MAXK = 16;
 template <typename T>
 __global__ void combine_bwd_kernel(const T* __restrict__ dout, const T* __restrict__ y, const int64_t* __restrict__ y_idx,
-                                   const float* __restrict__ gate, float* __restrict__ dgate, T* __restrict__ dy,
-                                   const int64_t* __restrict__ dy_idx, int k, int64_t d) {
+                                   int64_t y_rows, const float* __restrict__ gate, float* __restrict__ dgate,
+                                   T* __restrict__ dy, const int64_t* __restrict__ dy_idx, int64_t dy_rows, int k,
+                                   int64_t d) {
   __shared__ float red[32 * CB_MAXK];
   const int64_t t = blockIdx.x;
   float part[CB_MAXK];
@@ -187,8 +195,10 @@ __global__ void combine_bwd_kernel(const T* __restrict__ dout, const T* __restri
     for (int j = 0; j < CB_MAXK; ++j) {
       if (j >= k) break;
       const int64_t q = t * k + j;
+      const int64_t yr = y_idx ? y_idx[q] : q, dr = dy_idx ? dy_idx[q] : q;
+      if (!MAMF_BOUND(yr >= 0 && yr < y_rows && dr >= 0 && dr < dy_rows, 1103)) continue;
       float f[8];
-      Chunk<T>::load(y + (y_idx ? y_idx[q] : q) * d + c, f);
+      Chunk<T>::load(y + yr * d + c, f);
       float s = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) s += f[i] * g[i];
@@ -197,7 +207,7 @@ __global__ void combine_bwd_kernel(const T* __restrict__ dout, const T* __restri
       float o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = gw * g[i];
-      Chunk<T>::store(dy + (dy_idx ? dy_idx[q] : q) * d + c, o);
+      Chunk<T>::store(dy + dr * d + c, o);
     }
   }
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -231,8 +241,8 @@ void moe_combine_bwd(at::Tensor dout, at::Tensor y, c10::optional<at::Tensor> y_
   MAMF_DISPATCH_FLOAT_BF16(dout.scalar_type(), "combine_bwd", [&] {
     combine_bwd_kernel<scalar_t><<<(unsigned)T, thr, 0, stream()>>>(
         (const scalar_t*)dout.data_ptr(), (const scalar_t*)y.data_ptr(), y_idx ? y_idx->data_ptr<int64_t>() : nullptr,
-        gate.data_ptr<float>(), dgate.data_ptr<float>(), (scalar_t*)dy.data_ptr(),
-        dy_idx ? dy_idx->data_ptr<int64_t>() : nullptr, (int)k, d);
+        y.size(0), gate.data_ptr<float>(), dgate.data_ptr<float>(), (scalar_t*)dy.data_ptr(),
+        dy_idx ? dy_idx->data_ptr<int64_t>() : nullptr, dy.size(0), (int)k, d);
   });
   MAMF_LAUNCH_CHECK();
 }
@@ -647,7 +657,8 @@ void ep_positions(at::Tensor idx, at::Tensor srow, at::Tensor start, at::Tensor 
 
 // Owner pull: dst rows [0, seg[El]) of the expert-grouped operand, one warp per row.
 __global__ void ep_pull_rows_kernel(__nv_bfloat16* __restrict__ dst, int64_t ld_dst, int64_t dst_rows, PtrTable tab,
-                                    int64_t ld_src, const int* __restrict__ plan, int P, int El, int64_t d) {
+                                    int64_t ld_src, int64_t src_rows, const int* __restrict__ plan, int P, int El,
+                                    int64_t d) {
   const PlanOff o(P, El);
   __shared__ int seg[SORT_MAXE + 1], tot[SORT_MAXE], before[SORT_MAXE], src[SORT_MAXE];
   for (int i = threadIdx.x; i <= El; i += blockDim.x) seg[i] = plan[o.seg + i];
@@ -670,13 +681,16 @@ __global__ void ep_pull_rows_kernel(__nv_bfloat16* __restrict__ dst, int64_t ld_
     int s = 0;
     while (s + 1 < P && before[(s + 1) * El + le] <= j) ++s;
     const int64_t row = (int64_t)src[s * El + le] + (j - before[s * El + le]);
+    if (!MAMF_BOUND(row >= 0 && row < src_rows, 1104)) continue;
     const int4* in = reinterpret_cast<const int4*>(static_cast<const __nv_bfloat16*>(tab.p[s]) + row * ld_src);
     for (int64_t v = lane; v < nv; v += 32) out[v] = in[v];
   }
 }
 
-// dst (>= seg[El] rows, bf16); table: every rank's stage base (row stride ld_src); plan from ep_layout.
-void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at::Tensor plan, int64_t P) {
+// dst (>= seg[El] rows, bf16); table: every rank's stage base (row stride ld_src, src_rows rows);
+// plan from ep_layout.
+void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, int64_t src_rows, at::Tensor plan,
+                  int64_t P) {
   c10::cuda::CUDAGuard guard(dst.device());
   const int64_t d = dst.size(1);
   TORCH_CHECK(dst.scalar_type() == at::kBFloat16 && d % 8 == 0 && (dst.stride(0) * 2) % 16 == 0 && (ld_src * 2) % 16 == 0,
@@ -688,10 +702,13 @@ void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, at
   const int el = (int)((plan.numel() - 2) / (3 + 3 * P));      // total = 3*El + 2 + 3*P*El
   TORCH_CHECK(el >= 1 && PlanOff((int)P, el).total == plan.numel(), "ep_pull_rows: plan size");
   ep_pull_rows_kernel<<<4 * num_sms(), 256, 0, stream()>>>((__nv_bfloat16*)dst.data_ptr(), dst.stride(0), dst.size(0),
-                                                           tab, ld_src, plan.data_ptr<int>(), (int)P, el, d);
+                                                           tab, ld_src, src_rows, plan.data_ptr<int>(), (int)P, el, d);
   MAMF_LAUNCH_CHECK();
 }
 
 int64_t ep_plan_size(int64_t P, int64_t El) { return PlanOff((int)P, (int)El).total; }
+
+MAMF_BOUNDS_READER(bounds_error_moe_rows)
+bool bounds_check_built() { return MAMF_BOUNDS_BUILT != 0; }
 
 }  // namespace mamf

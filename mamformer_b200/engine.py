@@ -77,6 +77,10 @@ class Trainer:
         self._loss_acc = torch.zeros((), device=dev)
         self.step_count = 0
         self.skipped_steps = 0
+        from mamformer_b200.utils.nvtx import PhaseTimer
+        # CUDA-event breakdown of a step (forward / backward / exposed gradient reduction /
+        # optimizer); off unless enabled, e.g. by bench.py --breakdown
+        self.timer = PhaseTimer(False)
 
     def train_step(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor] = None,
                    sync_loss: bool = False, check_grads: bool = False):
@@ -94,16 +98,20 @@ class Trainer:
         self._loss_acc.zero_()
         if eng is not None:
             eng.begin_step(self.model)
+        tm = self.timer
+        tm.mark("begin")
         for i in range(n_micro):
             sl = slice(i * cfg.micro_batch, (i + 1) * cfg.micro_batch)
             out = self.model(input_ids[sl], labels=labels[sl])
             loss = out["loss"]
+            tm.mark("forward")
             if i == n_micro - 1:
                 if eng is not None:
                     eng.record_status()           # expert-parallel capacity check of this step
                 self.optimizer.reducer.arm()      # overlap the gradient all-reduce with this backward
             (loss / n_micro).backward()
             self._loss_acc += loss.detach().float() / n_micro
+            tm.mark("backward")
         if eng is not None and eng.step_overflowed():
             # some expert owner needed more rows than its fixed capacity: discard and rerun the
             # step with the larger capacity the engine has just set (identically on every rank)
@@ -137,7 +145,11 @@ class Trainer:
                 self.skipped_steps += 1
                 self.optimizer.zero_grad()
                 return loss_val if sync_loss else self._loss_acc
+        if tm.enabled:
+            self.optimizer.reduce_gradients()
+            tm.mark("dp_reduce_exposed")
         self.optimizer.step()
+        tm.mark("optimizer")
         self.scheduler.step()
         self.step_count += 1
         return loss_val if sync_loss else self._loss_acc

@@ -39,6 +39,37 @@ from mamformer_b200.models.norm import RMSNorm
 from mamformer_b200.sampling import apply_repetition_penalty, sample_one_token
 
 
+def _checkpointed_layer(layer: MamformerBlock, h, attention_mask, kw):
+    """Run one layer under non-reentrant activation checkpointing, keeping the cross-layer SSM
+    state it emits (a tensor output of the checkpointed function) and its MoE statistics.  The
+    recomputation in the backward pass replays the routing of the original forward (the MoE
+    layers stash their router bias per call) and does not update routing statistics again."""
+    from mamformer_b200.models.moe import routing_replay
+    calls = {"n": 0}
+    aux: dict = {}
+    pend = kw.get("ssm_h_states")
+    rest = {k: v for k, v in kw.items() if k != "ssm_h_states"}
+
+    def run(hs, am, ph):
+        replay = calls["n"] > 0
+        calls["n"] += 1
+        extra = dict(rest)
+        if ph is not None:
+            extra["ssm_h_states"] = ph
+        with routing_replay(replay):
+            out, entry = layer(hs, attention_mask=am, use_cache=False, cache=None, **extra)
+        if not replay and entry is not None and "moe_aux_info" in entry:
+            aux["moe_aux_info"] = entry["moe_aux_info"]
+        hst = entry.get("ssm_h_states") if entry is not None else None
+        return (out, hst) if hst is not None else (out,)
+
+    outs = activation_checkpoint(run, h, attention_mask, pend, use_reentrant=False)
+    entry = dict(aux)
+    if len(outs) > 1:
+        entry["ssm_h_states"] = outs[1]
+    return outs[0], (entry or None)
+
+
 def _is_full_attention_checkpointable(layer: MamformerBlock) -> bool:
     attn = getattr(layer, "attention", None)
     if attn is None:
@@ -135,6 +166,7 @@ class MamformerModel(nn.Module):
                 attn_counter += 1
         self.norm = RMSNorm(config.d_model, eps=config.rms_norm_eps)
         self.gradient_checkpointing = False
+        self.checkpoint_all = False
         reinit_like_reference(self, config.initializer_range)
 
     def _init_weights(self, module: nn.Module) -> None:
@@ -185,7 +217,9 @@ class MamformerModel(nn.Module):
             if rope_offset:
                 kw["rope_offset"] = rope_offset
             with nvtx_rng(f"layer{idx}"):
-                if (self.gradient_checkpointing and self.training and layer.has_attention
+                if self.gradient_checkpointing and self.training and self.checkpoint_all and not use_cache:
+                    h, entry = _checkpointed_layer(layer, h, attention_mask, kw)
+                elif (self.gradient_checkpointing and self.training and layer.has_attention
                         and _is_full_attention_checkpointable(layer)):
                     def run(hs, am, _layer=layer, _kw=kw):
                         return _layer(hs, attention_mask=am, use_cache=False, cache=None, **_kw)[0]
@@ -203,8 +237,13 @@ class MamformerModel(nn.Module):
                 aux_list.append(entry["moe_aux_info"])
         return h, pending, new_caches, aux_list
 
-    def enable_gradient_checkpointing(self) -> None:
+    def enable_gradient_checkpointing(self, all_layers: bool = False) -> None:
+        """Recompute activations in the backward pass.  Default: the reference's selective form
+        (full-attention layers only, ``model.py:252-277``).  ``all_layers=True``: every layer
+        keeps only its input and recomputes the rest, the form that lets the full 32-layer MoE
+        models fit; MoE layers then replay their original routing during the recomputation."""
         self.gradient_checkpointing = True
+        self.checkpoint_all = bool(all_layers)
 
     def disable_gradient_checkpointing(self) -> None:
         self.gradient_checkpointing = False

@@ -24,6 +24,8 @@ Deviation: ``aux_info`` values are 0-dim tensors instead of Python floats (the r
 
 from __future__ import annotations
 
+import collections
+import contextlib
 import math
 from typing import Optional, Tuple
 
@@ -82,6 +84,42 @@ class _RoutedExpertList:
         return (self[e] for e in range(o.expert_offset, o.expert_offset + o.n_local_experts))
 
 
+# Routing replay for activation checkpointing of whole layers: the original forward ("record")
+# stashes the routing state it used (router bias, and any other state a subclass names) in
+# first-in first-out order per module; the recomputation in the backward pass ("replay") routes
+# with the stashed state and leaves the routing statistics alone, so it reproduces the original
+# top-k choice exactly even if other micro-batches moved the bias in between.
+_ROUTING_MODE: list = [None]
+
+
+@contextlib.contextmanager
+def routing_replay(replay: bool):
+    _ROUTING_MODE.append("replay" if replay else "record")
+    try:
+        yield
+    finally:
+        _ROUTING_MODE.pop()
+
+
+def _routing_mode():
+    return _ROUTING_MODE[-1]
+
+
+# Expert slice to allocate at construction (expert-parallel models too large to build whole):
+# inside ``build_expert_slice(rank, size)`` every DeepSeekMoE allocates and initialises only the
+# routed experts [rank * E/size, (rank + 1) * E/size).
+_BUILD_SLICE: list = [None]
+
+
+@contextlib.contextmanager
+def build_expert_slice(rank: int, size: int):
+    _BUILD_SLICE.append((int(rank), int(size)))
+    try:
+        yield
+    finally:
+        _BUILD_SLICE.pop()
+
+
 class DeepSeekMoE(nn.Module):
     def __init__(self, d_model: int, n_shared_experts: int = 2, shared_expert_dim: int = 2304,
                  n_routed_experts: int = 64, top_k: int = 8, routed_expert_dim: int = 576,
@@ -100,15 +138,22 @@ class DeepSeekMoE(nn.Module):
         self.dropout_rate = dropout
         self.expert_offset = 0
         self.n_local_experts = n_routed_experts
+        sl = _BUILD_SLICE[-1]
+        if sl is not None:
+            if n_routed_experts % sl[1]:
+                raise ValueError(f"{n_routed_experts} routed experts do not split over {sl[1]} ranks")
+            self.n_local_experts = n_routed_experts // sl[1]
+            self.expert_offset = sl[0] * self.n_local_experts
         # Optional expert-parallel engine (set by parallel.expert_parallel.shard_experts_ep).
         self.ep_engine = None
 
         self.shared_experts = nn.ModuleList(
             [_SwiGLUExpert(d_model, shared_expert_dim, dropout) for _ in range(n_shared_experts)])
         I = routed_expert_dim
-        self.routed_gate_proj = nn.Parameter(torch.empty(n_routed_experts, I, d_model))
-        self.routed_up_proj = nn.Parameter(torch.empty(n_routed_experts, I, d_model))
-        self.routed_down_proj = nn.Parameter(torch.empty(n_routed_experts, d_model, I))
+        El = self.n_local_experts
+        self.routed_gate_proj = nn.Parameter(torch.empty(El, I, d_model))
+        self.routed_up_proj = nn.Parameter(torch.empty(El, I, d_model))
+        self.routed_down_proj = nn.Parameter(torch.empty(El, d_model, I))
         self._init_routed_like_reference(construct=True)
         self.router = nn.Linear(d_model, n_routed_experts, bias=False)
         if aux_loss_free:
@@ -201,9 +246,21 @@ class DeepSeekMoE(nn.Module):
             logits = logits / self.router_temperature
         return logits
 
+    def _replayed(self, name: str, value: torch.Tensor) -> torch.Tensor:
+        """``value`` in normal operation; under activation checkpointing, the value stashed by
+        the original forward (record mode stashes a copy, replay mode takes it back)."""
+        mode = _routing_mode()
+        if mode is None:
+            return value
+        stash = self.__dict__.setdefault("_replay_stash", collections.defaultdict(collections.deque))
+        if mode == "record":
+            stash[name].append(value.detach().clone())
+            return value
+        return stash[name].popleft()
+
     def _select(self, logits: torch.Tensor):
         if self.aux_loss_free and self.training:
-            scores = logits + self.expert_bias.float()
+            scores = logits + self._replayed("expert_bias", self.expert_bias).float()
         else:
             scores = logits
         return ops.router_topk(scores, self.top_k)
@@ -215,7 +272,7 @@ class DeepSeekMoE(nn.Module):
                               self.routed_down_proj)
 
     def _after_routing(self, idx: torch.Tensor, n_tokens: int, aux: dict) -> None:
-        if not self.training:
+        if not self.training or _routing_mode() == "replay":
             return
         counts = ops.expert_histogram(idx, self.n_routed_experts)
         if self.ep_engine is not None:

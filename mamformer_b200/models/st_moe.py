@@ -16,7 +16,7 @@ import torch
 import torch.nn as nn
 
 from mamformer_b200 import ops
-from mamformer_b200.models.moe import DeepSeekMoE
+from mamformer_b200.models.moe import DeepSeekMoE, _routing_mode
 
 
 class SpaceTimeMoE(DeepSeekMoE):
@@ -70,7 +70,7 @@ class SpaceTimeMoE(DeepSeekMoE):
 
     def _apply_balance_lock(self, combined: torch.Tensor, spatial: torch.Tensor):
         info = {"locks_triggered": 0}
-        locked = self._consecutive_count >= self.balance_lock_threshold
+        locked = self._replayed("consecutive_count", self._consecutive_count) >= self.balance_lock_threshold
         n = int(locked.sum().item())
         if n > 0:
             info["locks_triggered"] = n
@@ -104,7 +104,7 @@ class SpaceTimeMoE(DeepSeekMoE):
         routed = self._routed(xf, idx, gates)
         if self.aux_loss_free and self.training:
             pass  # bias update happens in _after_routing
-        if self.use_balance_lock and self.training and h_flat is not None:
+        if self.use_balance_lock and self.training and h_flat is not None and _routing_mode() != "replay":
             self._update_consecutive_counts(idx)
         self._after_routing(idx, B * S, aux)
         aux["routed_expert_count"] = self.n_routed_experts

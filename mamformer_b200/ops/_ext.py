@@ -37,3 +37,23 @@ def require_native():
             "`python setup.py build_ext --inplace` (or __graft_entry__.build()). "
             f"Import error: {_ERR!r}")
     return _C
+
+
+def bounds_errors() -> dict:
+    """Read and clear the bounds-check error words of the native modules: ``{name: code}`` for
+    every word that is set.  Only kernels compiled with MAMF_BOUNDS_CHECK record anything (the
+    module ``_C_check`` always is; ``_C`` when built with MAMF_BOUNDS_CHECK=1)."""
+    out = {}
+    mods = [("_C", ext())]
+    try:
+        mods.append(("_C_check", importlib.import_module("mamformer_b200._C_check")))
+    except Exception:
+        pass
+    for name, mod in mods:
+        if mod is None:
+            continue
+        for fn in ("bounds_error_moe_rows", "bounds_error_ce"):
+            v = int(getattr(mod, fn)())
+            if v:
+                out[f"{name}.{fn[len('bounds_error_'):]}"] = v
+    return out

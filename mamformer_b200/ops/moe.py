@@ -122,7 +122,7 @@ class _RoutedExperts(torch.autograd.Function):
         ctx.gdtype = gates.dtype
         if combine:
             out = torch.empty(T, d, device=x.device, dtype=x.dtype)
-            _C.moe_combine(out, [yp.data_ptr()], yp.stride(0), yp.dtype, None, pos, g32, k, None)
+            _C.moe_combine(out, [yp.data_ptr()], yp.stride(0), yp.shape[0], yp.dtype, None, pos, g32, k, None)
             return out
         return yp[pos].view(T, k, d)
 
@@ -143,7 +143,7 @@ class _RoutedExperts(torch.autograd.Function):
             _C.moe_scatter_rows(dyp, pos, dout.reshape(T * k, d), 1)
         dxp, (gw_g, gw_u, gw_d) = mlp_backward(dyp, xp, hg, hu, act, seg, tile_off, w_gate, w_up, w_down)
         dx = torch.empty(T, d, device=xp.device, dtype=xp.dtype)
-        _C.moe_combine(dx, [dxp.data_ptr()], dxp.stride(0), dxp.dtype, None, pos, None, k, None)
+        _C.moe_combine(dx, [dxp.data_ptr()], dxp.stride(0), dxp.shape[0], dxp.dtype, None, pos, None, k, None)
         return dx, dgates, None, gw_g, gw_u, gw_d, None
 
 

@@ -366,7 +366,7 @@ class _P2PRouted(torch.autograd.Function):
         # owners pull their rows (already expert-sorted by each sender) into the grouped operand
         xp = torch.empty(cap, d, device=x.device, dtype=x.dtype)
         with rng("ep.pull"):
-            _C.ep_pull_rows(xp, st.hx.buffer_ptrs, d, pl["plan"], P)
+            _C.ep_pull_rows(xp, st.hx.buffer_ptrs, d, st.rows_x, pl["plan"], P)
             eng.barrier(_C)                              # every stage read: stages reusable
         tm.mark("fwd.pull")
         with rng("ep.expert_gemms"):
@@ -378,7 +378,7 @@ class _P2PRouted(torch.autograd.Function):
             g32 = gates.float().reshape(-1).contiguous()
             out = torch.empty(T, d, device=x.device, dtype=x.dtype)
             y_rows = torch.empty(T * k, d, device=x.device, dtype=x.dtype)
-            _C.moe_combine(out, st.hy.buffer_ptrs, d, torch.bfloat16, pl["owner"], pl["pos"], g32, k, y_rows)
+            _C.moe_combine(out, st.hy.buffer_ptrs, d, st.rows_y, torch.bfloat16, pl["owner"], pl["pos"], g32, k, y_rows)
             eng.barrier(_C)                              # every output read: y stage reusable
         tm.mark("fwd.combine")
         ctx.save_for_backward(xp, hg, hu, act, y_rows, pl["pos"], pl["srow"], pl["owner"], pl["plan"], g32,
@@ -406,7 +406,7 @@ class _P2PRouted(torch.autograd.Function):
             _C.moe_combine_bwd(dout, y_rows, None, g32, dg, st.x, srow, k)
             eng.barrier(_C)
             dyp = torch.empty(cap, d, device=xp.device, dtype=xp.dtype)
-            _C.ep_pull_rows(dyp, st.hx.buffer_ptrs, d, plan, P)
+            _C.ep_pull_rows(dyp, st.hx.buffer_ptrs, d, st.rows_x, plan, P)
             eng.barrier(_C)
         tm.mark("bwd.pull")
         seg, tile_off = plan[: El + 1], plan[El + 1: 2 * El + 2]
@@ -417,7 +417,7 @@ class _P2PRouted(torch.autograd.Function):
         with rng("ep.bwd_combine"):
             eng.barrier(_C)
             dx = torch.empty(T, d, device=xp.device, dtype=xp.dtype)
-            _C.moe_combine(dx, st.hdx.buffer_ptrs, d, torch.float32, owner, pos, None, k, None)
+            _C.moe_combine(dx, st.hdx.buffer_ptrs, d, st.rows_y, torch.float32, owner, pos, None, k, None)
             eng.barrier(_C)
         tm.mark("bwd.combine")
         return dx, dg.view(T, k).to(gdt), None, gw_g, gw_u, gw_d, None, None
@@ -445,9 +445,13 @@ def shard_experts_ep(model: nn.Module, ep_group: ExpertParallelGroup, dp_factor:
         if E % ep_group.ep_size:
             raise ValueError(f"{E} routed experts do not split evenly over EP={ep_group.ep_size}")
         s, e = ep_group.get_expert_range(E)
+        prebuilt = mod.routed_gate_proj.shape[0] != E            # built as a slice (build_expert_slice)
+        if prebuilt and (mod.expert_offset, mod.expert_offset + mod.n_local_experts) != (s, e):
+            raise ValueError(f"MoE module holds experts [{mod.expert_offset}, "
+                             f"{mod.expert_offset + mod.n_local_experts}) but EP rank owns [{s}, {e})")
         for name in ("routed_gate_proj", "routed_up_proj", "routed_down_proj"):
             w = getattr(mod, name)
-            p = nn.Parameter(w.detach()[s:e].clone(), requires_grad=w.requires_grad)
+            p = w if prebuilt else nn.Parameter(w.detach()[s:e].clone(), requires_grad=w.requires_grad)
             p._mamf_expert = True
             p._mamf_ep_range = (s, e)
             setattr(mod, name, p)

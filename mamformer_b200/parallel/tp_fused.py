@@ -229,7 +229,7 @@ def gemm_rs_kernel(y: torch.Tensor, w: torch.Tensor, group, b_mn: bool = False) 
     out = torch.empty(rows, N, device=y.device, dtype=torch.bfloat16)
     stage = ws.stage[: P * rows * N].view(P * rows, N)
     pos = (torch.arange(P, device=y.device).view(1, P) * rows + torch.arange(rows, device=y.device).view(rows, 1))
-    C.moe_combine(out, [stage.data_ptr()], N, torch.bfloat16, None, pos.reshape(-1), None, P, None)
+    C.moe_combine(out, [stage.data_ptr()], N, stage.numel() // N, torch.bfloat16, None, pos.reshape(-1), None, P, None)
     ws.barrier(C)                                   # stage free for the next call
     return out
 

@@ -2,7 +2,9 @@
 
 Every .cu/.cpp under mamformer_b200/csrc is compiled for sm_100a only
 (-gencode arch=compute_100a,code=sm_100a); the resulting mamformer_b200/_C*.so is loaded by
-mamformer_b200.ops.
+mamformer_b200.ops.  A second module, mamformer_b200._C_check, holds a bounds-checked build of
+the index-driven kernels (MAMF_BOUNDS_CHECK: bad indices are recorded and skipped, never
+accessed); MAMF_BOUNDS_CHECK=1 in the environment builds the main module with the checks too.
 """
 
 import glob
@@ -26,6 +28,11 @@ if os.environ.get("MAMF_BOUNDS_CHECK") == "1":
     NVCC_FLAGS.append("-DMAMF_BOUNDS_CHECK=1")
 
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
+# Bounds-checked build of the index-driven kernels (always built; see csrc/check/).
+# The wrappers under csrc/check/ include the kernel files with MAMF_BOUNDS_CHECK defined, so their
+# objects never collide with the main module's.
+CHECK_SOURCES = sorted(glob.glob(os.path.join(CSRC, "check", "*.cu")) + glob.glob(os.path.join(CSRC, "check", "*.cpp")))
+CHECK_FLAGS = [f for f in NVCC_FLAGS if f != "-DMAMF_BOUNDS_CHECK=1"]
 
 setup(
     name="mamformer_b200",
@@ -37,7 +44,13 @@ setup(
             sources=sources,
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
+        ),
+        CUDAExtension(
+            name="mamformer_b200._C_check",
+            sources=CHECK_SOURCES,
+            include_dirs=[os.path.join(HERE, CSRC)],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": CHECK_FLAGS},
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -96,9 +96,14 @@ def ep_capacity_rerun_worker(rank, world):
         del tr, model
     (l_big, p_big, o_big), (l_small, p_small, o_small) = results
     assert o_big == 0 and o_small >= 1, (o_big, o_small)
-    assert l_big == l_small, (l_big, l_small)
+    # The capacity only sizes buffers, so the routed computation is the same; what differs run to
+    # run is the order of the float atomics in the scan backward (dA, dD), which can flip the
+    # sign of a near-zero AdamW update: parameters agree to 2 * lr per step.
+    for a, b in zip(l_big, l_small):
+        assert abs(a - b) <= 1e-5 * abs(a), (l_big, l_small)
     for n in p_big:
-        assert torch.equal(p_big[n], p_small[n]), n
+        diff = (p_big[n].float() - p_small[n].float()).abs().max().item()
+        assert diff <= 2 * 1e-3 * len(ids) + 1e-6, (n, diff)
     torch.cuda.synchronize()
 
 

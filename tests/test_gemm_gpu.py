@@ -17,7 +17,8 @@ def _bf(*shape, seed=0):
     return torch.randn(*shape, device="cuda", generator=g).bfloat16()
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 256), (304, 200, 136), (1024, 4096, 4096)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 256), (304, 200, 136), (1024, 4096, 4096),
+                                   (384, 576, 512), (256, 1152, 256), (200, 400, 128)])
 def test_dense_tn(M, N, K):
     a, b = _bf(M, K, seed=1), _bf(N, K, seed=2)
     out = gemm.mm(a, b)
@@ -26,7 +27,7 @@ def test_dense_tn(M, N, K):
     assert _rel(out, a.float() @ b.float().t()) < 1e-2
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (200, 320, 192)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (200, 320, 192), (256, 576, 128)])
 def test_dense_nn(M, N, K):
     a, b = _bf(M, K, seed=3), _bf(K, N, seed=4)
     out = gemm.mm_nn(a, b, out_dtype=torch.float32)
@@ -53,9 +54,11 @@ def _segments(counts, align=64):
     return seg
 
 
-def test_grouped_m_and_k():
+@pytest.mark.parametrize("N", [256, 576])
+def test_grouped_m_and_k(N):
+    """N = 576 (the MoE expert width) runs the 192-wide tile."""
     counts = [70, 0, 256, 5, 130, 64]
-    G, N, K = len(counts), 256, 192
+    G, K = len(counts), 192
     seg = _segments(counts)
     Mt = seg[-1]
     x = torch.zeros(Mt, K, device="cuda").bfloat16()

@@ -200,3 +200,37 @@ def test_bit_parity_with_reference(which):
         assert torch.equal(sa[k], sb[k]), k
     ids = torch.randint(0, c1.vocab_size, (2, 32), generator=torch.Generator().manual_seed(1))
     assert a(ids, labels=ids)["loss"].item() == b(ids, labels=ids)["loss"].item()
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_full_layer_checkpointing_matches_plain_backward(moe):
+    """enable_gradient_checkpointing(all_layers=True): same loss, same gradients, and MoE routing
+    statistics updated once per forward (the recomputation replays the stashed bias)."""
+    d = MamformerConfig.from_yaml(os.path.join(ROOT, "configs", "ultra-7b.yaml")).to_dict()
+    d.update(d_model=64, n_heads=2, n_kv_heads=1, head_dim=32, n_layers=4, vocab_size=128,
+             interleave_fusion_layers=[3], interleave_last_layers_dense=1, moe_enabled=moe,
+             moe_n_routed_experts=8, moe_top_k=2, moe_expert_intermediate_dim=32,
+             moe_shared_expert_intermediate_dim=32, kda_diff_kernel_dim=32, kda_diff_latent_dim=32,
+             d_ff=128, mamba_d_state=32, mtp_enabled=False)
+    cfg = MamformerConfig.from_dict(d)
+    ids = torch.randint(0, 128, (2, 48), generator=torch.Generator().manual_seed(3))
+    res = []
+    for ck in (False, True):
+        torch.manual_seed(0)
+        m = MamformerForCausalLM(cfg)
+        if ck:
+            m.model.enable_gradient_checkpointing(all_layers=True)
+        for _ in range(2):                      # the second pass sees biases moved by the first
+            m.zero_grad()
+            loss = m(ids, labels=ids)["loss"]
+            loss.backward()
+        grads = {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None}
+        bufs = {n: b.clone() for n, b in m.named_buffers() if "expert_bias" in n or "_expert_counts" in n}
+        res.append((loss.item(), grads, bufs))
+    (l0, g0, b0), (l1, g1, b1) = res
+    assert abs(l0 - l1) < 1e-6
+    assert set(g0) == set(g1)
+    for n in g0:
+        assert torch.allclose(g0[n], g1[n], rtol=1e-5, atol=1e-7), n
+    for n in b0:
+        assert torch.equal(b0[n], b1[n]), n

@@ -68,7 +68,7 @@ def _emulated_ep(P, El, T, k, d, cap_factor, seed=0):
         plan = torch.empty(C.ep_plan_size(P, El), dtype=torch.int32, device="cuda")
         C.ep_layout(Cmat, me, cap, plan, status)
         xp = torch.full((cap, d), float("nan"), device="cuda", dtype=torch.bfloat16)
-        C.ep_pull_rows(xp, [s.data_ptr() for s in stages], d, plan, P)
+        C.ep_pull_rows(xp, [s.data_ptr() for s in stages], d, Q, plan, P)
         pos = torch.empty(Q, dtype=torch.int64, device="cuda")
         owner = torch.empty(Q, dtype=torch.int32, device="cuda")
         C.ep_positions(idxs[me], sorts[me][0], sorts[me][2], plan, P, cap, pos, owner)
