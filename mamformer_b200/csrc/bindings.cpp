@@ -69,6 +69,9 @@ std::vector<at::Tensor> linear_attn_bwd(at::Tensor q1, at::Tensor q2, at::Tensor
 std::vector<at::Tensor> router_topk(at::Tensor scores, int64_t k);
 at::Tensor router_topk_bwd(at::Tensor dg, at::Tensor gates, at::Tensor idx, int64_t E);
 at::Tensor expert_histogram(at::Tensor idx, int64_t E);
+std::vector<at::Tensor> flash_tc_fwd(at::Tensor q1, c10::optional<at::Tensor> q2, at::Tensor k, at::Tensor v,
+                                     c10::optional<at::Tensor> lam, int64_t lo, int64_t hi, double scale);
+int64_t flash_tc_error();
 std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, int64_t lo, int64_t hi, double scale);
 std::vector<at::Tensor> flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor lse,
                                        at::Tensor dout, int64_t lo, int64_t hi, double scale);
@@ -127,6 +130,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_topk", &mamf::router_topk);
   m.def("router_topk_bwd", &mamf::router_topk_bwd);
   m.def("expert_histogram", &mamf::expert_histogram);
+  m.def("flash_tc_fwd", &mamf::flash_tc_fwd);
+  m.def("flash_tc_error", &mamf::flash_tc_error);
   m.def("flash_attn_fwd", &mamf::flash_attn_fwd);
   m.def("flash_attn_bwd", &mamf::flash_attn_bwd);
   m.def("gemm_ag", &mamf::gemm_ag);

@@ -1,0 +1,558 @@
+// Flash attention forward on the 5th-generation tensor cores (tcgen05 / TMEM / TMA), two query
+// streams per CTA sharing one K/V stream:
+//
+//   differential mode (KDA-Diff full attention, DSA):  streams A = Q1[h], B = Q2[h]
+//       out = (softmax(Q1 K^T s) V - lam[h] softmax(Q2 K^T s) V) / (1 - lam[h] + 1e-8)
+//   pair mode (GQA):  streams A = Q[h0], B = Q[h0 + 1], two query heads of one KV head
+//       out[h] = softmax(Q[h] K^T s) V
+//
+// Reference semantics: mamformer/layers/kda_diff.py:826-862 (two materialised S x S softmax
+// maps, then the lambda combine), dsa.py:276-317, attention.py:157-181.  Masking is the band
+// lo <= key - (query + Skv - S) <= hi of csrc/flash_attn.cu (causal: lo = -inf, hi = 0); a row
+// without any key gives 0 and lse = +inf.  The per-stream row log-sum-exp (natural log) and the
+// normalised per-stream outputs are kept for the backward (csrc/flash_attn.cu's kernels).
+//
+// One CTA = 128 query rows of one head (or head pair); 10 warps:
+//   warps 0-3  softmax of stream A, warps 4-7 softmax of stream B (thread = query row: its S row
+//              is read from TMEM with tcgen05.ld, P is written as bf16 into shared memory in the
+//              128-byte-swizzled K-major layout the MMA reads);
+//   warp 8     TMA producer (one lane): Q_A, Q_B once, then K / V tiles of 64 keys into a 2-deep
+//              ring (no multicast; the maps cover this GPU's memory only);
+//   warp 9     TMEM allocator + MMA issuer (one lane): S = Q K^T (M 128, N 64, K 128) into a
+//              double-buffered S region per stream, O += P V (M 128, N 128, K 64).
+// TMEM (512 columns): S_A[2] 0..127, S_B[2] 128..255, O_A 256..383, O_B 384..511 (fp32).
+// Online softmax with lazy rescaling: a row's running max is raised (and its O rescaled in TMEM
+// with tcgen05.ld / st) only when a new score exceeds it by more than 8 in log2 units, so P stays
+// below 2^8 and most tiles need no rescale.
+// Every wait is bounded (clock64); a timeout records a code in g_mamf_fa5_err, stops the CTA's
+// work, waits a bounded time for its TMA copies, frees TMEM and returns.
+#include "common.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace mamf {
+namespace fa5 {
+
+constexpr int BM = 128;            // query rows per stream
+constexpr int BN = 64;             // keys per tile
+constexpr int HD = 128;            // head dim
+constexpr int ST = 2;              // K / V ring depth
+constexpr int NT = 320;            // 10 warps
+constexpr long long WAIT_CYCLES = 4000000000LL;   // ~2 s
+constexpr float RESCALE_LOG2 = 8.f;
+
+__device__ int g_mamf_fa5_err = 0;
+
+// shared-memory layout (bytes, from a 1024-aligned base)
+constexpr int Q_BYTES = BM * HD * 2;                     // 32 KB per stream (2 chunks of 64 dims)
+constexpr int K_BYTES = BN * HD * 2;                     // 16 KB per tile
+constexpr int P_BYTES = BM * BN * 2;                     // 16 KB per buffer
+constexpr int OFF_QA = 0, OFF_QB = Q_BYTES;
+constexpr int OFF_K = 2 * Q_BYTES;                       // [ST] K tiles
+constexpr int OFF_V = OFF_K + ST * K_BYTES;              // [ST] V tiles
+constexpr int OFF_P = OFF_V + ST * K_BYTES;              // [stream][2] P buffers
+constexpr int OFF_BAR = OFF_P + 4 * P_BYTES;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;         // barriers + alignment slack
+
+struct Params {
+  int B, S, Skv, H, G, off, lo, hi;
+  float scale_log2;
+  int pair;                    // 1: GQA head pairs, 0: differential (two query tensors)
+  const float* lam;            // (H,) differential lambda (already clamped), null in pair mode
+  __nv_bfloat16* out;          // (B, S, H, HD): combined (differential) or per-head (pair)
+  __nv_bfloat16* oa;           // differential: normalised stream outputs (B, S, H, HD); null in pair mode
+  __nv_bfloat16* ob;
+  float* lse_a;                // (B, H, S) natural-log row log-sum-exp
+  float* lse_b;
+};
+
+// ---- PTX helpers -----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(su32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait; false on timeout (code recorded) or when another role already failed.
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int code) {
+  if (bar_try(b, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (bar_try(b, parity)) return true;
+    if (*((volatile int*)&g_mamf_fa5_err) != 0) return false;
+    if (clock64() - t0 > WAIT_CYCLES) { atomicCAS(&g_mamf_fa5_err, 0, code); return false; }
+  }
+}
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(su32(dst)), "l"(map), "r"(su32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+// UMMA shared-memory descriptor (sm100: version 1 at bit 46, 128-byte swizzle at bits 61-63)
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, M = 128, N = n
+__host__ __device__ constexpr uint32_t idesc(int n, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+               ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tld32(uint32_t taddr, float (&r)[32]) {
+  uint32_t v[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(v[i]);
+}
+__device__ __forceinline__ void tst32(uint32_t taddr, const float (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(__float_as_uint(r[0])), "r"(__float_as_uint(r[1])), "r"(__float_as_uint(r[2])),
+        "r"(__float_as_uint(r[3])), "r"(__float_as_uint(r[4])), "r"(__float_as_uint(r[5])), "r"(__float_as_uint(r[6])),
+        "r"(__float_as_uint(r[7])), "r"(__float_as_uint(r[8])), "r"(__float_as_uint(r[9])), "r"(__float_as_uint(r[10])),
+        "r"(__float_as_uint(r[11])), "r"(__float_as_uint(r[12])), "r"(__float_as_uint(r[13])), "r"(__float_as_uint(r[14])),
+        "r"(__float_as_uint(r[15])), "r"(__float_as_uint(r[16])), "r"(__float_as_uint(r[17])), "r"(__float_as_uint(r[18])),
+        "r"(__float_as_uint(r[19])), "r"(__float_as_uint(r[20])), "r"(__float_as_uint(r[21])), "r"(__float_as_uint(r[22])),
+        "r"(__float_as_uint(r[23])), "r"(__float_as_uint(r[24])), "r"(__float_as_uint(r[25])), "r"(__float_as_uint(r[26])),
+        "r"(__float_as_uint(r[27])), "r"(__float_as_uint(r[28])), "r"(__float_as_uint(r[29])), "r"(__float_as_uint(r[30])),
+        "r"(__float_as_uint(r[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---- the kernel ---------------------------------------------------------------------------------
+struct Maps { CUtensorMap qa, qb, k, v; };
+
+__global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ Maps mp, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;          // [ST]
+  uint64_t* kv_empty = bars + 1 + ST;    // [ST]
+  uint64_t* s_full = bars + 1 + 2 * ST;  // [stream][buf]
+  uint64_t* s_free = s_full + 4;
+  uint64_t* p_full = s_free + 4;
+  uint64_t* o_done = p_full + 4;
+  uint64_t* ex_full = o_done + 4;        // stream B's normalised rows are in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ex_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, q0 = blockIdx.x * BM;
+  const int hpg = p.H / p.G;
+  const int hA = p.pair ? 2 * blockIdx.y : blockIdx.y;
+  const int hB = p.pair ? hA + 1 : hA;
+  const int g = hA / hpg;
+  const int qrows = min(BM, p.S - q0);
+  const int kmin = max(0, q0 + p.off + p.lo);
+  const int kmax = min(p.Skv - 1, q0 + qrows - 1 + p.off + p.hi);
+  const int kt0 = kmax >= kmin ? kmin / BN : 0;
+  const int ntile = kmax >= kmin ? kmax / BN - kt0 + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    bar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) { bar_init(&kv_full[s], 1); bar_init(&kv_empty[s], 1); }
+    for (int i = 0; i < 4; ++i) {
+      bar_init(&s_full[i], 1); bar_init(&s_free[i], 128); bar_init(&p_full[i], 128); bar_init(&o_done[i], 1);
+    }
+    bar_init(ex_full, 128);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 9) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(su32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------- TMA producer -------------------------------
+    if (lane == 0 && ntile > 0) {
+      bar_expect_tx(q_full, 2 * Q_BYTES);
+      const CUtensorMap* mqb = p.pair ? &mp.qa : &mp.qb;
+      for (int c = 0; c < 2; ++c) {
+        tma_3d(sm + OFF_QA + c * (Q_BYTES / 2), &mp.qa, q_full, c * 64, hA, b * p.S + q0);
+        tma_3d(sm + OFF_QB + c * (Q_BYTES / 2), mqb, q_full, c * 64, hB, b * p.S + q0);
+      }
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int j = 0; j < ntile; ++j) {
+        if (!bar_wait(&kv_empty[stage], phase ^ 1, 11)) break;
+        bar_expect_tx(&kv_full[stage], 2 * K_BYTES);
+        const int key0 = b * p.Skv + (kt0 + j) * BN;
+        uint8_t* sK = sm + OFF_K + stage * K_BYTES;
+        uint8_t* sV = sm + OFF_V + stage * K_BYTES;
+        for (int c = 0; c < 2; ++c) {
+          tma_3d(sK + c * (K_BYTES / 2), &mp.k, &kv_full[stage], c * 64, g, key0);
+          tma_3d(sV + c * (K_BYTES / 2), &mp.v, &kv_full[stage], c * 64, g, key0);
+        }
+        ++issued;
+        if (++stage == ST) { stage = 0; phase ^= 1; }
+      }
+      // on an error exit, wait (bounded) for the copies still in flight before the CTA can end
+      if (*((volatile int*)&g_mamf_fa5_err) != 0) {
+        bar_wait(q_full, 0, 0);
+        for (int j = 0; j < issued; ++j) bar_wait(&kv_full[j % ST], (uint32_t)((j / ST) & 1), 0);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (lane == 0 && ntile > 0) {
+      bool ok = bar_wait(q_full, 0, 12);
+      fence_after();
+      constexpr uint32_t ID_QK = idesc(BN, false), ID_PV = idesc(HD, true);
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j % ST, buf = j & 1, use = j >> 1;
+        if (!bar_wait(&kv_full[st], (uint32_t)((j / ST) & 1), 13)) return false;
+        for (int s = 0; s < 2; ++s)
+          if (!bar_wait(&s_free[s * 2 + buf], (uint32_t)((use & 1) ^ 1), 14)) return false;
+        fence_after();
+        const uint32_t kb = su32(sm + OFF_K + st * K_BYTES);
+        for (int s = 0; s < 2; ++s) {
+          const uint32_t qb = su32(sm + (s ? OFF_QB : OFF_QA));
+          const uint32_t d = tmem + (uint32_t)(s * 128 + buf * 64);
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k) {
+            const uint64_t a = sdesc(qb + (k >> 2) * (Q_BYTES / 2) + (k & 3) * 32, 16, 1024);
+            const uint64_t bd = sdesc(kb + (k >> 2) * (K_BYTES / 2) + (k & 3) * 32, 16, 1024);
+            mma(d, a, bd, ID_QK, k > 0 ? 1u : 0u);
+          }
+          commit(&s_full[s * 2 + buf]);
+        }
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; j < ntile && ok; ++j) {
+        if (j + 1 < ntile && !issue_qk(j + 1)) { ok = false; break; }
+        const int st = j % ST, buf = j & 1;
+        const uint32_t vb = su32(sm + OFF_V + st * K_BYTES);
+        for (int s = 0; s < 2 && ok; ++s) {
+          if (!bar_wait(&p_full[s * 2 + buf], (uint32_t)((j >> 1) & 1), 15)) { ok = false; break; }
+          fence_after();
+          const uint32_t pb = su32(sm + OFF_P + (s * 2 + buf) * P_BYTES);
+          const uint32_t d = tmem + (uint32_t)(256 + s * 128);
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k) {
+            const uint64_t a = sdesc(pb + k * 32, 16, 1024);
+            const uint64_t bd = sdesc(vb + k * 2048, K_BYTES / 2, 1024);
+            mma(d, a, bd, ID_PV, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          commit(&o_done[s * 2 + buf]);
+        }
+        if (ok) commit(&kv_empty[st]);
+      }
+    }
+  } else {
+    // ------------------------------- softmax (warps 0-3: A, 4-7: B) -------------------------------
+    const int s = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;                 // query row in the tile = TMEM lane
+    const int qi = q0 + r;
+    const bool row_ok = qi < p.S;
+    const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const int klo = qi + p.off + p.lo, khi = qi + p.off + p.hi;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    uint8_t* prow = sm + OFF_P + r * 128;
+    for (int j = 0; j < ntile && ok; ++j) {
+      const int buf = j & 1;
+      ok = __all_sync(0xffffffffu, bar_wait(&s_full[s * 2 + buf], (uint32_t)((j >> 1) & 1), 21));
+      if (!ok) break;
+      fence_after();
+      float sv[BN];
+      tld32(tl + (uint32_t)(s * 128 + buf * 64), *reinterpret_cast<float(*)[32]>(&sv[0]));
+      tld32(tl + (uint32_t)(s * 128 + buf * 64 + 32), *reinterpret_cast<float(*)[32]>(&sv[32]));
+      fence_before();
+      bar_arrive(&s_free[s * 2 + buf]);
+      const int kbase = (kt0 + j) * BN;
+      const bool full = row_ok && klo <= kbase && khi >= kbase + BN - 1 && kbase + BN - 1 < p.Skv;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        float v = sv[c] * p.scale_log2;
+        if (!full) {
+          const int key = kbase + c;
+          v = (row_ok && key >= klo && key <= khi && key < p.Skv) ? v : -INFINITY;
+        }
+        sv[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      const bool need = m_new > m + RESCALE_LOG2;          // also true for the first key of a row
+      if (__any_sync(0xffffffffu, need && m != -INFINITY)) {
+        // O of this stream holds earlier tiles: wait for the last P V product, then rescale rows
+        ok = __all_sync(0xffffffffu, bar_wait(&o_done[s * 2 + ((j - 1) & 1)], (uint32_t)(((j - 1) >> 1) & 1), 22));
+        if (!ok) break;
+        fence_after();
+        const float f = (need && m != -INFINITY) ? ex2(m - m_new) : 1.f;
+#pragma unroll 1
+        for (int cc = 0; cc < HD; cc += 32) {
+          float o[32];
+          tld32(tl + (uint32_t)(256 + s * 128 + cc), o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= f;
+          tst32(tl + (uint32_t)(256 + s * 128 + cc), o);
+        }
+      }
+      if (need) {
+        l = (m == -INFINITY) ? 0.f : l * ex2(m - m_new);
+        m = m_new;
+      }
+      // the P buffer of tile j - 2 must have been consumed by its P V product
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, bar_wait(&o_done[s * 2 + buf], (uint32_t)(((j - 2) >> 1) & 1), 23));
+        if (!ok) break;
+      }
+      uint8_t* pdst = prow + (s * 2 + buf) * P_BYTES;
+      float rs = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < BN / 8; ++cc) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = (m == -INFINITY) ? 0.f : ex2(sv[cc * 8 + i] - m);
+          rs += e[i];
+        }
+        uint4 v;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(e[0], e[1]), h1 = __floats2bfloat162_rn(e[2], e[3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(e[4], e[5]), h3 = __floats2bfloat162_rn(e[6], e[7]);
+        v.x = *reinterpret_cast<uint32_t*>(&h0); v.y = *reinterpret_cast<uint32_t*>(&h1);
+        v.z = *reinterpret_cast<uint32_t*>(&h2); v.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = v;      // 128-byte swizzle
+      }
+      l += rs;
+      fence_async_smem();
+      fence_before();
+      bar_arrive(&p_full[s * 2 + buf]);
+    }
+    // ---- epilogue ----
+    if (ok && ntile > 0)
+      ok = __all_sync(0xffffffffu, bar_wait(&o_done[s * 2 + ((ntile - 1) & 1)], (uint32_t)(((ntile - 1) >> 1) & 1), 24));
+    if (ok) {
+      fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int h = s ? hB : hA;
+      float* xrow = reinterpret_cast<float*>(sm) + r * (HD + 4);   // stream B's rows (Q / K area is free now)
+      __nv_bfloat16* own = nullptr;
+      if (p.pair) own = p.out;
+      else own = s ? p.ob : p.oa;
+      const int64_t orow = (((int64_t)b * p.S + qi) * p.H + h) * HD;
+#pragma unroll 1
+      for (int cc = 0; cc < HD; cc += 32) {
+        float o[32];
+        if (ntile > 0) tld32(tl + (uint32_t)(256 + s * 128 + cc), o);
+        else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] *= inv;
+        if (row_ok) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 v;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(o[8 * q], o[8 * q + 1]), h1 = __floats2bfloat162_rn(o[8 * q + 2], o[8 * q + 3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(o[8 * q + 4], o[8 * q + 5]), h3 = __floats2bfloat162_rn(o[8 * q + 6], o[8 * q + 7]);
+            v.x = *reinterpret_cast<uint32_t*>(&h0); v.y = *reinterpret_cast<uint32_t*>(&h1);
+            v.z = *reinterpret_cast<uint32_t*>(&h2); v.w = *reinterpret_cast<uint32_t*>(&h3);
+            *reinterpret_cast<uint4*>(own + orow + cc + 8 * q) = v;
+          }
+        }
+        if (!p.pair && s == 1) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(xrow + cc + 4 * q) = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        }
+        if (!p.pair && s == 0) {
+          // keep stream A's normalised values in registers for the combine: stash in the O_A
+          // columns (this thread's own TMEM row) so no extra registers are held across chunks
+          tst32(tl + (uint32_t)(256 + cc), o);
+        }
+      }
+      float* lse = s ? p.lse_b : p.lse_a;
+      if (row_ok) lse[((int64_t)b * p.H + h) * p.S + qi] = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : INFINITY;
+      if (!p.pair) {
+        if (s == 1) {
+          fence_before();
+          bar_arrive(ex_full);
+        } else {
+          ok = __all_sync(0xffffffffu, bar_wait(ex_full, 0, 25));
+          if (ok) {
+            const float lam = p.lam[hA];
+            const float den = 1.f / (1.f - lam + 1e-8f);
+            const float* brow = reinterpret_cast<const float*>(sm) + r * (HD + 4);
+#pragma unroll 1
+            for (int cc = 0; cc < HD; cc += 32) {
+              float a[32];
+              tld32(tl + (uint32_t)(256 + cc), a);
+              if (row_ok) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  float c8[8];
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) c8[i] = (a[8 * q + i] - lam * brow[cc + 8 * q + i]) * den;
+                  uint4 v;
+                  __nv_bfloat162 h0 = __floats2bfloat162_rn(c8[0], c8[1]), h1 = __floats2bfloat162_rn(c8[2], c8[3]);
+                  __nv_bfloat162 h2 = __floats2bfloat162_rn(c8[4], c8[5]), h3 = __floats2bfloat162_rn(c8[6], c8[7]);
+                  v.x = *reinterpret_cast<uint32_t*>(&h0); v.y = *reinterpret_cast<uint32_t*>(&h1);
+                  v.z = *reinterpret_cast<uint32_t*>(&h2); v.w = *reinterpret_cast<uint32_t*>(&h3);
+                  *reinterpret_cast<uint4*>(p.out + orow + cc + 8 * q) = v;
+                }
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+
+}  // namespace fa5
+
+// ---- host side ------------------------------------------------------------------------------------
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn fa5_encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    MAMF_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+
+// (B, L, heads, 128) bf16 -> 3-D map (dim, head, B*L rows), box 64 dims x 1 head x `rows` rows.
+static CUtensorMap fa5_map(const at::Tensor& t, uint32_t rows) {
+  TORCH_CHECK(t.is_contiguous() && t.dim() == 4 && t.size(3) == fa5::HD && t.scalar_type() == at::kBFloat16,
+              "tcgen05 attention: contiguous bf16 (B, L, heads, 128) tensors");
+  TORCH_CHECK(aligned16(t.data_ptr()), "tcgen05 attention: 16-byte aligned base");
+  const int64_t heads = t.size(2);
+  CUtensorMap m;
+  cuuint64_t gd[3] = {(cuuint64_t)fa5::HD, (cuuint64_t)heads, (cuuint64_t)(t.size(0) * t.size(1))};
+  cuuint64_t gs[2] = {(cuuint64_t)fa5::HD * 2, (cuuint64_t)(heads * fa5::HD * 2)};
+  cuuint32_t bx[3] = {64u, 1u, rows}, es[3] = {1, 1, 1};
+  CUresult r = fa5_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), gd, gs, bx, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (attention) failed: ", (int)r);
+  return m;
+}
+
+// Differential mode: q1, q2 (B, S, H, 128), k, v (B, Skv, G, 128), lam (H,) fp32.
+//   returns (out, o1, o2, lse1, lse2): out = (o1 - lam o2) / (1 - lam + 1e-8), o1 / o2 the
+//   normalised stream outputs, lse (B, H, S).
+// Pair mode (q2 undefined): q (B, S, H, 128), H / G even; returns (out, lse).
+std::vector<at::Tensor> flash_tc_fwd(at::Tensor q1, c10::optional<at::Tensor> q2, at::Tensor k, at::Tensor v,
+                                     c10::optional<at::Tensor> lam, int64_t lo, int64_t hi, double scale) {
+  using namespace fa5;
+  c10::cuda::CUDAGuard guard(q1.device());
+  const bool diff = q2.has_value();
+  Params p{};
+  p.B = q1.size(0); p.S = q1.size(1); p.H = q1.size(2); p.Skv = k.size(1); p.G = k.size(2);
+  TORCH_CHECK(k.sizes() == v.sizes() && k.size(0) == p.B && p.H % p.G == 0, "tcgen05 attention: shapes");
+  TORCH_CHECK(p.S <= p.Skv, "tcgen05 attention: S <= Skv");
+  p.off = p.Skv - p.S;
+  p.lo = (int)std::max<int64_t>(lo, -(1LL << 30));
+  p.hi = (int)std::min<int64_t>(hi, (1LL << 30));
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.pair = diff ? 0 : 1;
+  auto f32 = q1.options().dtype(at::kFloat);
+  at::Tensor out = at::empty_like(q1), o1, o2;
+  at::Tensor lse1 = at::empty({p.B, p.H, p.S}, f32), lse2;
+  Maps mp{};
+  mp.qa = fa5_map(q1, BM);
+  mp.k = fa5_map(k.contiguous(), BN);
+  mp.v = fa5_map(v.contiguous(), BN);
+  if (diff) {
+    TORCH_CHECK(q2->sizes() == q1.sizes() && lam.has_value() && lam->numel() == p.H &&
+                lam->scalar_type() == at::kFloat, "tcgen05 attention: q2 like q1, lam (H,) fp32");
+    mp.qb = fa5_map(*q2, BM);
+    o1 = at::empty_like(q1);
+    o2 = at::empty_like(q1);
+    lse2 = at::empty({p.B, p.H, p.S}, f32);
+    p.lam = lam->data_ptr<float>();
+    p.oa = (__nv_bfloat16*)o1.data_ptr();
+    p.ob = (__nv_bfloat16*)o2.data_ptr();
+    p.lse_b = lse2.data_ptr<float>();
+  } else {
+    TORCH_CHECK((p.H / p.G) % 2 == 0, "tcgen05 attention (pair mode): an even number of query heads per KV head");
+    mp.qb = mp.qa;
+    p.lse_b = lse1.data_ptr<float>();
+  }
+  p.out = (__nv_bfloat16*)out.data_ptr();
+  p.lse_a = lse1.data_ptr<float>();
+  if (p.S > 0) {
+    auto kfn = fa5_fwd_kernel;
+    MAMF_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    dim3 grid((unsigned)((p.S + BM - 1) / BM), (unsigned)(diff ? p.H : p.H / 2), (unsigned)p.B);
+    kfn<<<grid, NT, SMEM_BYTES, stream()>>>(mp, p);
+    MAMF_LAUNCH_CHECK();
+  }
+  if (diff) return {out, o1, o2, lse1, lse2};
+  return {out, lse1};
+}
+
+int64_t flash_tc_error() {
+  int v = 0;
+  MAMF_CUDA_CHECK(cudaMemcpyFromSymbol(&v, fa5::g_mamf_fa5_err, sizeof(int)));
+  if (v) {
+    int z = 0;
+    MAMF_CUDA_CHECK(cudaMemcpyToSymbol(fa5::g_mamf_fa5_err, &z, sizeof(int)));
+  }
+  return v;
+}
+
+}  // namespace mamf

@@ -7,6 +7,8 @@ states, not per-step states).
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from mamformer_b200.ops import NATIVE
@@ -296,6 +298,61 @@ class _FlashAttn(torch.autograd.Function):
         return dq, dk, dv, None, None, None
 
 
+class _FlashTCPair(torch.autograd.Function):
+    """GQA attention with the forward on the tcgen05 kernel (two query heads of one KV head per
+    CTA, csrc/flash_tc.cu) and the backward on csrc/flash_attn.cu's kernels."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lo, hi, scale):
+        out, lse = _C.flash_tc_fwd(q, None, k, v, None, int(lo), int(hi), float(scale))
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.args = (int(lo), int(hi), float(scale))
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = _C.flash_attn_bwd(q, k, v, out, lse, dout.to(q.dtype).contiguous(), *ctx.args)
+        return dq, dk, dv, None, None, None
+
+
+class _DiffFlashTC(torch.autograd.Function):
+    """Differential attention: one tcgen05 forward for both softmax maps (shared K / V stream,
+    lambda combine in the epilogue); backward = the flash backward of each map with
+    dO1 = dout / (1 - lam + 1e-8), dO2 = -lam dout / (1 - lam + 1e-8), and
+    d lam = sum dout . (o1 - (1 + 1e-8) o2) / (1 - lam + 1e-8)^2."""
+
+    @staticmethod
+    def forward(ctx, q1, q2, k, v, lam, lo, hi, scale):
+        lam32 = lam.detach().float().contiguous()
+        out, o1, o2, lse1, lse2 = _C.flash_tc_fwd(q1, q2, k, v, lam32, int(lo), int(hi), float(scale))
+        ctx.save_for_backward(q1, q2, k, v, o1, o2, lse1, lse2, lam32)
+        ctx.args = (int(lo), int(hi), float(scale))
+        ctx.lam_dtype = lam.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q1, q2, k, v, o1, o2, lse1, lse2, lam = ctx.saved_tensors
+        den = 1.0 / (1.0 - lam + 1e-8)                               # (H,)
+        d32 = dout.float()
+        do1 = (d32 * den.view(1, 1, -1, 1)).to(q1.dtype).contiguous()
+        do2 = (d32 * (-lam * den).view(1, 1, -1, 1)).to(q1.dtype).contiguous()
+        dq1, dk1, dv1 = _C.flash_attn_bwd(q1, k, v, o1, lse1, do1, *ctx.args)
+        dq2, dk2, dv2 = _C.flash_attn_bwd(q2, k, v, o2, lse2, do2, *ctx.args)
+        diff = o1.float() - (1.0 + 1e-8) * o2.float()
+        dlam = (d32 * diff).sum(dim=(0, 1, 3)) * den * den
+        return dq1, dq2, dk1 + dk2, dv1 + dv2, dlam.to(ctx.lam_dtype), None, None, None
+
+
+_TC_ATTN = os.environ.get("MAMF_FLASH_TC", "1") != "0"
+
+
+def _tc_ok(q, k):
+    return (_TC_ATTN and q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and q.shape[-1] == 128
+            and k.shape[-1] == 128 and q.shape[2] % k.shape[2] == 0 and q.shape[1] <= k.shape[1])
+
+
 def _fa_ok(q, k):
     return q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and q.shape[-1] in (64, 128) \
         and q.shape[2] % k.shape[2] == 0
@@ -307,20 +364,26 @@ def flash_attention(q, k, v, lo=-_BIG, hi=0, scale=None):
     return _FlashAttn.apply(q.contiguous(), k.contiguous(), v.contiguous(), lo, hi, scale)
 
 
-@_register("attention", "csrc/flash_attn.cu")
+@_register("attention", "csrc/flash_tc.cu + csrc/flash_attn.cu")
 def attention(q, k, v, lo, hi):
     if not _fa_ok(q, k):
         from mamformer_b200.ops import reference
         return reference.attention_band(q, k, v, lo, hi)
+    if _tc_ok(q, k) and (q.shape[2] // k.shape[2]) % 2 == 0:
+        return _FlashTCPair.apply(q.contiguous(), k.contiguous(), v.contiguous(), lo, hi, q.shape[-1] ** -0.5)
     return flash_attention(q, k, v, lo, hi)
 
 
-@_register("diff_attention", "csrc/flash_attn.cu")
+@_register("diff_attention", "csrc/flash_tc.cu + csrc/flash_attn.cu")
 def diff_attention(q1, q2, k, v, lam, lo, hi, scale=None):
-    """(softmax(q1 k^T s) - lam softmax(q2 k^T s)) v / (1 - lam): two flash passes combined."""
+    """(softmax(q1 k^T s) - lam softmax(q2 k^T s)) v / (1 - lam): at head_dim 128 one tcgen05
+    forward over a shared K / V stream; otherwise two flash passes combined."""
     if not _fa_ok(q1, k):
         from mamformer_b200.ops import reference
         return reference.diff_attention_band(q1, q2, k, v, lam, lo, hi, scale)
+    if _tc_ok(q1, k) and lam.numel() == q1.shape[2]:
+        sc = q1.shape[-1] ** -0.5 if scale is None else scale
+        return _DiffFlashTC.apply(q1.contiguous(), q2.contiguous(), k.contiguous(), v.contiguous(), lam, lo, hi, sc)
     o1 = flash_attention(q1, k, v, lo, hi, scale)
     o2 = flash_attention(q2, k, v, lo, hi, scale)
     lam4 = lam.view(1, 1, -1, 1).to(o1.dtype)

@@ -155,6 +155,20 @@ def case_flash_attn(B=1, S=4096, H=32, G=8, hd=128, backward=False):
     return (lambda: _C.flash_attn_bwd(q, k, v, out, lse, dout, lo, hi, scale)), 2.5 * flops, 0
 
 
+def case_flash_tc(B=1, S=4096, H=32, G=8, hd=128, diff=False):
+    """tcgen05 flash forward (csrc/flash_tc.cu), causal, 32 query / 8 KV heads: GQA head pairs, or
+    the differential form (two query tensors, one shared K / V stream, lambda combine)."""
+    from mamformer_b200.ops.native import _C
+    mk = lambda h: (torch.randn(B, S, h, hd, device="cuda") * 0.5).bfloat16()  # noqa: E731
+    q, q2, k, v = mk(H), mk(H), mk(G), mk(G)
+    lo, hi, scale = -(1 << 30), 0, hd ** -0.5
+    flops = 4.0 * B * H * S * S * hd / 2 * (2 if diff else 1)
+    if diff:
+        lam = torch.full((H,), 0.5, device="cuda")
+        return (lambda: _C.flash_tc_fwd(q, q2, k, v, lam, lo, hi, scale)), flops, 0
+    return (lambda: _C.flash_tc_fwd(q, None, k, v, None, lo, hi, scale)), flops, 0
+
+
 def case_router(T=4096, E=128, k=8):
     """Router top-k + softmax over the selected scores + per-expert histogram."""
     from mamformer_b200.ops.native import _C
@@ -166,7 +180,8 @@ CASES = {"gemm": case_gemm, "grouped": case_grouped, "wgrad": case_wgrad, "scan"
          "scan_bwd": lambda: case_scan(backward=True), "linear_attn": case_linear_attn,
          "linear_attn_bwd": lambda: case_linear_attn(backward=True), "ce": case_ce, "moe": case_moe,
          "adamw": case_adamw, "flash_attn": case_flash_attn,
-         "flash_attn_bwd": lambda: case_flash_attn(backward=True), "router": case_router}
+         "flash_attn_bwd": lambda: case_flash_attn(backward=True), "router": case_router,
+         "flash_tc": case_flash_tc, "flash_tc_diff": lambda: case_flash_tc(diff=True)}
 
 
 def run(op: str, iters: int = 20, once: bool = False) -> dict:
