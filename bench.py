@@ -61,6 +61,10 @@ def _args():
     ap.add_argument("--breakdown", type=int, default=1,
                     help="after the timed steps, one extra step with CUDA-event marks: forward, backward, "
                          "exposed gradient reduction, optimizer and the expert-parallel phases (max over ranks)")
+    ap.add_argument("--workload", default="ultra7b", choices=["ultra7b", "7b-tp"],
+                    help="ultra7b: the headline MoE benchmark; 7b-tp: configs/7b.yaml (dense hybrid, all "
+                         "layers) tensor-parallel over the N GPUs at seq 8192, global batch 64 sequences "
+                         "(tokens/s of the job; strong scaling)")
     ap.add_argument("--checkpoint", default="none", choices=["none", "attention", "all"],
                     help="activation recomputation: none, the reference's selective form (full-attention "
                          "layers), or every layer (needed by the full 32-layer model)")
@@ -396,12 +400,88 @@ def _exception_summary(exc: BaseException) -> str:
     return f"{kind.__module__}.{kind.__qualname__}: {msg[:300]}{where}"
 
 
+def run_tp(args, rank, world):
+    """configs/7b.yaml tensor-parallel over every GPU: the sharded model computes the unsharded
+    function, every rank sees the same token batch; the all-reduces after row-parallel GEMMs run
+    as this repository's GEMM -> reduce-scatter + all-gather paths."""
+    import torch
+    from mamformer_b200 import ops
+    from mamformer_b200.config import MamformerConfig
+    from mamformer_b200.engine import TrainConfig, Trainer
+    from mamformer_b200.models.model import MamformerForCausalLM
+    from mamformer_b200.parallel import DistributedCoordinator, ParallelConfig
+    from mamformer_b200.utils.clocks import ClockSampler
+    if not ops.has_native():
+        raise RuntimeError("native extension missing")
+    cfg = MamformerConfig.from_yaml(os.path.join(ROOT, "configs", "7b.yaml"))
+    seq = args.seq if args.seq != 4096 else 8192
+    global_batch = 64
+    mb = 1
+    tcfg = TrainConfig(learning_rate=2e-4, warmup_steps=10, max_steps=1000, micro_batch=mb,
+                       grad_accum=global_batch // mb)
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        model = MamformerForCausalLM(cfg)
+    if args.checkpoint != "none":
+        model.model.enable_gradient_checkpointing(all_layers=args.checkpoint == "all")
+    if world > 1:
+        coord = DistributedCoordinator(ParallelConfig(tp_size=world)).initialize()
+        model = coord.shard_model(model)
+    torch.cuda.empty_cache()
+    trainer = Trainer(model, tcfg)
+    g = torch.Generator().manual_seed(1234)                   # identical batch on every TP rank
+    host = torch.randint(0, cfg.vocab_size, (global_batch, seq), generator=g).pin_memory()
+    dev = host.cuda()
+    for _ in range(args.warmup):
+        trainer.train_step(dev)
+    _barrier(world)
+    clocks = ClockSampler(gpu_index=torch.cuda.current_device()).start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        trainer.train_step(dev)
+    e.record()
+    torch.cuda.synchronize()
+    _barrier(world)
+    clk = clocks.stop()
+    ms = _max_over_ranks(s.elapsed_time(e), world) / args.steps
+    value = global_batch * seq / (ms / 1000.0)
+    e2e = None
+    if not args.no_e2e and args.e2e_steps > 0:
+        _barrier(world)
+        t0 = time.perf_counter()
+        loss = None
+        for _ in range(args.e2e_steps):
+            loss = trainer.train_step(host, sync_loss=True)
+        torch.cuda.synchronize()
+        el = _max_over_ranks(time.perf_counter() - t0, world) / args.e2e_steps
+        e2e = {"value": global_batch * seq / el, "unit": "tokens/s",
+               "h2d_bytes_per_step": host.numel() * host.element_size(), "d2h_bytes_per_step": 4,
+               "last_loss": loss}
+    from mamformer_b200.utils.metrics import matmul_params_per_token
+    n_mm = matmul_params_per_token(model) * world              # the shards add up to the model
+    peak_tf, peak_src = _peak_tflops()
+    _emit({"metric": "train tokens/s per box, configs/7b.yaml dense hybrid bf16 TP over N B200, max over ranks",
+           "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic uniform-random token ids, random-init weights", "impl": "mamformer_b200",
+           "config": {"model": f"7b (configs/7b.yaml, {cfg.n_layers} layers, {cfg.layout_string()})",
+                      "global_batch": global_batch, "seq_len": seq, "micro_batch": mb,
+                      "grad_accum": global_batch // mb, "parallelism": f"tp{world}", "checkpoint": args.checkpoint,
+                      "l2": "working set >> L2 (inputs larger than L2)"},
+           "clocks": clk, "e2e": e2e, "peak_mem_gib": round(torch.cuda.max_memory_allocated() / 2 ** 30, 1),
+           "mfu": {"value": round(value / world * 6.0 * n_mm / (peak_tf * 1e12), 4), "peak": peak_src,
+                   "counts": "6 x matmul weights per token, approximate under TP (per-rank shards x N)"}}, rank)
+
+
 def main():
     args = _args()
     rank, world, _ = _dist_init()
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.workload == "7b-tp":
+            run_tp(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

@@ -62,6 +62,8 @@ struct Params {
   __nv_bfloat16* out;          // (B, S, H, HD): combined (differential) or per-head (pair)
   __nv_bfloat16* oa;           // differential: normalised stream outputs (B, S, H, HD); null in pair mode
   __nv_bfloat16* ob;
+  __nv_bfloat16* od;           // differential: o_a - o_b computed in fp32 (the d lambda term; the
+                               // difference of the two bf16-rounded maps would lose it to cancellation)
   float* lse_a;                // (B, H, S) natural-log row log-sum-exp
   float* lse_b;
 };
@@ -430,15 +432,24 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
               if (row_ok) {
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                  float c8[8];
+                  float c8[8], d8[8];
 #pragma unroll
-                  for (int i = 0; i < 8; ++i) c8[i] = (a[8 * q + i] - lam * brow[cc + 8 * q + i]) * den;
-                  uint4 v;
+                  for (int i = 0; i < 8; ++i) {
+                    const float bv = brow[cc + 8 * q + i];
+                    c8[i] = (a[8 * q + i] - lam * bv) * den;
+                    d8[i] = a[8 * q + i] - bv;
+                  }
+                  uint4 v, w;
                   __nv_bfloat162 h0 = __floats2bfloat162_rn(c8[0], c8[1]), h1 = __floats2bfloat162_rn(c8[2], c8[3]);
                   __nv_bfloat162 h2 = __floats2bfloat162_rn(c8[4], c8[5]), h3 = __floats2bfloat162_rn(c8[6], c8[7]);
                   v.x = *reinterpret_cast<uint32_t*>(&h0); v.y = *reinterpret_cast<uint32_t*>(&h1);
                   v.z = *reinterpret_cast<uint32_t*>(&h2); v.w = *reinterpret_cast<uint32_t*>(&h3);
                   *reinterpret_cast<uint4*>(p.out + orow + cc + 8 * q) = v;
+                  h0 = __floats2bfloat162_rn(d8[0], d8[1]); h1 = __floats2bfloat162_rn(d8[2], d8[3]);
+                  h2 = __floats2bfloat162_rn(d8[4], d8[5]); h3 = __floats2bfloat162_rn(d8[6], d8[7]);
+                  w.x = *reinterpret_cast<uint32_t*>(&h0); w.y = *reinterpret_cast<uint32_t*>(&h1);
+                  w.z = *reinterpret_cast<uint32_t*>(&h2); w.w = *reinterpret_cast<uint32_t*>(&h3);
+                  *reinterpret_cast<uint4*>(p.od + orow + cc + 8 * q) = w;
                 }
               }
             }
@@ -492,8 +503,8 @@ static CUtensorMap fa5_map(const at::Tensor& t, uint32_t rows) {
 }
 
 // Differential mode: q1, q2 (B, S, H, 128), k, v (B, Skv, G, 128), lam (H,) fp32.
-//   returns (out, o1, o2, lse1, lse2): out = (o1 - lam o2) / (1 - lam + 1e-8), o1 / o2 the
-//   normalised stream outputs, lse (B, H, S).
+//   returns (out, o1, o2, lse1, lse2, od): out = (o1 - lam o2) / (1 - lam + 1e-8), o1 / o2 the
+//   normalised stream outputs, lse (B, H, S), od = o1 - o2 formed in fp32.
 // Pair mode (q2 undefined): q (B, S, H, 128), H / G even; returns (out, lse).
 std::vector<at::Tensor> flash_tc_fwd(at::Tensor q1, c10::optional<at::Tensor> q2, at::Tensor k, at::Tensor v,
                                      c10::optional<at::Tensor> lam, int64_t lo, int64_t hi, double scale) {
@@ -510,7 +521,7 @@ std::vector<at::Tensor> flash_tc_fwd(at::Tensor q1, c10::optional<at::Tensor> q2
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.pair = diff ? 0 : 1;
   auto f32 = q1.options().dtype(at::kFloat);
-  at::Tensor out = at::empty_like(q1), o1, o2;
+  at::Tensor out = at::empty_like(q1), o1, o2, od;
   at::Tensor lse1 = at::empty({p.B, p.H, p.S}, f32), lse2;
   Maps mp{};
   mp.qa = fa5_map(q1, BM);
@@ -522,7 +533,9 @@ std::vector<at::Tensor> flash_tc_fwd(at::Tensor q1, c10::optional<at::Tensor> q2
     mp.qb = fa5_map(*q2, BM);
     o1 = at::empty_like(q1);
     o2 = at::empty_like(q1);
+    od = at::empty_like(q1);
     lse2 = at::empty({p.B, p.H, p.S}, f32);
+    p.od = (__nv_bfloat16*)od.data_ptr();
     p.lam = lam->data_ptr<float>();
     p.oa = (__nv_bfloat16*)o1.data_ptr();
     p.ob = (__nv_bfloat16*)o2.data_ptr();
@@ -541,7 +554,7 @@ std::vector<at::Tensor> flash_tc_fwd(at::Tensor q1, c10::optional<at::Tensor> q2
     kfn<<<grid, NT, SMEM_BYTES, stream()>>>(mp, p);
     MAMF_LAUNCH_CHECK();
   }
-  if (diff) return {out, o1, o2, lse1, lse2};
+  if (diff) return {out, o1, o2, lse1, lse2, od};
   return {out, lse1};
 }
 

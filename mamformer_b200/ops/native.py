@@ -320,28 +320,28 @@ class _DiffFlashTC(torch.autograd.Function):
     """Differential attention: one tcgen05 forward for both softmax maps (shared K / V stream,
     lambda combine in the epilogue); backward = the flash backward of each map with
     dO1 = dout / (1 - lam + 1e-8), dO2 = -lam dout / (1 - lam + 1e-8), and
-    d lam = sum dout . (o1 - (1 + 1e-8) o2) / (1 - lam + 1e-8)^2."""
+    d lam = sum dout . (o1 - (1 + 1e-8) o2) / (1 - lam + 1e-8)^2, with o1 - o2 taken from the
+    kernel's fp32 difference (the two maps are close, so bf16 copies of each would lose it)."""
 
     @staticmethod
     def forward(ctx, q1, q2, k, v, lam, lo, hi, scale):
         lam32 = lam.detach().float().contiguous()
-        out, o1, o2, lse1, lse2 = _C.flash_tc_fwd(q1, q2, k, v, lam32, int(lo), int(hi), float(scale))
-        ctx.save_for_backward(q1, q2, k, v, o1, o2, lse1, lse2, lam32)
+        out, o1, o2, lse1, lse2, od = _C.flash_tc_fwd(q1, q2, k, v, lam32, int(lo), int(hi), float(scale))
+        ctx.save_for_backward(q1, q2, k, v, o1, o2, lse1, lse2, lam32, od)
         ctx.args = (int(lo), int(hi), float(scale))
         ctx.lam_dtype = lam.dtype
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        q1, q2, k, v, o1, o2, lse1, lse2, lam = ctx.saved_tensors
+        q1, q2, k, v, o1, o2, lse1, lse2, lam, od = ctx.saved_tensors
         den = 1.0 / (1.0 - lam + 1e-8)                               # (H,)
         d32 = dout.float()
         do1 = (d32 * den.view(1, 1, -1, 1)).to(q1.dtype).contiguous()
         do2 = (d32 * (-lam * den).view(1, 1, -1, 1)).to(q1.dtype).contiguous()
         dq1, dk1, dv1 = _C.flash_attn_bwd(q1, k, v, o1, lse1, do1, *ctx.args)
         dq2, dk2, dv2 = _C.flash_attn_bwd(q2, k, v, o2, lse2, do2, *ctx.args)
-        diff = o1.float() - (1.0 + 1e-8) * o2.float()
-        dlam = (d32 * diff).sum(dim=(0, 1, 3)) * den * den
+        dlam = (d32 * od.float()).sum(dim=(0, 1, 3)) * den * den    # the 1e-8 o2 term is below fp32 noise
         return dq1, dq2, dk1 + dk2, dv1 + dv2, dlam.to(ctx.lam_dtype), None, None, None
 
 

@@ -71,7 +71,7 @@ def test_rows_without_keys_give_zero_and_infinite_lse():
     q1, q2, k, v = _qkv(1, 128, 2, 1, seed=3)
     lam = torch.full((2,), 0.5, device="cuda")
     # band entirely after the sequence end: no query row has a key
-    out, o1, o2, lse1, lse2 = C.flash_tc_fwd(q1, q2, k, v, lam, 1000, 2000, 128 ** -0.5)
+    out, o1, o2, lse1, lse2, od = C.flash_tc_fwd(q1, q2, k, v, lam, 1000, 2000, 128 ** -0.5)
     torch.cuda.synchronize()
     assert C.flash_tc_error() == 0
     assert torch.count_nonzero(out) == 0 and torch.isinf(lse1).all() and torch.isinf(lse2).all()
