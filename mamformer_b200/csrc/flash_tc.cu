@@ -140,6 +140,29 @@ __device__ __forceinline__ void tld32(uint32_t taddr, float (&r)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(v[i]);
 }
+// 64 consecutive columns of this thread's TMEM lane: two loads in flight, one wait
+__device__ __forceinline__ void tld64(uint32_t taddr, float* r) {
+  uint32_t v[64];
+#define MAMF_TLD32_ASM(DST, ADDR)                                                                          \
+  asm volatile(                                                                                            \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"     \
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                           \
+      : "=r"(DST[0]), "=r"(DST[1]), "=r"(DST[2]), "=r"(DST[3]), "=r"(DST[4]), "=r"(DST[5]), "=r"(DST[6]),   \
+        "=r"(DST[7]), "=r"(DST[8]), "=r"(DST[9]), "=r"(DST[10]), "=r"(DST[11]), "=r"(DST[12]),             \
+        "=r"(DST[13]), "=r"(DST[14]), "=r"(DST[15]), "=r"(DST[16]), "=r"(DST[17]), "=r"(DST[18]),          \
+        "=r"(DST[19]), "=r"(DST[20]), "=r"(DST[21]), "=r"(DST[22]), "=r"(DST[23]), "=r"(DST[24]),          \
+        "=r"(DST[25]), "=r"(DST[26]), "=r"(DST[27]), "=r"(DST[28]), "=r"(DST[29]), "=r"(DST[30]),          \
+        "=r"(DST[31])                                                                                      \
+      : "r"(ADDR))
+  uint32_t* lo = v;
+  uint32_t* hi = v + 32;
+  MAMF_TLD32_ASM(lo, taddr);
+  MAMF_TLD32_ASM(hi, taddr + 32u);
+#undef MAMF_TLD32_ASM
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) r[i] = __uint_as_float(v[i]);
+}
 __device__ __forceinline__ void tst32(uint32_t taddr, const float (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -304,23 +327,27 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
       if (!ok) break;
       fence_after();
       float sv[BN];
-      tld32(tl + (uint32_t)(s * 128 + buf * 64), *reinterpret_cast<float(*)[32]>(&sv[0]));
-      tld32(tl + (uint32_t)(s * 128 + buf * 64 + 32), *reinterpret_cast<float(*)[32]>(&sv[32]));
+      tld64(tl + (uint32_t)(s * 128 + buf * 64), sv);
       fence_before();
       bar_arrive(&s_free[s * 2 + buf]);
       const int kbase = (kt0 + j) * BN;
       const bool full = row_ok && klo <= kbase && khi >= kbase + BN - 1 && kbase + BN - 1 < p.Skv;
-      float mx = -INFINITY;
+      if (__any_sync(0xffffffffu, !full)) {           // band edge or sequence end: mask raw scores
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        float v = sv[c] * p.scale_log2;
-        if (!full) {
+        for (int c = 0; c < BN; ++c) {
           const int key = kbase + c;
-          v = (row_ok && key >= klo && key <= khi && key < p.Skv) ? v : -INFINITY;
+          sv[c] = (row_ok && key >= klo && key <= khi && key < p.Skv) ? sv[c] : -INFINITY;
         }
-        sv[c] = v;
-        mx = fmaxf(mx, v);
       }
+      // row max of the raw scores with 8 independent chains (the scale is positive)
+      float mq[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mq[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mq[c & 7] = fmaxf(mq[c & 7], sv[c]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) mq[i] = fmaxf(mq[i], mq[i + 4]);
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * p.scale_log2;
       const float m_new = fmaxf(m, mx);
       const bool need = m_new > m + RESCALE_LOG2;          // also true for the first key of a row
       if (__any_sync(0xffffffffu, need && m != -INFINITY)) {
@@ -348,14 +375,17 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
         if (!ok) break;
       }
       uint8_t* pdst = prow + (s * 2 + buf) * P_BYTES;
-      float rs = 0.f;
+      // p = 2^(s * scale_log2 - m); masked scores are -inf and give 0.  A row without any key so
+      // far (m = -inf) has only masked scores, so subtracting 0 instead keeps it at 0.
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      float rq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int cc = 0; cc < BN / 8; ++cc) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          e[i] = (m == -INFINITY) ? 0.f : ex2(sv[cc * 8 + i] - m);
-          rs += e[i];
+          e[i] = ex2(fmaf(sv[cc * 8 + i], p.scale_log2, neg_m));
+          rq[i] += e[i];
         }
         uint4 v;
         __nv_bfloat162 h0 = __floats2bfloat162_rn(e[0], e[1]), h1 = __floats2bfloat162_rn(e[2], e[3]);
@@ -364,7 +394,7 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
         v.z = *reinterpret_cast<uint32_t*>(&h2); v.w = *reinterpret_cast<uint32_t*>(&h3);
         *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = v;      // 128-byte swizzle
       }
-      l += rs;
+      l += ((rq[0] + rq[1]) + (rq[2] + rq[3])) + ((rq[4] + rq[5]) + (rq[6] + rq[7]));
       fence_async_smem();
       fence_before();
       bar_arrive(&p_full[s * 2 + buf]);

@@ -13,8 +13,13 @@ from mamformer_b200.ops import reference as ref  # noqa: E402
 BIG = 1 << 30
 
 
-def _rel(a, b):
-    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp(min=1e-6)).item()
+def _rel(a, b, floor=1e-6):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp(min=floor)).item()
+
+
+# Gradient comparisons use an absolute floor: with the one-key diagonal band the exact dq / dk
+# are zero (softmax over a single key has no gradient), and only rounding noise is left.
+GFLOOR = 0.05
 
 
 def _qkv(B, S, H, G, seed, Skv=None):
@@ -45,7 +50,7 @@ def test_diff_forward_and_grads_match_fp32(B, S, H, G, band):
     (out.float() * dout).sum().backward()
     (want * dout).sum().backward()
     for name, a, b in zip(["dq1", "dq2", "dk", "dv", "dlam"], leaves, rl):
-        assert _rel(a.grad, b.grad) < 3e-2, (name, _rel(a.grad, b.grad))
+        assert _rel(a.grad, b.grad, GFLOOR) < 3e-2, (name, _rel(a.grad, b.grad, GFLOOR))
 
 
 @pytest.mark.parametrize("B,S,H,G", [(1, 256, 4, 2), (2, 333, 8, 2), (1, 512, 8, 1)])
@@ -63,7 +68,7 @@ def test_gqa_pair_forward_and_grads_match_fp32(B, S, H, G, band):
     (out.float() * dout).sum().backward()
     (want * dout).sum().backward()
     for name, a, b in zip(["dq", "dk", "dv"], leaves, rl):
-        assert _rel(a.grad, b.grad) < 3e-2, (name, _rel(a.grad, b.grad))
+        assert _rel(a.grad, b.grad, GFLOOR) < 3e-2, (name, _rel(a.grad, b.grad, GFLOOR))
 
 
 def test_rows_without_keys_give_zero_and_infinite_lse():
