@@ -16,7 +16,7 @@
 //   warps 0-3  softmax of stream A, warps 4-7 softmax of stream B (thread = query row: its S row
 //              is read from TMEM with tcgen05.ld, P is written as bf16 into shared memory in the
 //              128-byte-swizzled K-major layout the MMA reads);
-//   warp 8     TMA producer (one lane): Q_A, Q_B once, then K / V tiles of 64 keys into a 2-deep
+//   warp 8     TMA producer (one lane): Q_A, Q_B once, then K / V tiles of 64 keys into a 3-deep
 //              ring (no multicast; the maps cover this GPU's memory only);
 //   warp 9     TMEM allocator + MMA issuer (one lane): S = Q K^T (M 128, N 64, K 128) into a
 //              double-buffered S region per stream, O += P V (M 128, N 128, K 64).
@@ -36,7 +36,7 @@ namespace fa5 {
 constexpr int BM = 128;            // query rows per stream
 constexpr int BN = 64;             // keys per tile
 constexpr int HD = 128;            // head dim
-constexpr int ST = 2;              // K / V ring depth
+constexpr int ST = 3;              // K / V ring depth (two tiles of TMA prefetch)
 constexpr int NT = 320;            // 10 warps
 constexpr long long WAIT_CYCLES = 4000000000LL;   // ~2 s
 constexpr float RESCALE_LOG2 = 8.f;
