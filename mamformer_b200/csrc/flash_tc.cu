@@ -16,7 +16,7 @@
 //   warps 0-3  softmax of stream A, warps 4-7 softmax of stream B (thread = query row: its S row
 //              is read from TMEM with tcgen05.ld, P is written as bf16 into shared memory in the
 //              128-byte-swizzled K-major layout the MMA reads);
-//   warp 8     TMA producer (one lane): Q_A, Q_B once, then K / V tiles of 64 keys into a 3-deep
+//   warp 8     TMA producer (one lane): Q_A, Q_B once, then K / V tiles of 64 keys into a 4-deep
 //              ring (no multicast; the maps cover this GPU's memory only);
 //   warp 9     TMEM allocator + MMA issuer (one lane): S = Q K^T (M 128, N 64, K 128) into a
 //              double-buffered S region per stream, O += P V (M 128, N 128, K 64).
@@ -36,7 +36,7 @@ namespace fa5 {
 constexpr int BM = 128;            // query rows per stream
 constexpr int BN = 64;             // keys per tile
 constexpr int HD = 128;            // head dim
-constexpr int ST = 3;              // K / V ring depth (two tiles of TMA prefetch)
+constexpr int ST = 4;              // K / V ring depth (three tiles of TMA prefetch)
 constexpr int NT = 320;            // 10 warps
 constexpr long long WAIT_CYCLES = 4000000000LL;   // ~2 s
 constexpr float RESCALE_LOG2 = 8.f;
@@ -50,8 +50,8 @@ constexpr int P_BYTES = BM * BN * 2;                     // 16 KB per buffer
 constexpr int OFF_QA = 0, OFF_QB = Q_BYTES;
 constexpr int OFF_K = 2 * Q_BYTES;                       // [ST] K tiles
 constexpr int OFF_V = OFF_K + ST * K_BYTES;              // [ST] V tiles
-constexpr int OFF_P = OFF_V + ST * K_BYTES;              // [stream][2] P buffers
-constexpr int OFF_BAR = OFF_P + 4 * P_BYTES;
+constexpr int OFF_P = OFF_V + ST * K_BYTES;              // [stream] P buffer (written after the last P V read it)
+constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;         // barriers + alignment slack
 
 struct Params {
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
         for (int s = 0; s < 2 && ok; ++s) {
           if (!bar_wait(&p_full[s * 2 + buf], (uint32_t)((j >> 1) & 1), 15)) { ok = false; break; }
           fence_after();
-          const uint32_t pb = su32(sm + OFF_P + (s * 2 + buf) * P_BYTES);
+          const uint32_t pb = su32(sm + OFF_P + s * P_BYTES);
           const uint32_t d = tmem + (uint32_t)(256 + s * 128);
 #pragma unroll
           for (int k = 0; k < BN / 16; ++k) {
@@ -369,12 +369,12 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
         l = (m == -INFINITY) ? 0.f : l * ex2(m - m_new);
         m = m_new;
       }
-      // the P buffer of tile j - 2 must have been consumed by its P V product
-      if (j >= 2) {
-        ok = __all_sync(0xffffffffu, bar_wait(&o_done[s * 2 + buf], (uint32_t)(((j - 2) >> 1) & 1), 23));
+      // the stream's P buffer must have been consumed by the P V product of tile j - 1
+      if (j >= 1) {
+        ok = __all_sync(0xffffffffu, bar_wait(&o_done[s * 2 + ((j - 1) & 1)], (uint32_t)(((j - 1) >> 1) & 1), 23));
         if (!ok) break;
       }
-      uint8_t* pdst = prow + (s * 2 + buf) * P_BYTES;
+      uint8_t* pdst = prow + s * P_BYTES;
       // p = 2^(s * scale_log2 - m); masked scores are -inf and give 0.  A row without any key so
       // far (m = -inf) has only masked scores, so subtracting 0 instead keeps it at 0.
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
