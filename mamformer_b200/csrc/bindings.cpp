@@ -55,6 +55,7 @@ int64_t bounds_error_moe_rows();
 int64_t bounds_error_ce();
 bool bounds_check_built();
 int64_t ep_plan_size(int64_t P, int64_t El);
+void moe_zero_pad_rows(at::Tensor buf, at::Tensor seg, at::Tensor counts);
 void moe_bias_update(at::Tensor counts, double n_assign, int64_t E, double speed, at::Tensor bias, at::Tensor ema);
 int64_t dp_slice(int64_t lo, int64_t hi, int64_t P);
 at::Tensor dp_reduce_scatter(std::vector<int64_t> bufs, int64_t me, int64_t lo, int64_t hi, double scale, bool want_sq);
@@ -115,6 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_positions", &mamf::ep_positions);
   m.def("ep_pull_rows", &mamf::ep_pull_rows);
   m.def("ep_plan_size", &mamf::ep_plan_size);
+  m.def("moe_zero_pad_rows", &mamf::moe_zero_pad_rows);
   m.def("bounds_error_moe_rows", &mamf::bounds_error_moe_rows);
   m.def("bounds_error_ce", &mamf::bounds_error_ce);
   m.def("bounds_check_built", &mamf::bounds_check_built);

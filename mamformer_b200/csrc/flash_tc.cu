@@ -14,13 +14,16 @@
 //
 // One CTA = 128 query rows of one head (or head pair); 10 warps:
 //   warps 0-3  softmax of stream A, warps 4-7 softmax of stream B (thread = query row: its S row
-//              is read from TMEM with tcgen05.ld, P is written as bf16 into shared memory in the
-//              128-byte-swizzled K-major layout the MMA reads);
-//   warp 8     TMA producer (one lane): Q_A, Q_B once, then K / V tiles of 64 keys into a 4-deep
+//              is read from TMEM with tcgen05.ld and its P row is written back as packed bf16
+//              over the first 32 columns of the same S buffer with tcgen05.st);
+//   warp 8     TMA producer (one lane): Q_A, Q_B once, then K / V tiles of 64 keys into a 5-deep
 //              ring (no multicast; the maps cover this GPU's memory only);
 //   warp 9     TMEM allocator + MMA issuer (one lane): S = Q K^T (M 128, N 64, K 128) into a
-//              double-buffered S region per stream, O += P V (M 128, N 128, K 64).
+//              double-buffered S region per stream, O += P V (M 128, N 128, K 64) with P read
+//              from TMEM (the A-in-tensor-memory form of tcgen05.mma) and V from shared memory.
 // TMEM (512 columns): S_A[2] 0..127, S_B[2] 128..255, O_A 256..383, O_B 384..511 (fp32).
+// The MMA thread issues O += P(j) V before S(j + 2) = Q K^T into the same buffer, and the tensor
+// pipe runs one thread's MMAs in order, so P needs no buffer of its own and no proxy fence.
 // Online softmax with lazy rescaling: a row's running max is raised (and its O rescaled in TMEM
 // with tcgen05.ld / st) only when a new score exceeds it by more than 8 in log2 units, so P stays
 // below 2^8 and most tiles need no rescale.
@@ -36,7 +39,7 @@ namespace fa5 {
 constexpr int BM = 128;            // query rows per stream
 constexpr int BN = 64;             // keys per tile
 constexpr int HD = 128;            // head dim
-constexpr int ST = 4;              // K / V ring depth (three tiles of TMA prefetch)
+constexpr int ST = 5;              // K / V ring depth (four tiles of TMA prefetch)
 constexpr int NT = 320;            // 10 warps
 constexpr long long WAIT_CYCLES = 4000000000LL;   // ~2 s
 constexpr float RESCALE_LOG2 = 8.f;
@@ -46,12 +49,10 @@ __device__ int g_mamf_fa5_err = 0;
 // shared-memory layout (bytes, from a 1024-aligned base)
 constexpr int Q_BYTES = BM * HD * 2;                     // 32 KB per stream (2 chunks of 64 dims)
 constexpr int K_BYTES = BN * HD * 2;                     // 16 KB per tile
-constexpr int P_BYTES = BM * BN * 2;                     // 16 KB per buffer
 constexpr int OFF_QA = 0, OFF_QB = Q_BYTES;
 constexpr int OFF_K = 2 * Q_BYTES;                       // [ST] K tiles
 constexpr int OFF_V = OFF_K + ST * K_BYTES;              // [ST] V tiles
-constexpr int OFF_P = OFF_V + ST * K_BYTES;              // [stream] P buffer (written after the last P V read it)
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+constexpr int OFF_BAR = OFF_V + ST * K_BYTES;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;         // barriers + alignment slack
 
 struct Params {
@@ -119,12 +120,16 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
   asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
                ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
 }
+// A operand read from tensor memory (P), B from shared memory (V)
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+               ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+}
 __device__ __forceinline__ void commit(uint64_t* b) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b)) : "memory");
 }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tld32(uint32_t taddr, float (&r)[32]) {
   uint32_t v[32];
@@ -196,8 +201,7 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
   uint64_t* kv_full = bars + 1;          // [ST]
   uint64_t* kv_empty = bars + 1 + ST;    // [ST]
   uint64_t* s_full = bars + 1 + 2 * ST;  // [stream][buf]
-  uint64_t* s_free = s_full + 4;
-  uint64_t* p_full = s_free + 4;
+  uint64_t* p_full = s_full + 4;         // P of tile j in TMEM (128 arrivals)
   uint64_t* o_done = p_full + 4;
   uint64_t* ex_full = o_done + 4;        // stream B's normalised rows are in shared memory
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ex_full + 1);
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
     bar_init(q_full, 1);
     for (int s = 0; s < ST; ++s) { bar_init(&kv_full[s], 1); bar_init(&kv_empty[s], 1); }
     for (int i = 0; i < 4; ++i) {
-      bar_init(&s_full[i], 1); bar_init(&s_free[i], 128); bar_init(&p_full[i], 128); bar_init(&o_done[i], 1);
+      bar_init(&s_full[i], 1); bar_init(&p_full[i], 128); bar_init(&o_done[i], 1);
     }
     bar_init(ex_full, 128);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -270,10 +274,9 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
       fence_after();
       constexpr uint32_t ID_QK = idesc(BN, false), ID_PV = idesc(HD, true);
       auto issue_qk = [&](int j) -> bool {
-        const int st = j % ST, buf = j & 1, use = j >> 1;
+        const int st = j % ST, buf = j & 1;
+        // S buffer `buf` last held P(j - 2), read by O += P V issued earlier by this thread
         if (!bar_wait(&kv_full[st], (uint32_t)((j / ST) & 1), 13)) return false;
-        for (int s = 0; s < 2; ++s)
-          if (!bar_wait(&s_free[s * 2 + buf], (uint32_t)((use & 1) ^ 1), 14)) return false;
         fence_after();
         const uint32_t kb = su32(sm + OFF_K + st * K_BYTES);
         for (int s = 0; s < 2; ++s) {
@@ -297,13 +300,12 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
         for (int s = 0; s < 2 && ok; ++s) {
           if (!bar_wait(&p_full[s * 2 + buf], (uint32_t)((j >> 1) & 1), 15)) { ok = false; break; }
           fence_after();
-          const uint32_t pb = su32(sm + OFF_P + s * P_BYTES);
+          const uint32_t pa = tmem + (uint32_t)(s * 128 + buf * 64);     // P: 32 columns of bf16 pairs
           const uint32_t d = tmem + (uint32_t)(256 + s * 128);
 #pragma unroll
           for (int k = 0; k < BN / 16; ++k) {
-            const uint64_t a = sdesc(pb + k * 32, 16, 1024);
             const uint64_t bd = sdesc(vb + k * 2048, K_BYTES / 2, 1024);
-            mma(d, a, bd, ID_PV, (j > 0 || k > 0) ? 1u : 0u);
+            mma_ts(d, pa + (uint32_t)(k * 8), bd, ID_PV, (j > 0 || k > 0) ? 1u : 0u);
           }
           commit(&o_done[s * 2 + buf]);
         }
@@ -320,7 +322,6 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
     const int klo = qi + p.off + p.lo, khi = qi + p.off + p.hi;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    uint8_t* prow = sm + OFF_P + r * 128;
     for (int j = 0; j < ntile && ok; ++j) {
       const int buf = j & 1;
       ok = __all_sync(0xffffffffu, bar_wait(&s_full[s * 2 + buf], (uint32_t)((j >> 1) & 1), 21));
@@ -328,8 +329,6 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
       fence_after();
       float sv[BN];
       tld64(tl + (uint32_t)(s * 128 + buf * 64), sv);
-      fence_before();
-      bar_arrive(&s_free[s * 2 + buf]);
       const int kbase = (kt0 + j) * BN;
       const bool full = row_ok && klo <= kbase && khi >= kbase + BN - 1 && kbase + BN - 1 < p.Skv;
       if (__any_sync(0xffffffffu, !full)) {           // band edge or sequence end: mask raw scores
@@ -369,33 +368,22 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
         l = (m == -INFINITY) ? 0.f : l * ex2(m - m_new);
         m = m_new;
       }
-      // the stream's P buffer must have been consumed by the P V product of tile j - 1
-      if (j >= 1) {
-        ok = __all_sync(0xffffffffu, bar_wait(&o_done[s * 2 + ((j - 1) & 1)], (uint32_t)(((j - 1) >> 1) & 1), 23));
-        if (!ok) break;
-      }
-      uint8_t* pdst = prow + s * P_BYTES;
       // p = 2^(s * scale_log2 - m); masked scores are -inf and give 0.  A row without any key so
       // far (m = -inf) has only masked scores, so subtracting 0 instead keeps it at 0.
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
       float rq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float pk[BN / 2];                                   // P as bf16 pairs, bit patterns in fp32 slots
 #pragma unroll
-      for (int cc = 0; cc < BN / 8; ++cc) {
-        float e[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = ex2(fmaf(sv[cc * 8 + i], p.scale_log2, neg_m));
-          rq[i] += e[i];
-        }
-        uint4 v;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(e[0], e[1]), h1 = __floats2bfloat162_rn(e[2], e[3]);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(e[4], e[5]), h3 = __floats2bfloat162_rn(e[6], e[7]);
-        v.x = *reinterpret_cast<uint32_t*>(&h0); v.y = *reinterpret_cast<uint32_t*>(&h1);
-        v.z = *reinterpret_cast<uint32_t*>(&h2); v.w = *reinterpret_cast<uint32_t*>(&h3);
-        *reinterpret_cast<uint4*>(pdst + ((cc ^ (r & 7)) << 4)) = v;      // 128-byte swizzle
+      for (int c2 = 0; c2 < BN / 2; ++c2) {
+        const float e0 = ex2(fmaf(sv[2 * c2], p.scale_log2, neg_m));
+        const float e1 = ex2(fmaf(sv[2 * c2 + 1], p.scale_log2, neg_m));
+        rq[(2 * c2) & 7] += e0;
+        rq[(2 * c2 + 1) & 7] += e1;
+        __nv_bfloat162 h = __floats2bfloat162_rn(e0, e1);
+        pk[c2] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h));
       }
       l += ((rq[0] + rq[1]) + (rq[2] + rq[3])) + ((rq[4] + rq[5]) + (rq[6] + rq[7]));
-      fence_async_smem();
+      tst32(tl + (uint32_t)(s * 128 + buf * 64), pk);     // over this row's S(j), already in registers
       fence_before();
       bar_arrive(&p_full[s * 2 + buf]);
     }

@@ -708,6 +708,37 @@ void ep_pull_rows(at::Tensor dst, std::vector<int64_t> table, int64_t ld_src, in
 
 int64_t ep_plan_size(int64_t P, int64_t El) { return PlanOff((int)P, (int)El).total; }
 
+// ---- zero the pad rows of an expert-grouped buffer ------------------------------------------------
+// Rows [seg[e] + counts[e], seg[e + 1]) of every expert segment: the grouped weight-gradient GEMM
+// contracts over whole 64-row segments, so they must hold zeros; all other rows are written by
+// the dispatch (so the buffer itself can start uninitialised).
+__global__ void zero_pad_rows_kernel(__nv_bfloat16* __restrict__ buf, int64_t ld, int64_t rows,
+                                     const int* __restrict__ seg, const int* __restrict__ counts, int64_t d) {
+  const int e = blockIdx.x;
+  const int64_t r0 = (int64_t)seg[e] + counts[e], r1 = seg[e + 1];
+  const int64_t nv = d / 8;
+  for (int64_t r = r0 + threadIdx.y; r < r1; r += blockDim.y) {
+    if (!MAMF_BOUND(r >= 0 && r < rows, 1105)) continue;
+    int4* o = reinterpret_cast<int4*>(buf + r * ld);
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x) o[v] = make_int4(0, 0, 0, 0);
+  }
+}
+
+// buf (rows, d) bf16; seg (E+1) int32 64-aligned offsets; counts (E) int32 rows per expert.
+void moe_zero_pad_rows(at::Tensor buf, at::Tensor seg, at::Tensor counts) {
+  c10::cuda::CUDAGuard guard(buf.device());
+  const int64_t E = counts.numel(), d = buf.size(1);
+  if (E == 0) return;
+  TORCH_CHECK(buf.scalar_type() == at::kBFloat16 && d % 8 == 0 && (buf.stride(0) * 2) % 16 == 0 &&
+              aligned16(buf.data_ptr()), "zero_pad_rows: bf16 16-byte aligned rows");
+  TORCH_CHECK(seg.scalar_type() == at::kInt && counts.scalar_type() == at::kInt && seg.numel() == E + 1,
+              "zero_pad_rows: int32 seg (E+1) and counts (E)");
+  zero_pad_rows_kernel<<<(unsigned)E, dim3(32, 8), 0, stream()>>>((__nv_bfloat16*)buf.data_ptr(), buf.stride(0),
+                                                                  buf.size(0), seg.data_ptr<int>(),
+                                                                  counts.data_ptr<int>(), d);
+  MAMF_LAUNCH_CHECK();
+}
+
 MAMF_BOUNDS_READER(bounds_error_moe_rows)
 bool bounds_check_built() { return MAMF_BOUNDS_BUILT != 0; }
 

@@ -62,6 +62,17 @@ def plan_eager(flat: torch.Tensor, n_experts: int):
     return pos, seg32, gemm.tile_offsets(seg32), counts
 
 
+def _grouped_buffer(rows, d, dtype, device, seg, counts):
+    """Expert-grouped row buffer whose pad rows are zero; the real rows are left for the caller
+    to write (native: only the pads are cleared, instead of the whole buffer)."""
+    if device.type == "cuda" and dtype == torch.bfloat16 and counts.dtype == torch.int32 and d % 8 == 0:
+        from mamformer_b200.ops._ext import require_native
+        buf = torch.empty(rows, d, device=device, dtype=dtype)
+        require_native().moe_zero_pad_rows(buf, seg, counts)
+        return buf
+    return torch.zeros(rows, d, device=device, dtype=dtype)
+
+
 def _grad_sink(w: torch.Tensor):
     """fp32 buffer the weight gradient is accumulated into (the optimizer's, if attached)."""
     mg = getattr(w, "main_grad", None)
@@ -111,12 +122,12 @@ class _RoutedExperts(torch.autograd.Function):
         T, d = x.shape
         k = idx.shape[1]
         E = w_gate.shape[0]
-        pos, seg, tile_off, _, rows = plan(idx, E)
-        xp = torch.zeros(rows, d, device=x.device, dtype=x.dtype)
+        pos, seg, tile_off, counts, rows = plan(idx, E)
+        xp = _grouped_buffer(rows, d, x.dtype, x.device, seg, counts)
         _C.moe_scatter_rows(xp, pos, x, k)
         hg, hu, act, yp = mlp_forward(xp, seg, tile_off, w_gate, w_up, w_down)
         g32 = gates.float().reshape(-1).contiguous()
-        ctx.save_for_backward(xp, hg, hu, act, yp, pos, seg, tile_off, g32, w_gate, w_up, w_down)
+        ctx.save_for_backward(xp, hg, hu, act, yp, pos, seg, tile_off, g32, w_gate, w_up, w_down, counts)
         ctx.combine = combine
         ctx.shape = (T, k, d)
         ctx.gdtype = gates.dtype
@@ -129,10 +140,10 @@ class _RoutedExperts(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         from mamformer_b200.ops.native import _C
-        xp, hg, hu, act, yp, pos, seg, tile_off, g32, w_gate, w_up, w_down = ctx.saved_tensors
+        xp, hg, hu, act, yp, pos, seg, tile_off, g32, w_gate, w_up, w_down, counts = ctx.saved_tensors
         T, k, d = ctx.shape
         rows = xp.shape[0]
-        dyp = torch.zeros(rows, d, device=xp.device, dtype=xp.dtype)
+        dyp = _grouped_buffer(rows, d, xp.dtype, xp.device, seg, counts)
         dout = dout.to(xp.dtype).contiguous()
         if ctx.combine:
             dg = torch.empty(T * k, device=xp.device, dtype=torch.float32)

@@ -43,9 +43,16 @@ def _spawn(fn, world, timeout=240):
 
 
 def _worlds(*sizes):
-    """World sizes of a multi-GPU test: every one this box has GPUs for (2 and up)."""
+    """World sizes of a multi-GPU test: every one this box has GPUs for (2 and up), optionally
+    restricted by MAMF_TEST_WORLDS (e.g. "8")."""
+    import os
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
-    return [pytest.param(w, marks=pytest.mark.skipif(n < w, reason=f"needs {w} GPUs")) for w in sizes]
+    only = {int(x) for x in os.environ.get("MAMF_TEST_WORLDS", "").split(",") if x.strip()}
+    out = []
+    for w in sizes:
+        skip = n < w or (bool(only) and w not in only)
+        out.append(pytest.param(w, marks=pytest.mark.skipif(skip, reason=f"needs {w} GPUs / not selected")))
+    return out
 
 
 ALL = _worlds(2, 4, 8)
