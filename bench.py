@@ -65,6 +65,10 @@ def _args():
                     help="ultra7b: the headline MoE benchmark; 7b-tp: configs/7b.yaml (dense hybrid, all "
                          "layers) tensor-parallel over the N GPUs at seq 8192, global batch 64 sequences "
                          "(tokens/s of the job; strong scaling)")
+    ap.add_argument("--window-mode", default="reference", choices=["reference", "causal"],
+                    help="sliding-window masks: the reference's (0 <= key - query < W, which with the causal "
+                         "mask leaves only the diagonal in full differential attention and looks ahead in "
+                         "GQA) or the causal window (0 <= query - key < W)")
     ap.add_argument("--checkpoint", default="none", choices=["none", "attention", "all"],
                     help="activation recomputation: none, the reference's selective form (full-attention "
                          "layers), or every layer (needed by the full 32-layer model)")
@@ -225,6 +229,10 @@ def run_ours(args, rank, world):
         model = MamformerForCausalLM(cfg).cuda()
     if args.checkpoint != "none":
         model.model.enable_gradient_checkpointing(all_layers=args.checkpoint == "all")
+    if args.window_mode != "reference":
+        for m in model.modules():
+            if hasattr(m, "window_mode"):
+                m.window_mode = args.window_mode
     if world > 1 and args.parallel == "ep":
         from mamformer_b200.parallel import DistributedCoordinator, ParallelConfig
         coord = DistributedCoordinator(ParallelConfig(ep_size=world)).initialize()
@@ -303,6 +311,7 @@ def run_ours(args, rank, world):
                    "global_batch": world * per_gpu, "seq_len": args.seq,
                    "micro_batch": args.micro_batch, "grad_accum": args.grad_accum,
                    "parallelism": parallelism, "checkpoint": args.checkpoint, "zero": args.zero,
+                   "window_mode": args.window_mode,
                    "dp_transport": args.dp_transport if world > 1 else None,
                    "params_b": round(sum(p.numel() for p in model.parameters()) / 1e9, 3),
                    "l2": "working set >> L2 (inputs larger than L2)"},
