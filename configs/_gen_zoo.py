@@ -96,12 +96,9 @@ TRAIN_OVERRIDES = {
 }
 
 
-def main():
-    for name, model in ZOO.items():
-        train = dict(TRAIN, max_seq_len=model["max_seq_len"], **TRAIN_OVERRIDES.get(name, {}))
-        with open(os.path.join(HERE, f"{name}.yaml"), "w") as fh:
-            fh.write(f"# {model['name']} - generated by configs/_gen_zoo.py\n")
-            yaml.safe_dump({"model": model, "training": train}, fh, sort_keys=False, default_flow_style=None)
+def arch_verify_config():
+    """The small all-features model of ``_arch_verify.yaml`` (8 layers, KDA-Diff, 16-expert MoE,
+    MTP, cross-layer interleave with one fusion layer) used by the parity tests."""
     sys.path.insert(0, os.path.dirname(HERE))
     from mamformer_b200.config import (DSAConfig, InterleaveConfig, KDADiffConfig, MambaConfig,
                                        MamformerConfig, MoEConfig, MTPConfig)
@@ -115,7 +112,19 @@ def main():
                            interleave=InterleaveConfig(enabled=True, pattern="cross_layer", attn_every_k=4,
                                                        last_layers_dense=1, fusion_layers=[7]))
     arch.generation.max_context, arch.generation.max_output_tokens = 512, 256
-    arch.to_yaml(os.path.join(HERE, "_arch_verify.yaml"))
+    return arch
+
+
+def main():
+    for name, model in ZOO.items():
+        train = dict(TRAIN, max_seq_len=model["max_seq_len"], **TRAIN_OVERRIDES.get(name, {}))
+        with open(os.path.join(HERE, f"{name}.yaml"), "w") as fh:
+            fh.write(f"# {model['name']} - generated by configs/_gen_zoo.py\n")
+            yaml.safe_dump({"model": model, "training": train}, fh, sort_keys=False, default_flow_style=None)
+    sys.path.insert(0, os.path.dirname(HERE))
+    from mamformer_b200.config import (DSAConfig, InterleaveConfig, KDADiffConfig, MambaConfig,
+                                       MamformerConfig, MTPConfig)
+    arch_verify_config().to_yaml(os.path.join(HERE, "_arch_verify.yaml"))
     dense = MamformerConfig(name="Mamformer-1b", d_model=2048, n_layers=24, n_heads=16, n_kv_heads=4,
                             head_dim=128, d_ff=5632, vocab_size=64000, max_seq_len=2048,
                             mamba=MambaConfig(expand=1, d_state=128, d_conv=4, dt_rank=128),

@@ -30,6 +30,8 @@ def build_parser():
     p.add_argument("--summary_budget", type=int, default=0)
     p.add_argument("--show_thinking", action="store_true")
     p.add_argument("--bf16", action="store_true")
+    p.add_argument("--seed", type=int, default=42, help="seeds the weights of a model built without a checkpoint "
+                                                         "and the sampling")
     return p
 
 
@@ -59,6 +61,7 @@ def main(argv=None):
     import torch
     from mamformer_b200.tokenizer import MamformerTokenizer
     args = build_parser().parse_args(argv)
+    torch.manual_seed(args.seed)
     model, cfg = _common.load_model(args.config, args.checkpoint, args.device,
                                     torch.bfloat16 if args.bf16 else None)
     tok = MamformerTokenizer()

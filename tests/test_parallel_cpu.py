@@ -128,3 +128,26 @@ def test_dp_slice_bounds_partition():
                     sl = C.dp_slice(lo, hi, P)
                     assert s0 == min(hi, lo + q * sl)
             assert covered == list(range(lo, hi))
+
+
+def test_ep_engine_capacity_and_overflow_bookkeeping():
+    """Host side of the expert-parallel capacity protocol: buffer sizes, when a step can
+    overflow, and what a detected overflow does (restore the routing state, raise the factor)."""
+    import types
+    from mamformer_b200.parallel.expert_parallel import EPEngine, ExpertParallelGroup
+    eng = EPEngine(ExpertParallelGroup(ep_size=8, ep_rank=3), capacity_factor=2.0)
+    assert eng.can_overflow
+    assert eng.capacity(1000, 16) == 3072                     # ceil(2 * 1000) + 64 * 16 -> 128-aligned
+    assert not EPEngine(ExpertParallelGroup(ep_size=2, ep_rank=0), capacity_factor=2.0).can_overflow
+    assert EPEngine(ExpertParallelGroup(ep_size=4, ep_rank=0), capacity_factor=8.0).capacity(1000, 16) == \
+        (4 * 1000 + 64 * 16 + 127) // 128 * 128                # never more than P * T * k rows needed
+    bias = torch.tensor([0.5, -0.5])
+    eng._snapshot = [(bias, torch.tensor([0.0, 0.0]))]
+    eng._stage = types.SimpleNamespace(rows_x=1000)
+    eng._status_event = types.SimpleNamespace(synchronize=lambda: None)
+    eng._status_host = torch.tensor([0, 1234], dtype=torch.int32)
+    assert not eng.step_overflowed() and eng.capacity_factor == 2.0
+    eng._status_host = torch.tensor([1, 5000], dtype=torch.int32)
+    assert eng.step_overflowed()
+    assert torch.equal(bias, torch.zeros(2))                  # routing state of the step restored
+    assert eng.capacity_factor == 6.25 and eng.overflow_steps == 1

@@ -144,8 +144,8 @@ def test_data_pipeline_and_thinking_generation_cpu(tmp_path):
     _run(["scripts/data_pipeline.py", "--input", str(src), "--output", str(tmp_path / "out")])
     assert any((tmp_path / "out").rglob("*")), "data pipeline wrote nothing"
     r = _run(["scripts/generate.py", "--config", "debug", "--prompt", "2+2?", "--max_new_tokens", "8",
-              "--thinking", "FastThink", "--temperature", "0"])
-    assert r.stdout.strip() != ""
+              "--thinking", "FastThink", "--temperature", "0", "--show_thinking", "--seed", "0"])
+    assert r.stdout.strip() != ""          # the control tokens of the thinking phases are shown
 
 
 def test_profile_kda_ablations_change_the_layer_stack():
@@ -176,3 +176,10 @@ def test_gen_1b_ultra_config_writes_the_file(tmp_path):
     assert cfg.layout_string().endswith("FF") and cfg.mtp.depth == 2
     committed = MamformerConfig.from_yaml(os.path.join(ROOT, "configs", "_1b_ultra.yaml"))
     assert committed.to_dict() == cfg.to_dict()
+
+
+def test_gen_arch_config_writes_the_committed_file(tmp_path):
+    out = tmp_path / "_arch_verify.yaml"
+    _run(["scripts/gen_arch_config.py", "--out", str(out)])
+    import yaml
+    assert yaml.safe_load(out.read_text()) == yaml.safe_load(open(os.path.join(ROOT, "configs", "_arch_verify.yaml")))
