@@ -51,10 +51,10 @@ def _args():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-launches", type=int, default=1)
-    ap.add_argument("--dp-transport", default="nccl", choices=["p2p", "nccl"],
-                    help="N > 1: dense-gradient all-reduce by NCCL (default; validated up to 8 ranks) or "
-                         "by this repository's peer-memory path (p2p: 0.145 ms vs 0.155 ms for NCCL per "
-                         "64 MiB bucket on 2 GPUs; equal step time, the reduction is overlapped)")
+    ap.add_argument("--dp-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: dense-gradient all-reduce by this repository's peer-memory path (default: "
+                         "copy-engine pulls of symmetric-memory gradient buckets, overlapped with the last "
+                         "backward; run at 2 and 8 GPUs) or by NCCL")
     ap.add_argument("--profile-table", type=int, default=0,
                     help="print the top-N kernels of one extra step by device time (torch profiler, for "
                          "ranking only; never a timed number) to stderr")
