@@ -73,6 +73,11 @@ at::Tensor expert_histogram(at::Tensor idx, int64_t E);
 std::vector<at::Tensor> flash_tc_fwd(at::Tensor q1, c10::optional<at::Tensor> q2, at::Tensor k, at::Tensor v,
                                      c10::optional<at::Tensor> lam, int64_t lo, int64_t hi, double scale);
 int64_t flash_tc_error();
+std::vector<at::Tensor> flash_tc_bwd(at::Tensor q1, c10::optional<at::Tensor> q2, at::Tensor k, at::Tensor v,
+                                     at::Tensor o1, c10::optional<at::Tensor> o2, at::Tensor lse1,
+                                     c10::optional<at::Tensor> lse2, at::Tensor dout, c10::optional<at::Tensor> coef,
+                                     int64_t lo, int64_t hi, double scale);
+int64_t flash_tc_bwd_error();
 std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, int64_t lo, int64_t hi, double scale);
 std::vector<at::Tensor> flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out, at::Tensor lse,
                                        at::Tensor dout, int64_t lo, int64_t hi, double scale);
@@ -134,6 +139,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("expert_histogram", &mamf::expert_histogram);
   m.def("flash_tc_fwd", &mamf::flash_tc_fwd);
   m.def("flash_tc_error", &mamf::flash_tc_error);
+  m.def("flash_tc_bwd", &mamf::flash_tc_bwd);
+  m.def("flash_tc_bwd_error", &mamf::flash_tc_bwd_error);
   m.def("flash_attn_fwd", &mamf::flash_attn_fwd);
   m.def("flash_attn_bwd", &mamf::flash_attn_bwd);
   m.def("gemm_ag", &mamf::gemm_ag);

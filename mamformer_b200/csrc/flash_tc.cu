@@ -29,9 +29,7 @@
 // below 2^8 and most tiles need no rescale.
 // Every wait is bounded (clock64); a timeout records a code in g_mamf_fa5_err, stops the CTA's
 // work, waits a bounded time for its TMA copies, frees TMEM and returns.
-#include "common.cuh"
-
-#include <cudaTypedefs.h>
+#include "tc5.cuh"
 
 namespace mamf {
 namespace fa5 {
@@ -69,126 +67,15 @@ struct Params {
   float* lse_b;
 };
 
-// ---- PTX helpers -----------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
-}
-__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-               : "=r"(ok) : "r"(su32(b)), "r"(parity) : "memory");
-  return ok != 0;
-}
+// ---- PTX helpers (csrc/tc5.cuh) -----------------------------------------------------------------
+using namespace tc5;
 // Bounded wait; false on timeout (code recorded) or when another role already failed.
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int code) {
-  if (bar_try(b, parity)) return true;
-  const long long t0 = clock64();
-  while (true) {
-    if (bar_try(b, parity)) return true;
-    if (*((volatile int*)&g_mamf_fa5_err) != 0) return false;
-    if (clock64() - t0 > WAIT_CYCLES) { atomicCAS(&g_mamf_fa5_err, 0, code); return false; }
-  }
+  return tc5::bar_wait(b, parity, code, &g_mamf_fa5_err, WAIT_CYCLES);
 }
-__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
-      ::"r"(su32(dst)), "l"(map), "r"(su32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
-}
-// UMMA shared-memory descriptor (sm100: version 1 at bit 46, 128-byte swizzle at bits 61-63)
-__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((addr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-// kind::f16 instruction descriptor: bf16 x bf16 -> f32, M = 128, N = n
-__host__ __device__ constexpr uint32_t idesc(int n, bool b_mn) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
-}
-__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
-  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-               ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
-}
-// A operand read from tensor memory (P), B from shared memory (V)
-__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
-  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
-               ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
-}
-__device__ __forceinline__ void commit(uint64_t* b) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tld32(uint32_t taddr, float (&r)[32]) {
-  uint32_t v[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(v[i]);
-}
-// 64 consecutive columns of this thread's TMEM lane: two loads in flight, one wait
-__device__ __forceinline__ void tld64(uint32_t taddr, float* r) {
-  uint32_t v[64];
-#define MAMF_TLD32_ASM(DST, ADDR)                                                                          \
-  asm volatile(                                                                                            \
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"     \
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                           \
-      : "=r"(DST[0]), "=r"(DST[1]), "=r"(DST[2]), "=r"(DST[3]), "=r"(DST[4]), "=r"(DST[5]), "=r"(DST[6]),   \
-        "=r"(DST[7]), "=r"(DST[8]), "=r"(DST[9]), "=r"(DST[10]), "=r"(DST[11]), "=r"(DST[12]),             \
-        "=r"(DST[13]), "=r"(DST[14]), "=r"(DST[15]), "=r"(DST[16]), "=r"(DST[17]), "=r"(DST[18]),          \
-        "=r"(DST[19]), "=r"(DST[20]), "=r"(DST[21]), "=r"(DST[22]), "=r"(DST[23]), "=r"(DST[24]),          \
-        "=r"(DST[25]), "=r"(DST[26]), "=r"(DST[27]), "=r"(DST[28]), "=r"(DST[29]), "=r"(DST[30]),          \
-        "=r"(DST[31])                                                                                      \
-      : "r"(ADDR))
-  uint32_t* lo = v;
-  uint32_t* hi = v + 32;
-  MAMF_TLD32_ASM(lo, taddr);
-  MAMF_TLD32_ASM(hi, taddr + 32u);
-#undef MAMF_TLD32_ASM
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 64; ++i) r[i] = __uint_as_float(v[i]);
-}
-__device__ __forceinline__ void tst32(uint32_t taddr, const float (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-      ::"r"(taddr), "r"(__float_as_uint(r[0])), "r"(__float_as_uint(r[1])), "r"(__float_as_uint(r[2])),
-        "r"(__float_as_uint(r[3])), "r"(__float_as_uint(r[4])), "r"(__float_as_uint(r[5])), "r"(__float_as_uint(r[6])),
-        "r"(__float_as_uint(r[7])), "r"(__float_as_uint(r[8])), "r"(__float_as_uint(r[9])), "r"(__float_as_uint(r[10])),
-        "r"(__float_as_uint(r[11])), "r"(__float_as_uint(r[12])), "r"(__float_as_uint(r[13])), "r"(__float_as_uint(r[14])),
-        "r"(__float_as_uint(r[15])), "r"(__float_as_uint(r[16])), "r"(__float_as_uint(r[17])), "r"(__float_as_uint(r[18])),
-        "r"(__float_as_uint(r[19])), "r"(__float_as_uint(r[20])), "r"(__float_as_uint(r[21])), "r"(__float_as_uint(r[22])),
-        "r"(__float_as_uint(r[23])), "r"(__float_as_uint(r[24])), "r"(__float_as_uint(r[25])), "r"(__float_as_uint(r[26])),
-        "r"(__float_as_uint(r[27])), "r"(__float_as_uint(r[28])), "r"(__float_as_uint(r[29])), "r"(__float_as_uint(r[30])),
-        "r"(__float_as_uint(r[31]))
-      : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, M = 128, N = n, A K-major
+__host__ __device__ constexpr uint32_t idesc(int n, bool b_mn) { return idesc_bf16(BM, n, false, b_mn); }
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) { mma_ss(d, a, b, id, acc); }
 
 // ---- the kernel ---------------------------------------------------------------------------------
 struct Maps { CUtensorMap qa, qb, k, v; };
@@ -487,38 +374,7 @@ __global__ void __launch_bounds__(NT, 1) fa5_fwd_kernel(const __grid_constant__ 
 }  // namespace fa5
 
 // ---- host side ------------------------------------------------------------------------------------
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeFn fa5_encode_fn() {
-  static EncodeFn fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* ptr = nullptr;
-    MAMF_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
-    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled unavailable");
-    fn = reinterpret_cast<EncodeFn>(ptr);
-  }
-  return fn;
-}
-
-// (B, L, heads, 128) bf16 -> 3-D map (dim, head, B*L rows), box 64 dims x 1 head x `rows` rows.
-static CUtensorMap fa5_map(const at::Tensor& t, uint32_t rows) {
-  TORCH_CHECK(t.is_contiguous() && t.dim() == 4 && t.size(3) == fa5::HD && t.scalar_type() == at::kBFloat16,
-              "tcgen05 attention: contiguous bf16 (B, L, heads, 128) tensors");
-  TORCH_CHECK(aligned16(t.data_ptr()), "tcgen05 attention: 16-byte aligned base");
-  const int64_t heads = t.size(2);
-  CUtensorMap m;
-  cuuint64_t gd[3] = {(cuuint64_t)fa5::HD, (cuuint64_t)heads, (cuuint64_t)(t.size(0) * t.size(1))};
-  cuuint64_t gs[2] = {(cuuint64_t)fa5::HD * 2, (cuuint64_t)(heads * fa5::HD * 2)};
-  cuuint32_t bx[3] = {64u, 1u, rows}, es[3] = {1, 1, 1};
-  CUresult r = fa5_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), gd, gs, bx, es,
-                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (attention) failed: ", (int)r);
-  return m;
-}
+static CUtensorMap fa5_map(const at::Tensor& t, uint32_t rows) { return tc5_head_map(t, rows, "tcgen05 attention"); }
 
 // Differential mode: q1, q2 (B, S, H, 128), k, v (B, Skv, G, 128), lam (H,) fp32.
 //   returns (out, o1, o2, lse1, lse2, od): out = (o1 - lam o2) / (1 - lam + 1e-8), o1 / o2 the

@@ -294,13 +294,21 @@ class _FlashAttn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse = ctx.saved_tensors
-        dq, dk, dv = _C.flash_attn_bwd(q, k, v, out, lse, dout.to(q.dtype).contiguous(), *ctx.args)
-        return dq, dk, dv, None, None, None
+        return (*_attn_bwd(q, k, v, out, lse, dout, ctx.args), None, None, None)
+
+
+def _attn_bwd(q, k, v, out, lse, dout, args):
+    """(dq, dk, dv) of softmax attention: the tcgen05 backward (csrc/flash_tc_bwd.cu) at head_dim
+    128 in bf16, else the mma.sync kernels of csrc/flash_attn.cu."""
+    dout = dout.to(q.dtype).contiguous()
+    if _tc_bwd_ok(q, k):
+        return tuple(_C.flash_tc_bwd(q, None, k, v, out, None, lse, None, dout, None, *args))
+    return tuple(_C.flash_attn_bwd(q, k, v, out, lse, dout, *args))
 
 
 class _FlashTCPair(torch.autograd.Function):
     """GQA attention with the forward on the tcgen05 kernel (two query heads of one KV head per
-    CTA, csrc/flash_tc.cu) and the backward on csrc/flash_attn.cu's kernels."""
+    CTA, csrc/flash_tc.cu) and the backward on the tcgen05 backward (csrc/flash_tc_bwd.cu)."""
 
     @staticmethod
     def forward(ctx, q, k, v, lo, hi, scale):
@@ -312,16 +320,16 @@ class _FlashTCPair(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse = ctx.saved_tensors
-        dq, dk, dv = _C.flash_attn_bwd(q, k, v, out, lse, dout.to(q.dtype).contiguous(), *ctx.args)
-        return dq, dk, dv, None, None, None
+        return (*_attn_bwd(q, k, v, out, lse, dout, ctx.args), None, None, None)
 
 
 class _DiffFlashTC(torch.autograd.Function):
     """Differential attention: one tcgen05 forward for both softmax maps (shared K / V stream,
-    lambda combine in the epilogue); backward = the flash backward of each map with
-    dO1 = dout / (1 - lam + 1e-8), dO2 = -lam dout / (1 - lam + 1e-8), and
+    lambda combine in the epilogue); backward = one tcgen05 backward over both maps (shared K / V,
+    dK and dV of the two maps summed in tensor memory) with dO1 = dout / (1 - lam + 1e-8) and
+    dO2 = -lam dout / (1 - lam + 1e-8) applied as per-head factors inside the kernel, and
     d lam = sum dout . (o1 - (1 + 1e-8) o2) / (1 - lam + 1e-8)^2, with o1 - o2 taken from the
-    kernel's fp32 difference (the two maps are close, so bf16 copies of each would lose it)."""
+    forward kernel's fp32 difference (the two maps are close, so bf16 copies would lose it)."""
 
     @staticmethod
     def forward(ctx, q1, q2, k, v, lam, lo, hi, scale):
@@ -337,20 +345,32 @@ class _DiffFlashTC(torch.autograd.Function):
         q1, q2, k, v, o1, o2, lse1, lse2, lam, od = ctx.saved_tensors
         den = 1.0 / (1.0 - lam + 1e-8)                               # (H,)
         d32 = dout.float()
-        do1 = (d32 * den.view(1, 1, -1, 1)).to(q1.dtype).contiguous()
-        do2 = (d32 * (-lam * den).view(1, 1, -1, 1)).to(q1.dtype).contiguous()
-        dq1, dk1, dv1 = _C.flash_attn_bwd(q1, k, v, o1, lse1, do1, *ctx.args)
-        dq2, dk2, dv2 = _C.flash_attn_bwd(q2, k, v, o2, lse2, do2, *ctx.args)
+        if _TC_BWD:
+            coef = torch.stack([den, -lam * den]).contiguous()
+            dq1, dq2, dk, dv = _C.flash_tc_bwd(q1, q2, k, v, o1, o2, lse1, lse2, dout.to(q1.dtype).contiguous(),
+                                               coef, *ctx.args)
+        else:
+            do1 = (d32 * den.view(1, 1, -1, 1)).to(q1.dtype).contiguous()
+            do2 = (d32 * (-lam * den).view(1, 1, -1, 1)).to(q1.dtype).contiguous()
+            dq1, dk1, dv1 = _C.flash_attn_bwd(q1, k, v, o1, lse1, do1, *ctx.args)
+            dq2, dk2, dv2 = _C.flash_attn_bwd(q2, k, v, o2, lse2, do2, *ctx.args)
+            dk, dv = dk1 + dk2, dv1 + dv2
         dlam = (d32 * od.float()).sum(dim=(0, 1, 3)) * den * den    # the 1e-8 o2 term is below fp32 noise
-        return dq1, dq2, dk1 + dk2, dv1 + dv2, dlam.to(ctx.lam_dtype), None, None, None
+        return dq1, dq2, dk, dv, dlam.to(ctx.lam_dtype), None, None, None
 
 
 _TC_ATTN = os.environ.get("MAMF_FLASH_TC", "1") != "0"
+# MAMF_FLASH_TC_BWD=0 keeps the tcgen05 forward but runs the backward on csrc/flash_attn.cu
+_TC_BWD = _TC_ATTN and os.environ.get("MAMF_FLASH_TC_BWD", "1") != "0"
 
 
 def _tc_ok(q, k):
     return (_TC_ATTN and q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and q.shape[-1] == 128
             and k.shape[-1] == 128 and q.shape[2] % k.shape[2] == 0 and q.shape[1] <= k.shape[1])
+
+
+def _tc_bwd_ok(q, k):
+    return _TC_BWD and _tc_ok(q, k)
 
 
 def _fa_ok(q, k):
@@ -364,7 +384,7 @@ def flash_attention(q, k, v, lo=-_BIG, hi=0, scale=None):
     return _FlashAttn.apply(q.contiguous(), k.contiguous(), v.contiguous(), lo, hi, scale)
 
 
-@_register("attention", "csrc/flash_tc.cu + csrc/flash_attn.cu")
+@_register("attention", "csrc/flash_tc.cu + csrc/flash_tc_bwd.cu + csrc/flash_attn.cu")
 def attention(q, k, v, lo, hi):
     if not _fa_ok(q, k):
         from mamformer_b200.ops import reference
@@ -374,7 +394,7 @@ def attention(q, k, v, lo, hi):
     return flash_attention(q, k, v, lo, hi)
 
 
-@_register("diff_attention", "csrc/flash_tc.cu + csrc/flash_attn.cu")
+@_register("diff_attention", "csrc/flash_tc.cu + csrc/flash_tc_bwd.cu + csrc/flash_attn.cu")
 def diff_attention(q1, q2, k, v, lam, lo, hi, scale=None):
     """(softmax(q1 k^T s) - lam softmax(q2 k^T s)) v / (1 - lam): at head_dim 128 one tcgen05
     forward over a shared K / V stream; otherwise two flash passes combined."""

@@ -169,6 +169,26 @@ def case_flash_tc(B=1, S=4096, H=32, G=8, hd=128, diff=False):
     return (lambda: _C.flash_tc_fwd(q, None, k, v, None, lo, hi, scale)), flops, 0
 
 
+def case_flash_tc_bwd(B=1, S=4096, H=32, G=8, hd=128, diff=False):
+    """tcgen05 flash backward (csrc/flash_tc_bwd.cu), causal, 32 query / 8 KV heads; the
+    differential form runs both maps in one launch (shared K / V, dK / dV summed in TMEM).
+    FLOPs: 2.5 x the forward's (S^T, dP^T, dV, dK, dQ products vs S and PV)."""
+    from mamformer_b200.ops.native import _C
+    mk = lambda h: (torch.randn(B, S, h, hd, device="cuda") * 0.5).bfloat16()  # noqa: E731
+    q, q2, k, v = mk(H), mk(H), mk(G), mk(G)
+    lo, hi, scale = -(1 << 30), 0, hd ** -0.5
+    flops = 2.5 * 4.0 * B * H * S * S * hd / 2 * (2 if diff else 1)
+    if diff:
+        lam = torch.full((H,), 0.5, device="cuda")
+        out, o1, o2, l1, l2, _ = _C.flash_tc_fwd(q, q2, k, v, lam, lo, hi, scale)
+        dout = torch.randn_like(out)
+        coef = torch.stack([1 / (1 - lam), -lam / (1 - lam)])
+        return (lambda: _C.flash_tc_bwd(q, q2, k, v, o1, o2, l1, l2, dout, coef, lo, hi, scale)), flops, 0
+    out, lse = _C.flash_tc_fwd(q, None, k, v, None, lo, hi, scale)
+    dout = torch.randn_like(out)
+    return (lambda: _C.flash_tc_bwd(q, None, k, v, out, None, lse, None, dout, None, lo, hi, scale)), flops, 0
+
+
 def case_router(T=4096, E=128, k=8):
     """Router top-k + softmax over the selected scores + per-expert histogram."""
     from mamformer_b200.ops.native import _C
@@ -176,12 +196,71 @@ def case_router(T=4096, E=128, k=8):
     return (lambda: _C.router_topk(scores, k)), 0.0, T * E * 4 + T * k * 12
 
 
+def case_rmsnorm(T=16384, d=4096, backward=False):
+    """RMSNorm over 4 micro-batch sequences of 4096 tokens at d_model 4096 (bf16 in / out)."""
+    from mamformer_b200.ops.native import _C
+    x = torch.randn(T, d, device="cuda").bfloat16()
+    w = torch.ones(d, device="cuda")
+    if not backward:
+        return (lambda: _C.rmsnorm_fwd(x, w, 1e-6)), 0.0, 2 * T * d * 2 + T * 4
+    _, rstd = _C.rmsnorm_fwd(x, w, 1e-6)
+    dy = torch.randn_like(x)
+    return (lambda: _C.rmsnorm_bwd(x, w, dy, rstd)), 0.0, 3 * T * d * 2 + T * 4
+
+
+def case_swiglu(T=16384, I=4608, backward=False):
+    """SwiGLU of the two shared experts (intermediate 2 x 2304) over 16384 tokens."""
+    from mamformer_b200.ops.native import _C
+    g, u = (torch.randn(T, I, device="cuda").bfloat16() for _ in range(2))
+    if not backward:
+        return (lambda: _C.swiglu_fwd(g, u)), 0.0, 3 * T * I * 2
+    dy = torch.randn_like(g)
+    return (lambda: _C.swiglu_bwd(g, u, dy)), 0.0, 5 * T * I * 2
+
+
+def case_rope(B=4, S=4096, H=32, hd=128):
+    """Rotary embedding of the 32 query heads (fp32 cos / sin tables of S x hd/2)."""
+    from mamformer_b200.ops.native import _C
+    x = torch.randn(B, S, H, hd, device="cuda").bfloat16()
+    ang = torch.arange(S, device="cuda")[:, None] * torch.rand(hd // 2, device="cuda")[None]
+    c, s = ang.cos(), ang.sin()
+    return (lambda: _C.rope_apply(x, c, s, False)), 0.0, 2 * x.numel() * 2 + 2 * c.numel() * 4
+
+
+def case_conv(B=4, S=4096, C=8192, K=4, backward=False):
+    """Causal depthwise conv (width 4) + SiLU of the Mamba block, d_inner 8192."""
+    from mamformer_b200.ops.native import _C
+    x = torch.randn(B, S, C, device="cuda").bfloat16()
+    w = torch.randn(C, K, device="cuda") * 0.3
+    if not backward:
+        return (lambda: _C.conv_silu_fwd(x, w)), 0.0, 2 * x.numel() * 2
+    dy = torch.randn_like(x)
+    return (lambda: _C.conv_silu_bwd(x, w, dy)), 0.0, 3 * x.numel() * 2
+
+
+def case_groupnorm(B=4, S=4096, H=32, hd=128, backward=False):
+    """Per-head GroupNorm of the KDA-Diff output (32 heads of 128 per token)."""
+    from mamformer_b200.ops.native import _C
+    x = torch.randn(B, S, H * hd, device="cuda").bfloat16()
+    w, b = torch.ones(H * hd, device="cuda"), torch.zeros(H * hd, device="cuda")
+    if not backward:
+        return (lambda: _C.head_groupnorm_fwd(x, H, w, b, 1e-5)), 0.0, 2 * x.numel() * 2
+    _, mr = _C.head_groupnorm_fwd(x, H, w, b, 1e-5)
+    dy = torch.randn_like(x)
+    return (lambda: _C.head_groupnorm_bwd(x, H, w, mr, dy)), 0.0, 3 * x.numel() * 2
+
+
 CASES = {"gemm": case_gemm, "grouped": case_grouped, "wgrad": case_wgrad, "scan": case_scan,
          "scan_bwd": lambda: case_scan(backward=True), "linear_attn": case_linear_attn,
          "linear_attn_bwd": lambda: case_linear_attn(backward=True), "ce": case_ce, "moe": case_moe,
          "adamw": case_adamw, "flash_attn": case_flash_attn,
          "flash_attn_bwd": lambda: case_flash_attn(backward=True), "router": case_router,
-         "flash_tc": case_flash_tc, "flash_tc_diff": lambda: case_flash_tc(diff=True)}
+         "flash_tc": case_flash_tc, "flash_tc_diff": lambda: case_flash_tc(diff=True),
+         "flash_tc_bwd": case_flash_tc_bwd, "flash_tc_diff_bwd": lambda: case_flash_tc_bwd(diff=True),
+         "rmsnorm": case_rmsnorm, "rmsnorm_bwd": lambda: case_rmsnorm(backward=True),
+         "swiglu": case_swiglu, "swiglu_bwd": lambda: case_swiglu(backward=True), "rope": case_rope,
+         "conv": case_conv, "conv_bwd": lambda: case_conv(backward=True), "groupnorm": case_groupnorm,
+         "groupnorm_bwd": lambda: case_groupnorm(backward=True)}
 
 
 def run(op: str, iters: int = 20, once: bool = False) -> dict:

@@ -53,10 +53,17 @@ def test_nonfinite_grad_skip():
         assert torch.equal(p.detach(), before[n]), n
 
 
+def _flush(q):
+    """os._exit skips the queue's feeder thread: hand the pending items to the pipe first."""
+    q.close()
+    q.join_thread()
+
+
 def _hb_worker(rank, world, port, q):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    result, code = None, 0
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world)
         hb = Heartbeat(stale_after_s=5.0)
@@ -69,18 +76,19 @@ def _hb_worker(rank, world, port, q):
         dist.barrier()
         try:
             hb.check()
-            q.put((rank, "no failure detected"))
+            result = "no failure detected"
         except RankFailureError as e:
-            q.put((rank, "ok" if "rank 1 failed" in str(e) else str(e)))
+            result = "ok" if "rank 1 failed" in str(e) else str(e)
         # stale detection: rank 1's beat is old relative to a clock far in the future
         try:
             hb.check(now=1e12)
-        except RankFailureError as e:
+        except RankFailureError:
             pass
-        os._exit(0)
     except Exception as e:
-        q.put((rank, repr(e)))
-        os._exit(1)
+        result, code = repr(e), 1
+    q.put((rank, result))
+    _flush(q)
+    os._exit(code)
 
 
 def test_heartbeat_detects_failed_rank():

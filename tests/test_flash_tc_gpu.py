@@ -1,7 +1,8 @@
-"""tcgen05 flash-attention forward (csrc/flash_tc.cu) against fp32 PyTorch references of the same
-op: differential attention (output and the gradients dq1, dq2, dk, dv, d lambda, whose backward
-runs the flash backward kernels on the saved per-map outputs / log-sum-exps) and GQA head pairs,
-for causal, windowed and look-ahead bands, ragged sequence lengths and several KV groupings."""
+"""tcgen05 flash attention (forward csrc/flash_tc.cu, backward csrc/flash_tc_bwd.cu) against fp32
+PyTorch references of the same op: differential attention (output and the gradients dq1, dq2, dk,
+dv, d lambda; one backward launch over both maps with the per-head dout factors applied inside the
+kernel), GQA head pairs and single heads, for causal, windowed and look-ahead bands, ragged
+sequence lengths, key sequences longer than the queries and several KV groupings."""
 
 import pytest
 import torch
@@ -54,6 +55,7 @@ def test_diff_forward_and_grads_match_fp32(B, S, H, G, band):
     tols = {"dq1": 3e-2, "dq2": 3e-2, "dk": 3e-2, "dv": 3e-2, "dlam": 6e-2}
     for name, a, b in zip(["dq1", "dq2", "dk", "dv", "dlam"], leaves, rl):
         assert _rel(a.grad, b.grad, GFLOOR) < tols[name], (name, _rel(a.grad, b.grad, GFLOOR))
+    assert C.flash_tc_bwd_error() == 0
 
 
 @pytest.mark.parametrize("B,S,H,G", [(1, 256, 4, 2), (2, 333, 8, 2), (1, 512, 8, 1)])
@@ -72,6 +74,65 @@ def test_gqa_pair_forward_and_grads_match_fp32(B, S, H, G, band):
     (want * dout).sum().backward()
     for name, a, b in zip(["dq", "dk", "dv"], leaves, rl):
         assert _rel(a.grad, b.grad, GFLOOR) < 3e-2, (name, _rel(a.grad, b.grad, GFLOOR))
+    import mamformer_b200._C as C
+    assert C.flash_tc_bwd_error() == 0
+
+
+@pytest.mark.parametrize("B,S,Skv,H,G", [(1, 200, 200, 6, 2), (2, 190, 320, 4, 4), (1, 64, 64, 3, 1)])
+@pytest.mark.parametrize("band", BANDS)
+def test_single_head_backward_matches_fp32(B, S, Skv, H, G, band):
+    """Odd query heads per KV head (the mma.sync forward) and keys longer than the queries
+    (queries aligned to the end of the keys): gradients from the tcgen05 backward."""
+    from mamformer_b200.ops import native
+    import mamformer_b200._C as C
+    lo, hi = band
+    q, _, k, v = _qkv(B, S, H, G, seed=S + 3 * Skv + H, Skv=Skv)
+    leaves = [t.clone().requires_grad_() for t in (q, k, v)]
+    out = native._FlashAttn.apply(*leaves, lo, hi, 128 ** -0.5)
+    rl = [t.detach().float().clone().requires_grad_() for t in (q, k, v)]
+    want = ref.attention_band(*rl, lo, hi)
+    assert _rel(out, want) < 2e-2, _rel(out, want)
+    dout = torch.randn_like(want)
+    (out.float() * dout).sum().backward()
+    (want * dout).sum().backward()
+    for name, a, b in zip(["dq", "dk", "dv"], leaves, rl):
+        assert _rel(a.grad, b.grad, GFLOOR) < 3e-2, (name, _rel(a.grad, b.grad, GFLOOR))
+    assert C.flash_tc_bwd_error() == 0
+
+
+def test_backward_of_rows_without_keys_is_zero():
+    import mamformer_b200._C as C
+    q, _, k, v = _qkv(1, 128, 2, 1, seed=5)
+    q2 = torch.cat([q, q], 2)                      # two query heads on one KV head (pair mode)
+    out, lse = C.flash_tc_fwd(q2, None, k, v, None, 1000, 2000, 128 ** -0.5)
+    dq, dk, dv = C.flash_tc_bwd(q2, None, k, v, out, None, lse, None, torch.randn_like(out), None, 1000, 2000,
+                                128 ** -0.5)
+    torch.cuda.synchronize()
+    assert C.flash_tc_bwd_error() == 0
+    assert torch.count_nonzero(dq) == 0 and torch.count_nonzero(dk) == 0 and torch.count_nonzero(dv) == 0
+
+
+def test_diff_backward_matches_two_single_map_backwards():
+    """The fused two-map backward equals the sum of two single-map tcgen05 backwards run with
+    dO1 = c1 dout and dO2 = c2 dout (to bf16 rounding of the dout factors)."""
+    import mamformer_b200._C as C
+    q1, q2, k, v = _qkv(2, 320, 8, 2, seed=21)
+    lam = torch.linspace(0.1, 0.7, 8, device="cuda")
+    lo, hi, sc = -BIG, 0, 128 ** -0.5
+    out, o1, o2, lse1, lse2, od = C.flash_tc_fwd(q1, q2, k, v, lam, lo, hi, sc)
+    dout = torch.randn_like(out)
+    den = 1.0 / (1.0 - lam + 1e-8)
+    coef = torch.stack([den, -lam * den])
+    dq1, dq2, dk, dv = C.flash_tc_bwd(q1, q2, k, v, o1, o2, lse1, lse2, dout, coef, lo, hi, sc)
+    do1 = (dout.float() * den.view(1, 1, -1, 1)).bfloat16()
+    do2 = (dout.float() * (-lam * den).view(1, 1, -1, 1)).bfloat16()
+    a1, ak1, av1 = C.flash_tc_bwd(q1, None, k, v, o1, None, lse1, None, do1, None, lo, hi, sc)
+    a2, ak2, av2 = C.flash_tc_bwd(q2, None, k, v, o2, None, lse2, None, do2, None, lo, hi, sc)
+    torch.cuda.synchronize()
+    assert C.flash_tc_bwd_error() == 0
+    assert _rel(dq1, a1, GFLOOR) < 2e-2 and _rel(dq2, a2, GFLOOR) < 2e-2
+    assert _rel(dk, ak1.float() + ak2.float(), GFLOOR) < 2e-2
+    assert _rel(dv, av1.float() + av2.float(), GFLOOR) < 2e-2
 
 
 def test_rows_without_keys_give_zero_and_infinite_lse():
