@@ -27,9 +27,9 @@
 //   warps 8-11  dQ epilogue (thread = head dimension): read dQ^T from TMEM and add it to the fp32
 //               dQ accumulator (B, H, S, 128) with fp32 reductions at L2 (one 128-byte line per
 //               warp instruction: the 32 lanes are 32 consecutive dimensions of one query);
-//   warp 12     producer: TMA loads of K / V once, then of Q and dO for each tile into a 2-deep
-//               ring (no multicast: every map covers this GPU's memory only), and the tile's
-//               {L, D} rows copied to shared memory by the warp's lanes;
+//   warp 12     TMA producer (one lane): K / V once, then Q, dO and the tile's {L, D} row for
+//               each tile into a 4-deep ring (no multicast: every map covers this GPU's memory
+//               only), so tile t + 1 is loaded while tiles t - 2 .. t still hold their stages;
 //   warp 13     TMEM allocator + MMA issuer (one lane).
 // MMAs per tile (M 128): S^T = K Q^T and dP^T = V dO^T (N 64, K 128, both operands K-major);
 // dQ^T = K^T dS^T (N 64, K 128 keys; A = the K tile read MN-major, B = dS^T from shared memory);
@@ -41,7 +41,11 @@
 // tile overlaps the tile's last two products, and a region is reused (S^T of tile t + 2) only
 // after the epilogue has read dQ^T of tile t.  The tensor pipe runs one thread's MMAs in order,
 // and tcgen05.commit arrives only when every earlier MMA has completed, so a region's bf16
-// operands and the dS^T shared-memory buffer are free once the next S^T of that region is done.
+// operands are free once the next S^T of that region is done.  The single dS^T shared-memory
+// buffer is rewritten for tile t + 1 only after the dQ^T product of tile t has completed (its
+// commit barrier), which the softmax warps wait for after their exponentials.
+// Waiting threads sleep in mbarrier.try_wait (suspend-time hint) and read the error word only
+// every 64th try, so they neither take issue slots nor add an L2 round trip to a hand-off.
 // Every wait is bounded (clock64); a timeout records a code in g_mamf_fa5b_err, stops the CTA's
 // work, waits a bounded time for its copies in flight, frees TMEM and returns.  Every global
 // access computed from the tile indices is checked against its tensor's size; a bad index is
@@ -56,7 +60,7 @@ using namespace tc5;
 constexpr int BK = 128;            // keys per CTA
 constexpr int BQ = 64;             // queries per tile
 constexpr int HD = 128;            // head dim
-constexpr int QS = 2;              // Q / dO ring depth
+constexpr int QS = 4;              // Q / dO / {L, D} ring depth
 constexpr int NT = 448;            // 14 warps
 constexpr long long WAIT_CYCLES = 4000000000LL;   // ~2 s
 
@@ -69,8 +73,8 @@ constexpr int LD_BYTES = BQ * 8;          // {L * log2 e, D} of 64 queries
 constexpr int OFF_K = 0, OFF_V = KV_BYTES;
 constexpr int OFF_Q = 2 * KV_BYTES;                      // [QS]
 constexpr int OFF_DO = OFF_Q + QS * QT_BYTES;            // [QS]
-constexpr int OFF_DS = OFF_DO + QS * QT_BYTES;           // [2]
-constexpr int OFF_LD = OFF_DS + 2 * DS_BYTES;            // [QS]
+constexpr int OFF_DS = OFF_DO + QS * QT_BYTES;           // one buffer
+constexpr int OFF_LD = OFF_DS + DS_BYTES;                // [QS]
 constexpr int OFF_BAR = OFF_LD + QS * LD_BYTES;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 
@@ -78,14 +82,15 @@ struct Params {
   int B, S, Skv, H, G, off, lo, hi, Spad, nstream;
   float scale_log2;            // softmax scale * log2(e)
   float scale;                 // softmax scale (applied to dK here and to dQ by the convert pass)
-  const float2* ld;            // (nstream, B, H, Spad): {L * log2 e (+inf: no key / padding), D}
   const float* coef;           // (nstream, H) factor of dout per stream and head, or null (1)
   float* dq;                   // (nstream, B, H, Spad, HD) fp32 accumulators, zeroed
   __nv_bfloat16* dk;           // (B, Skv, G, HD)
   __nv_bfloat16* dv;
-  int64_t ld_n, dq_n, kv_n;    // element counts of ld (float2), dq, dk / dv (checked indices)
+  int64_t dq_n, kv_n;          // element counts of dq and dk / dv (checked indices)
+  int skip_dq_red;             // profiling switch (MAMF_FA5B_SKIP_DQ_RED=1): drop the dQ reductions
 };
-struct Maps { CUtensorMap q0, q1, k, v, dout; };
+// ld: the {L * log2 e (+inf: no key / padding), D} pairs as rows (stream, b, h) of 2 * Spad fp32
+struct Maps { CUtensorMap q0, q1, k, v, dout, ld; };
 
 // false (and the code recorded) when i is outside [0, n)
 __device__ __forceinline__ bool in_range(int64_t i, int64_t n, int code) {
@@ -157,37 +162,28 @@ __global__ void __launch_bounds__(NT, 1) fa5_bwd_kernel(const __grid_constant__ 
 
   if (warp == 12) {
     // ------------------------------- producer -------------------------------
-    if (ntile > 0) {
-      if (lane == 0) {
-        bar_expect_tx(kv_full, 2 * KV_BYTES);
-        for (int c = 0; c < 2; ++c) {
-          tma_3d(sm + OFF_K + c * (KV_BYTES / 2), &mp.k, kv_full, c * 64, g, b * p.Skv + k0);
-          tma_3d(sm + OFF_V + c * (KV_BYTES / 2), &mp.v, kv_full, c * 64, g, b * p.Skv + k0);
-        }
+    if (lane == 0 && ntile > 0) {
+      bar_expect_tx(kv_full, 2 * KV_BYTES);
+      for (int c = 0; c < 2; ++c) {
+        tma_3d(sm + OFF_K + c * (KV_BYTES / 2), &mp.k, kv_full, c * 64, g, b * p.Skv + k0);
+        tma_3d(sm + OFF_V + c * (KV_BYTES / 2), &mp.v, kv_full, c * 64, g, b * p.Skv + k0);
       }
       int issued = 0;
       for (int t = 0; t < ntile; ++t) {
         const int st = t % QS;
-        const bool free_ok = lane == 0 ? wait(&qd_empty[st], (uint32_t)(((t / QS) & 1) ^ 1), 31) : true;
-        if (!__shfl_sync(0xffffffffu, free_ok, 0)) break;
+        if (!wait(&qd_empty[st], (uint32_t)(((t / QS) & 1) ^ 1), 31)) break;
         const Tile tl = tile_of(t, nqt, qt0, hpg, g);
-        // {L, D} of the tile's 64 queries: two rows per lane, then one arrival (lane 0's expect_tx)
-        float2* sld = reinterpret_cast<float2*>(sm + OFF_LD + st * LD_BYTES);
-        const int64_t ld0 = (((int64_t)tl.s * p.B + b) * p.H + tl.h) * p.Spad + tl.q0;
-        for (int i = lane; i < BQ; i += 32)
-          sld[i] = in_range(ld0 + i, p.ld_n, 101) ? p.ld[ld0 + i] : make_float2(INFINITY, 0.f);
-        __syncwarp();
-        if (lane == 0) {
-          const CUtensorMap* qm = tl.s ? &mp.q1 : &mp.q0;
-          bar_expect_tx(&qd_full[st], 2 * QT_BYTES);
-          for (int c = 0; c < 2; ++c) {
-            tma_3d(sm + OFF_Q + st * QT_BYTES + c * (QT_BYTES / 2), qm, &qd_full[st], c * 64, tl.h, b * p.S + tl.q0);
-            tma_3d(sm + OFF_DO + st * QT_BYTES + c * (QT_BYTES / 2), &mp.dout, &qd_full[st], c * 64, tl.h, b * p.S + tl.q0);
-          }
+        const CUtensorMap* qm = tl.s ? &mp.q1 : &mp.q0;
+        bar_expect_tx(&qd_full[st], 2 * QT_BYTES + LD_BYTES);
+        for (int c = 0; c < 2; ++c) {
+          tma_3d(sm + OFF_Q + st * QT_BYTES + c * (QT_BYTES / 2), qm, &qd_full[st], c * 64, tl.h, b * p.S + tl.q0);
+          tma_3d(sm + OFF_DO + st * QT_BYTES + c * (QT_BYTES / 2), &mp.dout, &qd_full[st], c * 64, tl.h, b * p.S + tl.q0);
         }
+        // {L, D} of the tile's 64 queries: 128 fp32 of row (stream, b, h) from column 2 * q0
+        tma_2d(sm + OFF_LD + st * LD_BYTES, &mp.ld, &qd_full[st], 2 * tl.q0, (tl.s * p.B + b) * p.H + tl.h);
         ++issued;
       }
-      if (lane == 0 && *((volatile int*)&g_mamf_fa5b_err) != 0) {   // error exit: let the copies in flight land
+      if (*((volatile int*)&g_mamf_fa5b_err) != 0) {   // error exit: let the copies in flight land
         wait(kv_full, 0, 0);
         for (int t = 0; t < issued; ++t) wait(&qd_full[t % QS], (uint32_t)((t / QS) & 1), 0);
       }
@@ -228,7 +224,7 @@ __global__ void __launch_bounds__(NT, 1) fa5_bwd_kernel(const __grid_constant__ 
         if (!wait(&p_full[r], (uint32_t)((t >> 1) & 1), 35)) { ok = false; break; }
         fence_after();
         const uint32_t sQ = su32(sm + OFF_Q + st * QT_BYTES), sO = su32(sm + OFF_DO + st * QT_BYTES);
-        const uint32_t sDS = su32(sm + OFF_DS + r * DS_BYTES);
+        const uint32_t sDS = su32(sm + OFF_DS);
         const uint32_t reg = tmem + (uint32_t)(r * 128);
         // dQ^T (128 dims x 64 queries) = K^T dS^T over the 128 keys, into the dP^T columns
 #pragma unroll
@@ -266,39 +262,53 @@ __global__ void __launch_bounds__(NT, 1) fa5_bwd_kernel(const __grid_constant__ 
                                    wait(&qd_full[st], (uint32_t)((t / QS) & 1), 42));
       if (!ok) break;
       fence_after();
-      float sv[32], dp[32];
-      tld32x2(tl + (uint32_t)(rg * 128 + hf * 32), tl + (uint32_t)(rg * 128 + 64 + hf * 32), sv, dp);
+      // S^T first; dP^T's load stays in flight while the exponentials run
+      uint32_t sr[32], dr[32];
+      MAMF_TC5_LD32(sr, tl + (uint32_t)(rg * 128 + hf * 32));
+      tld_wait();
+      MAMF_TC5_LD32(dr, tl + (uint32_t)(rg * 128 + 64 + hf * 32));
       const float c = p.coef ? __ldg(p.coef + tt.s * p.H + tt.h) : 1.f;
-      const float2* ldv = reinterpret_cast<const float2*>(sm + OFF_LD + st * LD_BYTES) + hf * 32;
+      const float4* ld4 = reinterpret_cast<const float4*>(sm + OFF_LD + st * LD_BYTES) + hf * 16;   // {L, D} pairs
       const int qa = tt.q0 + hf * 32;                 // first query of this thread's columns
       // the whole 32 x 32 block inside the band and the key range: no per-element mask
       const bool full = key_ok && (key - (qa + 31) - p.off >= p.lo) && (key - qa - p.off <= p.hi);
       const bool mask = __any_sync(0xffffffffu, !full);
+      float pv[32], dd[32];
+#pragma unroll
+      for (int j2 = 0; j2 < 16; ++j2) {
+        const float4 L = ld4[j2];                     // {L, D} of queries 2 j2, 2 j2 + 1
+        pv[2 * j2] = ex2(fmaf(__uint_as_float(sr[2 * j2]), p.scale_log2, -L.x));   // L = +inf gives 0
+        pv[2 * j2 + 1] = ex2(fmaf(__uint_as_float(sr[2 * j2 + 1]), p.scale_log2, -L.z));
+        dd[2 * j2] = L.y;
+        dd[2 * j2 + 1] = L.w;
+      }
+      if (mask) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int d = key - (qa + j) - p.off;
+          pv[j] = (key_ok && d >= p.lo && d <= p.hi) ? pv[j] : 0.f;
+        }
+      }
+      tld_wait();
       uint32_t pk[16], dk[16];
 #pragma unroll
       for (int j2 = 0; j2 < 16; ++j2) {
-        float pe[2], de[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int j = 2 * j2 + e;
-          const float2 L = ldv[j];
-          float pv = ex2(fmaf(sv[j], p.scale_log2, -L.x));      // L = +inf (no key, padding) gives 0
-          if (mask) {
-            const int d = key - (qa + j) - p.off;
-            pv = (key_ok && d >= p.lo && d <= p.hi) ? pv : 0.f;
-          }
-          pe[e] = pv * c;
-          de[e] = pv * (dp[j] - L.y) * c;
-        }
-        pk[j2] = pack_bf16(pe[0], pe[1]);
-        dk[j2] = pack_bf16(de[0], de[1]);
+        const float p0 = pv[2 * j2] * c, p1 = pv[2 * j2 + 1] * c;
+        pk[j2] = pack_bf16(p0, p1);
+        dk[j2] = pack_bf16(p0 * (__uint_as_float(dr[2 * j2]) - dd[2 * j2]),
+                           p1 * (__uint_as_float(dr[2 * j2 + 1]) - dd[2 * j2 + 1]));
       }
       // over this warp's own S^T columns (hf*32 .. hf*32+31, already read): c P^T in the first 16,
       // c dS^T in the last 16, so the two warps sharing these lanes never overwrite each other
       tst16_nowait(tl + (uint32_t)(rg * 128 + hf * 32), pk);
       tst16_nowait(tl + (uint32_t)(rg * 128 + hf * 32 + 16), dk);
-      // c dS^T row r into shared memory (128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7))
-      uint8_t* dsrow = sm + OFF_DS + rg * DS_BYTES + r * 128;
+      // c dS^T row r into shared memory (128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7)),
+      // once the dQ^T product of the previous tile, which reads the buffer, has completed
+      if (t > 0) {
+        ok = __all_sync(0xffffffffu, wait(&dq_full[(t - 1) & 1], (uint32_t)(((t - 1) >> 1) & 1), 44));
+        if (!ok) { tst_wait(); break; }
+      }
+      uint8_t* dsrow = sm + OFF_DS + r * 128;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int ch = hf * 4 + i;
@@ -350,7 +360,7 @@ __global__ void __launch_bounds__(NT, 1) fa5_bwd_kernel(const __grid_constant__ 
       bar_arrive(&r_free[rg]);
       // rows q0 .. q0+63 of the (stream, b, h) slab; rows past S land in its padding
       const int64_t base = ((((int64_t)tt.s * p.B + b) * p.H + tt.h) * p.Spad + tt.q0) * HD + d;
-      if (in_range(base + (int64_t)(BQ - 1) * HD, p.dq_n, 103)) {
+      if (!p.skip_dq_red && in_range(base + (int64_t)(BQ - 1) * HD, p.dq_n, 103)) {
 #pragma unroll
         for (int j = 0; j < BQ; ++j) atomicAdd(p.dq + base + (int64_t)j * HD, v[j]);
       }
@@ -473,14 +483,15 @@ std::vector<at::Tensor> flash_tc_bwd(at::Tensor q1, c10::optional<at::Tensor> q2
   at::Tensor ld = at::empty({(int64_t)ns * p.B * p.H * p.Spad * 2}, f32);
   at::Tensor acc = at::zeros({(int64_t)ns * p.B * p.H * p.Spad * HD}, f32);
   at::Tensor dk = at::empty_like(k), dv = at::empty_like(v);
-  p.ld = reinterpret_cast<const float2*>(ld.data_ptr<float>());
+  mp.ld = tc5_rows_map_f32(ld.data_ptr<float>(), (int64_t)ns * p.B * p.H, 2 * (int64_t)p.Spad, 2 * BQ,
+                           "tcgen05 attention bwd");
   p.dq = acc.data_ptr<float>();
   p.dk = (__nv_bfloat16*)dk.data_ptr();
   p.dv = (__nv_bfloat16*)dv.data_ptr();
-  p.ld_n = ld.numel() / 2;
   p.dq_n = acc.numel();
   p.kv_n = dk.numel();
   const bool dbg = std::getenv("MAMF_FA5B_DEBUG") != nullptr;   // host progress marks (stderr)
+  p.skip_dq_red = std::getenv("MAMF_FA5B_SKIP_DQ_RED") != nullptr;  // timing experiments only: dq is wrong
   auto mark = [&](const char* what) {
     if (dbg) { fprintf(stderr, "[flash_tc_bwd] %s\n", what); fflush(stderr); }
   };

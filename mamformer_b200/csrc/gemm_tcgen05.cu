@@ -79,23 +79,28 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// One try; the thread is suspended until the phase completes or about 1 ms passes (suspend-time
+// hint), so waiting warps leave the issue slots to the epilogue warps.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u) : "memory");
   return ok != 0;
 }
 // Bounded wait.  Returns false (and records `code`) on timeout or if another role already failed.
+// The error word (a global load) and the clock are read every 64th unsuccessful try only.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*((volatile int*)&g_mamf_gemm_err) != 0) return false;
-    if (clock64() - t0 > WAIT_CYCLES) {
-      atomicCAS(&g_mamf_gemm_err, 0, code);
-      return false;
+    if ((n & 63u) == 0) {
+      if (*((volatile int*)&g_mamf_gemm_err) != 0) return false;
+      if (clock64() - t0 > WAIT_CYCLES) {
+        atomicCAS(&g_mamf_gemm_err, 0, code);
+        return false;
+      }
     }
   }
 }

@@ -1,8 +1,7 @@
 // tcgen05 / TMA / mbarrier building blocks shared by the attention kernels (csrc/flash_tc.cu,
 // csrc/flash_tc_bwd.cu).  Inline PTX for sm_100a:
 //   * mbarrier init / arrive / expect_tx / bounded parity wait (clock64 limit, error word);
-//   * TMA: 3-D tiled loads (no multicast: every map covers this GPU's memory only), 1-D bulk
-//     loads, bulk reduce-add stores from shared memory;
+//   * TMA: 2-D / 3-D tiled loads (no multicast: every map covers this GPU's memory only);
 //   * UMMA shared-memory descriptors (128-byte swizzle) and kind::f16 instruction descriptors;
 //   * tcgen05.mma with A from shared memory or from tensor memory, tcgen05.commit;
 //   * tcgen05.ld / st of 32 lanes x 16 / 32 / 64 columns.
@@ -27,22 +26,28 @@ __device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ void bar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
+// One try: the thread is suspended until the phase completes or about 1 ms passes (the
+// suspend-time hint), so waiting warps take no issue slots from the warps doing the work.
 __device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
   uint32_t ok;
-  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-               : "=r"(ok) : "r"(su32(b)), "r"(parity) : "memory");
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(su32(b)), "r"(parity), "r"(1000000u) : "memory");
   return ok != 0;
 }
 // Wait for the phase with the given parity to complete, for at most `limit` clock64 cycles.
-// Returns false on timeout (code recorded in *err unless a code is already there) or as soon as
-// another role of the grid has recorded an error.
+// Returns false on timeout (code recorded in *err unless a code is already there) or once
+// another role of the grid has recorded an error.  The error word is a global load (an L2 round
+// trip): it and the clock are read only every 64th unsuccessful try, so a waiting thread notices
+// a completed phase within one try_wait instead of after a global load.
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int code, int* err, long long limit) {
   if (bar_try(b, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t n = 1;; ++n) {
     if (bar_try(b, parity)) return true;
-    if (*((volatile int*)err) != 0) return false;
-    if (clock64() - t0 > limit) { atomicCAS(err, 0, code); return false; }
+    if ((n & 63u) == 0) {
+      if (*((volatile int*)err) != 0) return false;
+      if (clock64() - t0 > limit) { atomicCAS(err, 0, code); return false; }
+    }
   }
 }
 
@@ -52,19 +57,11 @@ __device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, uint64
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
       ::"r"(su32(dst)), "l"(map), "r"(su32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
 }
-// contiguous global -> shared copy; both addresses 16-byte aligned, bytes a multiple of 16
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(su32(dst)), "l"(src), "r"(bytes), "r"(su32(bar)) : "memory");
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(su32(dst)), "l"(map), "r"(su32(bar)), "r"(c0), "r"(c1) : "memory");
 }
-// global[dst .. dst + bytes) += shared[src ..) elementwise in fp32 (performed at L2)
-__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;"
-               ::"l"(dst), "r"(su32(src)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // generic-proxy shared-memory writes made visible to the async proxy (TMA / tcgen05 reads)
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -206,6 +203,22 @@ inline CUtensorMap tc5_head_map(const at::Tensor& t, uint32_t rows, const char* 
   cuuint32_t bx[3] = {64u, 1u, rows}, es[3] = {1, 1, 1};
   CUresult r = tc5_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), gd, gs, bx, es,
                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (", what, ") failed: ", (int)r);
+  return m;
+}
+
+// (rows, cols) row-major fp32 -> 2-D map, box `box_cols` x 1 row, no swizzle
+inline CUtensorMap tc5_rows_map_f32(const float* base, int64_t rows, int64_t cols, uint32_t box_cols,
+                                    const char* what) {
+  TORCH_CHECK(aligned16(base) && (cols * 4) % 16 == 0 && (box_cols * 4) % 16 == 0 && box_cols <= 256, what,
+              ": fp32 row map alignment");
+  CUtensorMap m;
+  cuuint64_t gd[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gs[1] = {(cuuint64_t)cols * 4};
+  cuuint32_t bx[2] = {box_cols, 1u}, es[2] = {1, 1};
+  CUresult r = tc5_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gd, gs, bx, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (", what, ") failed: ", (int)r);
   return m;
