@@ -108,6 +108,146 @@ __global__ void rmsnorm_bwd_dw_kernel(const T* __restrict__ x, const T* __restri
   }
 }
 
+// dw partial sums, vector form: a thread owns V consecutive columns (16-byte loads) of a slab of
+// rows (row lanes y = 0..7); block = 32 column vectors x 8 row lanes.
+template <typename T>
+__global__ void rmsnorm_bwd_dw_vec_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                          const float* __restrict__ rstd, float* __restrict__ part,
+                                          int64_t rows, int d, int rows_per_block) {
+  constexpr int V = 16 / sizeof(T);
+  const int col = (blockIdx.x * 32 + threadIdx.x) * V;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+  const int64_t r1 = min(rows, r0 + rows_per_block);
+  float acc[V];
+#pragma unroll
+  for (int k = 0; k < V; ++k) acc[k] = 0.f;
+  if (col < d)
+    for (int64_t r = r0 + threadIdx.y; r < r1; r += blockDim.y) {
+      const Vec16<T> a = ld16(x + r * d + col), g = ld16(dy + r * d + col);
+      const float rs = rstd[r];
+#pragma unroll
+      for (int k = 0; k < V; ++k) acc[k] = fmaf(to_f(g.v[k]) * rs, to_f(a.v[k]), acc[k]);
+    }
+  __shared__ float sm[8][32 * V + 1];
+#pragma unroll
+  for (int k = 0; k < V; ++k) sm[threadIdx.y][threadIdx.x * V + k] = acc[k];
+  __syncthreads();
+  const int t = threadIdx.y * 32 + threadIdx.x;          // one output column per thread
+  const int c = blockIdx.x * 32 * V + t;
+  if (t < 32 * V && c < d) {
+    float s = 0.f;
+    for (int i = 0; i < 8; ++i) s += sm[i][t];
+    part[(int64_t)blockIdx.y * d + c] = s;
+  }
+}
+
+// Block-per-row variants (256 threads, NVT 16-byte vectors per thread): a row's data is spread
+// over the whole block, so each thread holds at most 4 vectors and the SM keeps 8 rows in flight
+// (the warp-per-row kernels above hold a 4096-wide row in one warp's registers, which limits
+// occupancy to 8-16 warps per SM).  Used when d is a multiple of the vector width and d / V <= 1024.
+constexpr int RMS_BT = 256;
+
+// w[col .. col + V) as fp32 (col a multiple of V, w 16-byte aligned)
+template <int V>
+__device__ __forceinline__ void ld_w(const float* __restrict__ w, int col, float (&out)[V]) {
+#pragma unroll
+  for (int q = 0; q < V / 4; ++q) {
+    const float4 f = *reinterpret_cast<const float4*>(w + col + 4 * q);
+    out[4 * q] = f.x; out[4 * q + 1] = f.y; out[4 * q + 2] = f.z; out[4 * q + 3] = f.w;
+  }
+}
+
+template <typename T, int NVT>
+__global__ void __launch_bounds__(RMS_BT) rms_blk_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                                            T* __restrict__ y, float* __restrict__ rstd_out, int d,
+                                                            float eps) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * d;
+  Vec16<T> buf[NVT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NVT; ++i) {
+    const int col = (i * RMS_BT + threadIdx.x) * V;
+    if (col < d) {
+      buf[i] = ld16(xr + col);
+#pragma unroll
+      for (int k = 0; k < V; ++k) { const float f = to_f(buf[i].v[k]); ss = fmaf(f, f, ss); }
+    }
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / d + eps);
+  if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
+  T* yr = y + row * d;
+#pragma unroll
+  for (int i = 0; i < NVT; ++i) {
+    const int col = (i * RMS_BT + threadIdx.x) * V;
+    if (col < d) {
+      float wv[V];
+      ld_w<V>(w, col, wv);
+      Vec16<T> o;
+#pragma unroll
+      for (int k = 0; k < V; ++k) o.v[k] = from_f<T>(to_f(buf[i].v[k]) * r * wv[k]);
+      st16(yr + col, o);
+    }
+  }
+}
+
+template <typename T, int NVT>
+__global__ void __launch_bounds__(RMS_BT) rms_blk_bwd_dx_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                                               const T* __restrict__ dy, const float* __restrict__ rstd,
+                                                               T* __restrict__ dx, int d) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const float r = rstd[row];
+  Vec16<T> xb[NVT], gb[NVT];
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NVT; ++i) {
+    const int col = (i * RMS_BT + threadIdx.x) * V;
+    if (col < d) {
+      xb[i] = ld16(x + row * d + col);
+      gb[i] = ld16(dy + row * d + col);
+      float wv[V];
+      ld_w<V>(w, col, wv);
+#pragma unroll
+      for (int k = 0; k < V; ++k) dot = fmaf(to_f(gb[i].v[k]) * wv[k], to_f(xb[i].v[k]), dot);
+    }
+  }
+  dot = block_sum(dot, red) * r / d;   // mean(g * xhat) = r * mean(g * x)
+#pragma unroll
+  for (int i = 0; i < NVT; ++i) {
+    const int col = (i * RMS_BT + threadIdx.x) * V;
+    if (col < d) {
+      float wv[V];
+      ld_w<V>(w, col, wv);
+      Vec16<T> o;
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float g = to_f(gb[i].v[k]) * wv[k];
+        const float xh = to_f(xb[i].v[k]) * r;
+        o.v[k] = from_f<T>(r * (g - xh * dot));
+      }
+      st16(dx + row * d + col, o);
+    }
+  }
+}
+
+// Calls fn(std::integral_constant<int, NVT>) for the block-per-row kernels; false if d does not fit.
+template <typename T, typename F>
+static bool with_blk_nvt(int d, F&& fn) {
+  constexpr int V = 16 / sizeof(T);
+  if (d % V != 0) return false;
+  const int nv = d / V;
+  if (nv <= RMS_BT) fn(std::integral_constant<int, 1>{});
+  else if (nv <= 2 * RMS_BT) fn(std::integral_constant<int, 2>{});
+  else if (nv <= 4 * RMS_BT) fn(std::integral_constant<int, 4>{});
+  else return false;
+  return true;
+}
+
 template <typename T>
 static int rms_nv(int d) {
   constexpr int V = 16 / sizeof(T);
@@ -136,13 +276,22 @@ std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
   at::Tensor wc = w.contiguous();
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "rmsnorm_fwd", [&] {
     TORCH_CHECK((d * sizeof(scalar_t)) % 16 == 0 && aligned16(x.data_ptr()), "rmsnorm: d*elt must be a multiple of 16 bytes");
-    const int blocks = (int)((rows + 7) / 8);
-    with_nv(rms_nv<scalar_t>(d), [&](auto nvc) {
-      constexpr int NVV = decltype(nvc)::value;
-      rmsnorm_fwd_kernel<scalar_t, NVV><<<blocks, 256, 0, stream()>>>(
-          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(),
-          rstd.data_ptr<float>(), rows, d, (float)eps);
-    });
+    const bool blk = rows > 0 && rows <= INT32_MAX && aligned16(wc.data_ptr()) &&
+                     with_blk_nvt<scalar_t>(d, [&](auto nc) {
+                       constexpr int NVT = decltype(nc)::value;
+                       rms_blk_fwd_kernel<scalar_t, NVT><<<(unsigned)rows, RMS_BT, 0, stream()>>>(
+                           (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(),
+                           rstd.data_ptr<float>(), d, (float)eps);
+                     });
+    if (!blk) {
+      const int blocks = (int)((rows + 7) / 8);
+      with_nv(rms_nv<scalar_t>(d), [&](auto nvc) {
+        constexpr int NVV = decltype(nvc)::value;
+        rmsnorm_fwd_kernel<scalar_t, NVV><<<blocks, 256, 0, stream()>>>(
+            (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(),
+            rstd.data_ptr<float>(), rows, d, (float)eps);
+      });
+    }
   });
   MAMF_LAUNCH_CHECK();
   return {y, rstd};
@@ -159,17 +308,35 @@ std::vector<at::Tensor> rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, a
   const int nrb = (int)((rows + rpb - 1) / rpb);
   at::Tensor part = at::empty({nrb, d}, x.options().dtype(at::kFloat));
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "rmsnorm_bwd", [&] {
-    const int blocks = (int)((rows + 7) / 8);
-    with_nv(rms_nv<scalar_t>(d), [&](auto nvc) {
-      constexpr int NVV = decltype(nvc)::value;
-      rmsnorm_bwd_dx_kernel<scalar_t, NVV><<<blocks, 256, 0, stream()>>>(
-          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
-          rstd.data_ptr<float>(), (scalar_t*)dx.data_ptr(), rows, d);
-    });
-    dim3 grid((d + 31) / 32, nrb);
-    rmsnorm_bwd_dw_kernel<scalar_t><<<grid, dim3(32, 8), 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), rstd.data_ptr<float>(),
-        part.data_ptr<float>(), rows, d, rpb);
+    const bool blk = rows > 0 && rows <= INT32_MAX && aligned16(wc.data_ptr()) && aligned16(x.data_ptr()) &&
+                     aligned16(dy.data_ptr()) &&
+                     with_blk_nvt<scalar_t>(d, [&](auto nc) {
+                       constexpr int NVT = decltype(nc)::value;
+                       rms_blk_bwd_dx_kernel<scalar_t, NVT><<<(unsigned)rows, RMS_BT, 0, stream()>>>(
+                           (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
+                           rstd.data_ptr<float>(), (scalar_t*)dx.data_ptr(), d);
+                     });
+    if (!blk) {
+      const int blocks = (int)((rows + 7) / 8);
+      with_nv(rms_nv<scalar_t>(d), [&](auto nvc) {
+        constexpr int NVV = decltype(nvc)::value;
+        rmsnorm_bwd_dx_kernel<scalar_t, NVV><<<blocks, 256, 0, stream()>>>(
+            (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
+            rstd.data_ptr<float>(), (scalar_t*)dx.data_ptr(), rows, d);
+      });
+    }
+    constexpr int V = 16 / sizeof(scalar_t);
+    if (d % V == 0 && aligned16(x.data_ptr()) && aligned16(dy.data_ptr())) {
+      dim3 grid((d / V + 31) / 32, nrb);
+      rmsnorm_bwd_dw_vec_kernel<scalar_t><<<grid, dim3(32, 8), 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), rstd.data_ptr<float>(),
+          part.data_ptr<float>(), rows, d, rpb);
+    } else {
+      dim3 grid((d + 31) / 32, nrb);
+      rmsnorm_bwd_dw_kernel<scalar_t><<<grid, dim3(32, 8), 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), rstd.data_ptr<float>(),
+          part.data_ptr<float>(), rows, d, rpb);
+    }
   });
   MAMF_LAUNCH_CHECK();
   return {dx, part.sum(0)};
@@ -278,6 +445,38 @@ __global__ void rope_kernel(const T* __restrict__ x, T* __restrict__ y, const fl
   }
 }
 
+// Vectorised form: one block per token row (b, s); a thread rotates V consecutive pairs
+// (j .. j+V-1, j+half .. j+half+V-1) of one head with 16-byte loads, the row's cos / sin read as
+// float4.  Needs half % V == 0 and 16-byte aligned rows.
+template <typename T>
+__global__ void rope_vec_kernel(const T* __restrict__ x, T* __restrict__ y, const float* __restrict__ cs,
+                                const float* __restrict__ sn, int S, int H, int hd, int64_t xs, float sign) {
+  constexpr int V = 16 / sizeof(T);
+  const int half = hd / 2, nv = half / V;
+  const int64_t bs = blockIdx.x;
+  const int s = (int)(bs % S);
+  const T* xr = x + bs * xs;
+  T* yr = y + bs * (int64_t)H * hd;
+  const float* cr = cs + (int64_t)s * half;
+  const float* sr = sn + (int64_t)s * half;
+  for (int e = threadIdx.x; e < H * nv; e += blockDim.x) {
+    const int h = e / nv, j = (e - h * nv) * V;
+    const Vec16<T> a = ld16(xr + h * hd + j), b = ld16(xr + h * hd + half + j);
+    float c[V], sv[V];
+    ld_w<V>(cr, j, c);
+    ld_w<V>(sr, j, sv);
+    Vec16<T> oa, ob;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float x1 = to_f(a.v[k]), x2 = to_f(b.v[k]), si = sign * sv[k];
+      oa.v[k] = from_f<T>(x1 * c[k] - x2 * si);
+      ob.v[k] = from_f<T>(x2 * c[k] + x1 * si);
+    }
+    st16(yr + h * hd + j, oa);
+    st16(yr + h * hd + half + j, ob);
+  }
+}
+
 at::Tensor rope_apply(at::Tensor x, at::Tensor cos, at::Tensor sin, bool inverse) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(x.dim() == 4, "rope: x must be (B, S, H, hd)");
@@ -288,6 +487,17 @@ at::Tensor rope_apply(at::Tensor x, at::Tensor cos, at::Tensor sin, bool inverse
   TORCH_CHECK(cc.size(0) == S && cc.size(1) == hd / 2, "rope: table shape");
   at::Tensor y = at::empty({B, S, H, hd}, x.options());
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "rope", [&] {
+    constexpr int V = 16 / sizeof(scalar_t);
+    const int64_t rows = (int64_t)B * S;
+    if ((hd / 2) % V == 0 && aligned16(x.data_ptr()) && (x.stride(1) * sizeof(scalar_t)) % 16 == 0 &&
+        aligned16(cc.data_ptr()) && aligned16(ss.data_ptr()) && rows > 0 && rows <= INT32_MAX) {
+      const int work = H * (hd / 2 / V);
+      const int threads = std::min(256, (work + 31) / 32 * 32);
+      rope_vec_kernel<scalar_t><<<(unsigned)rows, threads, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), (scalar_t*)y.data_ptr(), cc.data_ptr<float>(), ss.data_ptr<float>(), S, H,
+          hd, x.stride(1), inverse ? -1.f : 1.f);
+      return;
+    }
     const int64_t n = (int64_t)B * S * H * (hd / 2);
     rope_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream()>>>(
         (const scalar_t*)x.data_ptr(), (scalar_t*)y.data_ptr(), cc.data_ptr<float>(), ss.data_ptr<float>(),
@@ -375,6 +585,166 @@ __global__ void conv_silu_bwd_kernel(const T* __restrict__ x, const float* __res
   for (int k = 0; k < K; ++k) dw_part[(pidx * C + c) * K + k] = dwa[k];
 }
 
+// Vectorised forms: a thread owns CV = 4 consecutive channels (8-byte bf16 / 16-byte fp32 loads),
+// so a warp moves 256 / 512 contiguous bytes per time step.  The backward keeps a register window
+// of x[t - K + 1 .. t + K] per channel and the K pending d pre-activations, so each step loads one
+// x row and one dy row (the scalar kernel above recomputes every x tap from global memory).
+constexpr int CV = 4;
+
+template <typename T>
+__device__ __forceinline__ void ld_cv(const T* __restrict__ p, float (&o)[CV]) {
+  if constexpr (sizeof(T) == 2) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < CV; ++i) o[i] = to_f(h[i]);
+  } else {
+    const float4 f = *reinterpret_cast<const float4*>(p);
+    o[0] = to_f(f.x); o[1] = to_f(f.y); o[2] = to_f(f.z); o[3] = to_f(f.w);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st_cv(T* __restrict__ p, const float (&v)[CV]) {
+  if constexpr (sizeof(T) == 2) {
+    uint2 u;
+    T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int i = 0; i < CV; ++i) h[i] = from_f<T>(v[i]);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+template <typename T, int K>
+__global__ void conv_silu_fwd_vec_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                         T* __restrict__ y, int S, int C, int64_t xs) {
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * CV;
+  const int t0 = blockIdx.y * CONV_TT;
+  const int b = blockIdx.z;
+  if (c0 >= C) return;
+  float wk[CV][K], hist[K][CV];
+#pragma unroll
+  for (int i = 0; i < CV; ++i)
+#pragma unroll
+    for (int k = 0; k < K; ++k) wk[i][k] = w[(c0 + i) * K + k];
+#pragma unroll
+  for (int k = 0; k < K - 1; ++k) {
+    const int t = t0 - (K - 1) + k;
+    if (t >= 0) ld_cv(x + ((int64_t)b * S + t) * xs + c0, hist[k]);
+    else {
+#pragma unroll
+      for (int i = 0; i < CV; ++i) hist[k][i] = 0.f;
+    }
+  }
+  const int t1 = min(S, t0 + CONV_TT);
+  for (int t = t0; t < t1; ++t) {
+    ld_cv(x + ((int64_t)b * S + t) * xs + c0, hist[K - 1]);
+    float o[CV];
+#pragma unroll
+    for (int i = 0; i < CV; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < K; ++k) acc = fmaf(wk[i][k], hist[k][i], acc);
+      o[i] = silu_f(acc);
+    }
+    st_cv(y + ((int64_t)b * S + t) * C + c0, o);
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k)
+#pragma unroll
+      for (int i = 0; i < CV; ++i) hist[k][i] = hist[k + 1][i];
+  }
+}
+
+template <typename T, int K>
+__global__ void conv_silu_bwd_vec_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                         const T* __restrict__ dy, T* __restrict__ dx,
+                                         float* __restrict__ dw_part, int S, int C, int64_t xs) {
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * CV;
+  const int tile = blockIdx.y;
+  const int t0 = tile * CONV_TT;
+  const int b = blockIdx.z;
+  if (c0 >= C) return;
+  float wk[CV][K];
+#pragma unroll
+  for (int i = 0; i < CV; ++i)
+#pragma unroll
+    for (int k = 0; k < K; ++k) wk[i][k] = w[(c0 + i) * K + k];
+  auto ldx = [&](int t, float (&o)[CV]) {
+    if (t >= 0 && t < S) ld_cv(x + ((int64_t)b * S + t) * xs + c0, o);
+    else {
+#pragma unroll
+      for (int i = 0; i < CV; ++i) o[i] = 0.f;
+    }
+  };
+  // xw[j] = x[t - K + 1 + j], j < 2K, for the current step t
+  float xw[2 * K][CV];
+#pragma unroll
+  for (int j = 0; j < 2 * K; ++j) ldx(t0 - K + 1 + j, xw[j]);
+  // d pre-activation at time u, from the window: pre(u) = sum_k w_k x[u - K + 1 + k]
+  auto dpre = [&](int u, int j0, float (&o)[CV]) {       // x[u - K + 1] is xw[j0]
+    if (u >= S) {
+#pragma unroll
+      for (int i = 0; i < CV; ++i) o[i] = 0.f;
+      return;
+    }
+    float g[CV];
+    ld_cv(dy + ((int64_t)b * S + u) * C + c0, g);
+#pragma unroll
+    for (int i = 0; i < CV; ++i) {
+      float pre = 0.f;
+#pragma unroll
+      for (int k = 0; k < K; ++k) pre = fmaf(wk[i][k], xw[j0 + k][i], pre);
+      const float sg = sigmoid_f(pre);
+      o[i] = g[i] * sg * (1.f + pre * (1.f - sg));
+    }
+  };
+  float dp[K][CV];                                        // dp[j] = dpre(t + j)
+#pragma unroll
+  for (int k = 0; k < K; ++k) dpre(t0 + k, k, dp[k]);
+  float dwa[CV][K];
+#pragma unroll
+  for (int i = 0; i < CV; ++i)
+#pragma unroll
+    for (int k = 0; k < K; ++k) dwa[i][k] = 0.f;
+  const int t1 = min(S, t0 + CONV_TT);
+  for (int t = t0; t < t1; ++t) {
+    float o[CV];
+#pragma unroll
+    for (int i = 0; i < CV; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < K; ++k) acc = fmaf(wk[i][k], dp[K - 1 - k][i], acc);
+      o[i] = acc;
+#pragma unroll
+      for (int k = 0; k < K; ++k) dwa[i][k] = fmaf(dp[0][i], xw[k][i], dwa[i][k]);
+    }
+    st_cv(dx + ((int64_t)b * S + t) * C + c0, o);
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k)
+#pragma unroll
+      for (int i = 0; i < CV; ++i) dp[k][i] = dp[k + 1][i];
+    dpre(t + K, K, dp[K - 1]);                            // x[t + 1 .. t + K] = xw[K .. 2K - 1]
+#pragma unroll
+    for (int j = 0; j < 2 * K - 1; ++j)
+#pragma unroll
+      for (int i = 0; i < CV; ++i) xw[j][i] = xw[j + 1][i];
+    ldx(t + K + 1, xw[2 * K - 1]);
+  }
+  const int64_t pidx = ((int64_t)b * gridDim.y + tile);
+#pragma unroll
+  for (int i = 0; i < CV; ++i)
+#pragma unroll
+    for (int k = 0; k < K; ++k) dw_part[(pidx * C + c0 + i) * K + k] = dwa[i][k];
+}
+
+template <typename T>
+static bool conv_vec_ok(int C, int64_t xs, const void* x, const void* other) {
+  return C % CV == 0 && (xs * (int64_t)sizeof(T)) % (CV * sizeof(T)) == 0 &&
+         (reinterpret_cast<uintptr_t>(x) % (CV * sizeof(T))) == 0 &&
+         (reinterpret_cast<uintptr_t>(other) % (CV * sizeof(T))) == 0;
+}
+
 at::Tensor conv_silu_fwd(at::Tensor x, at::Tensor w) {
   c10::cuda::CUDAGuard guard(x.device());
   const int B = x.size(0), S = x.size(1), C = x.size(2), K = w.size(1);
@@ -384,8 +754,14 @@ at::Tensor conv_silu_fwd(at::Tensor x, at::Tensor w) {
   dim3 grid((C + 127) / 128, (S + CONV_TT - 1) / CONV_TT, B);
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "conv_silu_fwd", [&] {
     TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
-    conv_silu_fwd_kernel<scalar_t, 4><<<grid, 128, 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(), B, S, C, x.stride(1));
+    if (conv_vec_ok<scalar_t>(C, x.stride(1), x.data_ptr(), y.data_ptr())) {
+      dim3 gv((C / CV + 127) / 128, (S + CONV_TT - 1) / CONV_TT, B);
+      conv_silu_fwd_vec_kernel<scalar_t, 4><<<gv, 128, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(), S, C, x.stride(1));
+    } else {
+      conv_silu_fwd_kernel<scalar_t, 4><<<grid, 128, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (scalar_t*)y.data_ptr(), B, S, C, x.stride(1));
+    }
   });
   MAMF_LAUNCH_CHECK();
   return y;
@@ -402,9 +778,16 @@ std::vector<at::Tensor> conv_silu_bwd(at::Tensor x, at::Tensor w, at::Tensor dy)
   dim3 grid((C + 127) / 128, tiles, B);
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "conv_silu_bwd", [&] {
     TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
-    conv_silu_bwd_kernel<scalar_t, 4><<<grid, 128, 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
-        (scalar_t*)dx.data_ptr(), part.data_ptr<float>(), B, S, C, x.stride(1));
+    if (conv_vec_ok<scalar_t>(C, x.stride(1), x.data_ptr(), dy.data_ptr())) {
+      dim3 gv((C / CV + 127) / 128, tiles, B);
+      conv_silu_bwd_vec_kernel<scalar_t, 4><<<gv, 128, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
+          (scalar_t*)dx.data_ptr(), part.data_ptr<float>(), S, C, x.stride(1));
+    } else {
+      conv_silu_bwd_kernel<scalar_t, 4><<<grid, 128, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), (const scalar_t*)dy.data_ptr(),
+          (scalar_t*)dx.data_ptr(), part.data_ptr<float>(), B, S, C, x.stride(1));
+    }
   });
   MAMF_LAUNCH_CHECK();
   return {dx, part.sum(0)};
@@ -439,6 +822,32 @@ __global__ void gn_stats_kernel(const T* __restrict__ x, float* __restrict__ par
   sum = block_sum(sum, sm);
   sq = block_sum(sq, sm);
   if (lin == 0) {
+    const int64_t o = (((int64_t)b * H + h) * gridDim.x + tile) * 3;
+    const float n = (float)((s1 - s0) * hd);
+    const float mean = sum / n;
+    part[o] = n; part[o + 1] = mean; part[o + 2] = fmaxf(sq - sum * mean, 0.f);
+  }
+}
+
+// Vector form of the stats pass: block = (hd / V) x (256 / (hd / V)) threads (hd / V a power of
+// two <= 32), a thread reads V consecutive dims of a row with one 16-byte load.
+template <typename T>
+__global__ void __launch_bounds__(256) gn_stats_vec_kernel(const T* __restrict__ x, float* __restrict__ part, int S,
+                                                          int H, int hd) {
+  constexpr int V = 16 / sizeof(T);
+  const int b = blockIdx.z, h = blockIdx.y, tile = blockIdx.x;
+  const int s0 = tile * GN_ROWS, s1 = min(S, s0 + GN_ROWS);
+  const int C = H * hd;
+  float sum = 0.f, sq = 0.f;
+  for (int s = s0 + threadIdx.y; s < s1; s += blockDim.y) {
+    const Vec16<T> a = ld16(x + ((int64_t)b * S + s) * C + (int64_t)h * hd + threadIdx.x * V);
+#pragma unroll
+    for (int k = 0; k < V; ++k) { const float v = to_f(a.v[k]); sum += v; sq = fmaf(v, v, sq); }
+  }
+  __shared__ float sm[64];
+  sum = block_sum(sum, sm);
+  sq = block_sum(sq, sm);
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
     const int64_t o = (((int64_t)b * H + h) * gridDim.x + tile) * 3;
     const float n = (float)((s1 - s0) * hd);
     const float mean = sum / n;
@@ -531,6 +940,62 @@ __global__ void gn_bwd_dx_kernel(const T* __restrict__ x, const T* __restrict__ 
   }
 }
 
+// Vectorised forms of the apply / dx passes: one block per token row, a thread handles V
+// consecutive channels (one head: hd % V == 0) with 16-byte loads and float4 weight reads.
+template <typename T>
+__global__ void gn_apply_vec_kernel(const T* __restrict__ x, const float* __restrict__ mr,
+                                    const float* __restrict__ w, const float* __restrict__ bias,
+                                    T* __restrict__ y, int S, int H, int hd) {
+  constexpr int V = 16 / sizeof(T);
+  const int C = H * hd;
+  const int64_t r = blockIdx.x;
+  const int b = (int)(r / S);
+  for (int v = threadIdx.x; v < C / V; v += blockDim.x) {
+    const int c = v * V, h = c / hd;
+    const float m = mr[2 * (b * H + h)], rs = mr[2 * (b * H + h) + 1];
+    const Vec16<T> a = ld16(x + r * C + c);
+    float wv[V], bv[V];
+    ld_w<V>(w, c, wv);
+    ld_w<V>(bias, c, bv);
+    Vec16<T> o;
+#pragma unroll
+    for (int k = 0; k < V; ++k) o.v[k] = from_f<T>(fmaf((to_f(a.v[k]) - m) * rs, wv[k], bv[k]));
+    st16(y + r * C + c, o);
+  }
+}
+
+template <typename T>
+__global__ void gn_bwd_dx_vec_kernel(const T* __restrict__ x, const T* __restrict__ dy, const float* __restrict__ mr,
+                                     const float* __restrict__ w, const float* __restrict__ gsum,
+                                     T* __restrict__ dx, int S, int H, int hd) {
+  constexpr int V = 16 / sizeof(T);
+  const int C = H * hd;
+  const float inv_n = 1.f / ((float)S * hd);
+  const int64_t r = blockIdx.x;
+  const int b = (int)(r / S);
+  for (int v = threadIdx.x; v < C / V; v += blockDim.x) {
+    const int c = v * V, g = b * H + c / hd;
+    const float m = mr[2 * g], rs = mr[2 * g + 1];
+    const float g1 = gsum[2 * g] * inv_n, g2 = gsum[2 * g + 1] * inv_n;
+    const Vec16<T> a = ld16(x + r * C + c), d = ld16(dy + r * C + c);
+    float wv[V];
+    ld_w<V>(w, c, wv);
+    Vec16<T> o;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float xh = (to_f(a.v[k]) - m) * rs;
+      o.v[k] = from_f<T>(rs * (to_f(d.v[k]) * wv[k] - g1 - xh * g2));
+    }
+    st16(dx + r * C + c, o);
+  }
+}
+
+template <typename T>
+static bool gn_vec_ok(int hd, int64_t rows, const void* a, const void* b, const void* c) {
+  constexpr int V = 16 / sizeof(T);
+  return hd % V == 0 && rows > 0 && rows <= INT32_MAX && aligned16(a) && aligned16(b) && aligned16(c);
+}
+
 std::vector<at::Tensor> head_groupnorm_fwd(at::Tensor x, int64_t H, at::Tensor w, at::Tensor bias, double eps) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(x.is_contiguous() && x.dim() == 3, "groupnorm: contiguous (B, S, C)");
@@ -542,13 +1007,24 @@ std::vector<at::Tensor> head_groupnorm_fwd(at::Tensor x, int64_t H, at::Tensor w
   at::Tensor y = at::empty_like(x);
   at::Tensor wc = w.to(at::kFloat).contiguous(), bc = bias.to(at::kFloat).contiguous();
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "gn_fwd", [&] {
-    gn_stats_kernel<scalar_t><<<dim3(tiles, H, B), gn_block(hd), 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), part.data_ptr<float>(), S, H, hd);
+    constexpr int V = 16 / sizeof(scalar_t);
+    const int nx = hd / V;
+    if (hd % V == 0 && nx > 0 && nx <= 32 && (nx & (nx - 1)) == 0 && aligned16(x.data_ptr()))
+      gn_stats_vec_kernel<scalar_t><<<dim3(tiles, H, B), dim3(nx, 256 / nx), 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), part.data_ptr<float>(), S, H, hd);
+    else
+      gn_stats_kernel<scalar_t><<<dim3(tiles, H, B), gn_block(hd), 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), part.data_ptr<float>(), S, H, hd);
     gn_finalize_kernel<<<(B * H + 127) / 128, 128, 0, stream()>>>(part.data_ptr<float>(), mr.data_ptr<float>(),
                                                                   B * H, tiles, (float)eps);
-    gn_apply_kernel<scalar_t><<<ew_blocks(x.numel()), 256, 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(), bc.data_ptr<float>(),
-        (scalar_t*)y.data_ptr(), (int64_t)B * S, S, H, hd);
+    if (gn_vec_ok<scalar_t>(hd, (int64_t)B * S, x.data_ptr(), wc.data_ptr(), bc.data_ptr()))
+      gn_apply_vec_kernel<scalar_t><<<(unsigned)((int64_t)B * S), 256, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(), bc.data_ptr<float>(),
+          (scalar_t*)y.data_ptr(), S, H, hd);
+    else
+      gn_apply_kernel<scalar_t><<<ew_blocks(x.numel()), 256, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(), bc.data_ptr<float>(),
+          (scalar_t*)y.data_ptr(), (int64_t)B * S, S, H, hd);
   });
   MAMF_LAUNCH_CHECK();
   return {y, mr};
@@ -570,9 +1046,14 @@ std::vector<at::Tensor> head_groupnorm_bwd(at::Tensor x, int64_t H, at::Tensor w
         (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(),
         gpart.data_ptr<float>(), wpart.data_ptr<float>(), S, H, hd);
     at::Tensor gsum = gpart.sum(1).contiguous();
-    gn_bwd_dx_kernel<scalar_t><<<ew_blocks(x.numel()), 256, 0, stream()>>>(
-        (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(),
-        gsum.data_ptr<float>(), (scalar_t*)dx.data_ptr(), (int64_t)B * S, S, H, hd);
+    if (gn_vec_ok<scalar_t>(hd, (int64_t)B * S, x.data_ptr(), dy.data_ptr(), wc.data_ptr()))
+      gn_bwd_dx_vec_kernel<scalar_t><<<(unsigned)((int64_t)B * S), 256, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(),
+          gsum.data_ptr<float>(), (scalar_t*)dx.data_ptr(), S, H, hd);
+    else
+      gn_bwd_dx_kernel<scalar_t><<<ew_blocks(x.numel()), 256, 0, stream()>>>(
+          (const scalar_t*)x.data_ptr(), (const scalar_t*)dy.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(),
+          gsum.data_ptr<float>(), (scalar_t*)dx.data_ptr(), (int64_t)B * S, S, H, hd);
   });
   MAMF_LAUNCH_CHECK();
   at::Tensor wsum = wpart.sum(0);
