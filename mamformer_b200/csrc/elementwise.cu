@@ -996,6 +996,26 @@ static bool gn_vec_ok(int hd, int64_t rows, const void* a, const void* b, const 
   return hd % V == 0 && rows > 0 && rows <= INT32_MAX && aligned16(a) && aligned16(b) && aligned16(c);
 }
 
+// Stats, finalize and apply passes of the forward.  Shared by head_groupnorm_fwd and the
+// allocation-free entry point at the end of this file, so both pick the same kernels (16-byte
+// forms when hd, the row count and the pointers allow) and give bitwise-equal results.
+template <typename T>
+static void gn_fwd_launch(const T* x, const float* w, const float* bias, T* y, float* part, float* mr, int B, int S,
+                          int H, int hd, int tiles, float eps, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const int nx = hd / V;
+  const int64_t rows = (int64_t)B * S;
+  if (hd % V == 0 && nx > 0 && nx <= 32 && (nx & (nx - 1)) == 0 && aligned16(x))
+    gn_stats_vec_kernel<T><<<dim3(tiles, H, B), dim3(nx, 256 / nx), 0, st>>>(x, part, S, H, hd);
+  else
+    gn_stats_kernel<T><<<dim3(tiles, H, B), gn_block(hd), 0, st>>>(x, part, S, H, hd);
+  gn_finalize_kernel<<<(B * H + 127) / 128, 128, 0, st>>>(part, mr, B * H, tiles, eps);
+  if (gn_vec_ok<T>(hd, rows, x, w, bias) && aligned16(y))
+    gn_apply_vec_kernel<T><<<(unsigned)rows, 256, 0, st>>>(x, mr, w, bias, y, S, H, hd);
+  else
+    gn_apply_kernel<T><<<ew_blocks(rows * H * hd), 256, 0, st>>>(x, mr, w, bias, y, rows, S, H, hd);
+}
+
 std::vector<at::Tensor> head_groupnorm_fwd(at::Tensor x, int64_t H, at::Tensor w, at::Tensor bias, double eps) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(x.is_contiguous() && x.dim() == 3, "groupnorm: contiguous (B, S, C)");
@@ -1007,24 +1027,9 @@ std::vector<at::Tensor> head_groupnorm_fwd(at::Tensor x, int64_t H, at::Tensor w
   at::Tensor y = at::empty_like(x);
   at::Tensor wc = w.to(at::kFloat).contiguous(), bc = bias.to(at::kFloat).contiguous();
   MAMF_DISPATCH_FLOAT_BF16(x.scalar_type(), "gn_fwd", [&] {
-    constexpr int V = 16 / sizeof(scalar_t);
-    const int nx = hd / V;
-    if (hd % V == 0 && nx > 0 && nx <= 32 && (nx & (nx - 1)) == 0 && aligned16(x.data_ptr()))
-      gn_stats_vec_kernel<scalar_t><<<dim3(tiles, H, B), dim3(nx, 256 / nx), 0, stream()>>>(
-          (const scalar_t*)x.data_ptr(), part.data_ptr<float>(), S, H, hd);
-    else
-      gn_stats_kernel<scalar_t><<<dim3(tiles, H, B), gn_block(hd), 0, stream()>>>(
-          (const scalar_t*)x.data_ptr(), part.data_ptr<float>(), S, H, hd);
-    gn_finalize_kernel<<<(B * H + 127) / 128, 128, 0, stream()>>>(part.data_ptr<float>(), mr.data_ptr<float>(),
-                                                                  B * H, tiles, (float)eps);
-    if (gn_vec_ok<scalar_t>(hd, (int64_t)B * S, x.data_ptr(), wc.data_ptr(), bc.data_ptr()))
-      gn_apply_vec_kernel<scalar_t><<<(unsigned)((int64_t)B * S), 256, 0, stream()>>>(
-          (const scalar_t*)x.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(), bc.data_ptr<float>(),
-          (scalar_t*)y.data_ptr(), S, H, hd);
-    else
-      gn_apply_kernel<scalar_t><<<ew_blocks(x.numel()), 256, 0, stream()>>>(
-          (const scalar_t*)x.data_ptr(), mr.data_ptr<float>(), wc.data_ptr<float>(), bc.data_ptr<float>(),
-          (scalar_t*)y.data_ptr(), (int64_t)B * S, S, H, hd);
+    gn_fwd_launch<scalar_t>((const scalar_t*)x.data_ptr(), wc.data_ptr<float>(), bc.data_ptr<float>(),
+                            (scalar_t*)y.data_ptr(), part.data_ptr<float>(), mr.data_ptr<float>(), B, S, (int)H, hd,
+                            tiles, (float)eps, stream());
   });
   MAMF_LAUNCH_CHECK();
   return {y, mr};
@@ -1154,20 +1159,11 @@ int mamf_head_groupnorm_fwd_noalloc(const void* x, const float* w, const float* 
   float* mr = mean_rstd_out ? mean_rstd_out : scratch + part_floats;
   cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
   const int Bi = (int)B, Si = (int)S, Hi = (int)H, hdi = (int)hd;
-  const int64_t numel = B * S * H * hd;
-  dim3 sgrid((unsigned)tiles, (unsigned)H, (unsigned)B), sblock = gn_block(hd);
-  if (dtype == 1) {
-    gn_stats_kernel<__nv_bfloat16><<<sgrid, sblock, 0, st>>>((const __nv_bfloat16*)x, part, Si, Hi, hdi);
-  } else {
-    gn_stats_kernel<float><<<sgrid, sblock, 0, st>>>((const float*)x, part, Si, Hi, hdi);
-  }
-  gn_finalize_kernel<<<(unsigned)((B * H + 127) / 128), 128, 0, st>>>(part, mr, Bi * Hi, (int)tiles, eps);
-  if (dtype == 1) {
-    gn_apply_kernel<__nv_bfloat16><<<ew_blocks(numel), 256, 0, st>>>(
-        (const __nv_bfloat16*)x, mr, w, b, (__nv_bfloat16*)y, B * S, Si, Hi, hdi);
-  } else {
-    gn_apply_kernel<float><<<ew_blocks(numel), 256, 0, st>>>((const float*)x, mr, w, b, (float*)y, B * S, Si, Hi, hdi);
-  }
+  if (dtype == 1)
+    gn_fwd_launch<__nv_bfloat16>((const __nv_bfloat16*)x, w, b, (__nv_bfloat16*)y, part, mr, Bi, Si, Hi, hdi,
+                                 (int)tiles, eps, st);
+  else
+    gn_fwd_launch<float>((const float*)x, w, b, (float*)y, part, mr, Bi, Si, Hi, hdi, (int)tiles, eps, st);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     noalloc::forget_current_device();   // a reset context invalidates the cached address
