@@ -599,6 +599,7 @@ constexpr int LC = C + 8;          // 64-wide tiles
 template <bool PHI>
 __device__ __forceinline__ void load_bf(__nv_bfloat16* dst, const __nv_bfloat16* src, int b, int s0, int rows,
                                         int head, int heads, int S) {
+#pragma unroll
   for (int i = threadIdx.x; i < C * (D / 8); i += NT) {
     const int r = i / (D / 8), c = (i % (D / 8)) * 8;
     int4 v = make_int4(0, 0, 0, 0);
@@ -611,13 +612,24 @@ __device__ __forceinline__ void load_bf(__nv_bfloat16* dst, const __nv_bfloat16*
     *reinterpret_cast<int4*>(dst + r * LB + c) = v;
   }
 }
-// fp32 state (K x D) (+ z column) -> bf16 smem [K][LSX]
+// fp32 (K x D) state rows -> bf16 smem rows of stride ld: 16-byte loads, eight in flight per thread
+__device__ __forceinline__ void load_state_rows(__nv_bfloat16* dst, int ld, const float* S, bool has) {
+#pragma unroll 8
+  for (int i = threadIdx.x; i < D * (D / 4); i += NT) {
+    const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+    const float4 v = has ? *reinterpret_cast<const float4*>(S + r * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint2 o;
+    o.x = wm::pack_bf16(v.x, v.y);
+    o.y = wm::pack_bf16(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst + r * ld + c) = o;
+  }
+}
+// fp32 state (K x D) (+ z column, zero pad to D + 16) -> bf16 smem [K][LSX]
 __device__ __forceinline__ void load_state(__nv_bfloat16* dst, const float* S, const float* z, bool has) {
-  for (int i = threadIdx.x; i < D * (D + 16); i += NT) {
-    const int r = i / (D + 16), c = i % (D + 16);
-    float v = 0.f;
-    if (has) v = c < D ? S[r * D + c] : (c == D && z ? z[r] : 0.f);
-    dst[r * LSX + c] = __float2bfloat16(v);
+  load_state_rows(dst, LSX, S, has);
+  for (int i = threadIdx.x; i < D * 16; i += NT) {
+    const int r = i / 16, c = D + i % 16;
+    dst[r * LSX + c] = __float2bfloat16((has && c == D && z) ? z[r] : 0.f);
   }
 }
 
@@ -918,11 +930,8 @@ __global__ void __launch_bounds__(NT) dqkv_kernel(Params p, const __nv_bfloat16*
   {
     const float* S = p.st + ((((int64_t)b * p.G + g) * p.NC + c) * D) * D;
     const float* R = p.Rg + ((((int64_t)b * p.G + g) * p.NC + c) * D) * D;
-    for (int i = threadIdx.x; i < D * D; i += NT) {
-      const int r = i / D, col = i % D;
-      sS[r * LB + col] = __float2bfloat16(has ? S[i] : 0.f);
-      sR[r * LB + col] = __float2bfloat16(hasR ? R[i] : 0.f);
-    }
+    load_state_rows(sS, LB, S, has);
+    load_state_rows(sR, LB, R, hasR);
     sz[threadIdx.x] = has ? p.zs[(((int64_t)b * p.G + g) * p.NC + c) * D + threadIdx.x] : 0.f;
     srn[threadIdx.x] = hasR ? p.rg[(((int64_t)b * p.G + g) * p.NC + c) * D + threadIdx.x] : 0.f;
   }

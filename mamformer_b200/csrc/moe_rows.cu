@@ -225,6 +225,59 @@ __global__ void combine_bwd_kernel(const T* __restrict__ dout, const T* __restri
   }
 }
 
+// Fixed top-k form (K known at compile time, the flagship's 8): a thread reads its K row indices
+// and gates once, then issues the K row loads of a column chunk together before using any of
+// them, so K independent 16-byte loads are in flight per thread (the generic kernel above waits
+// for each routed row in turn).
+template <typename T, int K>
+__global__ void combine_bwd_k_kernel(const T* __restrict__ dout, const T* __restrict__ y, const int64_t* __restrict__ y_idx,
+                                     int64_t y_rows, const float* __restrict__ gate, float* __restrict__ dgate,
+                                     T* __restrict__ dy, const int64_t* __restrict__ dy_idx, int64_t dy_rows, int64_t d) {
+  __shared__ float red[32 * K];
+  const int64_t t = blockIdx.x;
+  int64_t yr[K], dr[K];
+  float gw[K], part[K];
+  bool ok[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int64_t q = t * K + j;
+    yr[j] = y_idx ? y_idx[q] : q;
+    dr[j] = dy_idx ? dy_idx[q] : q;
+    ok[j] = MAMF_BOUND(yr[j] >= 0 && yr[j] < y_rows && dr[j] >= 0 && dr[j] < dy_rows, 1103);
+    gw[j] = gate[q];
+    part[j] = 0.f;
+  }
+  for (int64_t c = (int64_t)threadIdx.x * 8; c < d; c += (int64_t)blockDim.x * 8) {
+    float g[8], f[K][8];
+    Chunk<T>::load(dout + t * d + c, g);
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      if (ok[j]) Chunk<T>::load(y + yr[j] * d + c, f[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      if (!ok[j]) continue;
+      float sacc = 0.f, o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { sacc = fmaf(f[j][i], g[i], sacc); o[i] = gw[j] * g[i]; }
+      part[j] += sacc;
+      Chunk<T>::store(dy + dr[j] * d + c, o);
+    }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const float v = warp_sum(part[j]);
+    if (lane == 0) red[wid * K + j] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < K) {
+    float sum = 0.f;
+    for (int w = 0; w < nw; ++w) sum += red[w * K + threadIdx.x];
+    dgate[t * K + threadIdx.x] = sum;
+  }
+}
+
 // dout (T, d); y rows (indexed by y_idx[q] or q); gate (Q,) fp32 -> dgate (Q,) fp32,
 // dy rows (written at dy_idx[q] or q).
 void moe_combine_bwd(at::Tensor dout, at::Tensor y, c10::optional<at::Tensor> y_idx, at::Tensor gate,
@@ -239,6 +292,13 @@ void moe_combine_bwd(at::Tensor dout, at::Tensor y, c10::optional<at::Tensor> y_
               dgate.numel() == T * k, "combine_bwd: gate / dgate fp32 (Q,)");
   const int thr = std::max(32, row_threads(d) / 32 * 32);
   MAMF_DISPATCH_FLOAT_BF16(dout.scalar_type(), "combine_bwd", [&] {
+    if (k == 8) {
+      combine_bwd_k_kernel<scalar_t, 8><<<(unsigned)T, thr, 0, stream()>>>(
+          (const scalar_t*)dout.data_ptr(), (const scalar_t*)y.data_ptr(), y_idx ? y_idx->data_ptr<int64_t>() : nullptr,
+          y.size(0), gate.data_ptr<float>(), dgate.data_ptr<float>(), (scalar_t*)dy.data_ptr(),
+          dy_idx ? dy_idx->data_ptr<int64_t>() : nullptr, dy.size(0), d);
+      return;
+    }
     combine_bwd_kernel<scalar_t><<<(unsigned)T, thr, 0, stream()>>>(
         (const scalar_t*)dout.data_ptr(), (const scalar_t*)y.data_ptr(), y_idx ? y_idx->data_ptr<int64_t>() : nullptr,
         y.size(0), gate.data_ptr<float>(), dgate.data_ptr<float>(), (scalar_t*)dy.data_ptr(),
