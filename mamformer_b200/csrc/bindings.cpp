@@ -27,6 +27,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
 void sq_norm_accumulate(at::Tensor g, at::Tensor out);
 void clip_scale(at::Tensor sq, at::Tensor scale, double max_norm, double inv_world, at::Tensor norm_out);
 void grad_accumulate(at::Tensor dst, at::Tensor src);
+void embedding_grad_accumulate(at::Tensor mg, at::Tensor ids, at::Tensor dy);
 void gemm_tn(at::Tensor A, bool a_mn, at::Tensor B, bool b_mn, at::Tensor D, bool accumulate,
              c10::optional<at::Tensor> seg, c10::optional<at::Tensor> tile_off, int64_t mode, double alpha);
 int64_t gemm_error();
@@ -104,6 +105,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sq_norm_accumulate", &mamf::sq_norm_accumulate);
   m.def("clip_scale", &mamf::clip_scale);
   m.def("grad_accumulate", &mamf::grad_accumulate);
+  m.def("embedding_grad_accumulate", &mamf::embedding_grad_accumulate);
   m.def("gemm_tn", &mamf::gemm_tn);
   m.def("gemm_error", &mamf::gemm_error);
   m.def("gemm_clear_error", &mamf::gemm_clear_error);

@@ -157,4 +157,35 @@ void grad_accumulate(at::Tensor dst, at::Tensor src) {
   MAMF_LAUNCH_CHECK();
 }
 
+// Embedding weight gradient: mg (V, d) fp32 += dy rows (N, d) at rows ids (N,), with fp32
+// reductions at L2 (a block per token row, consecutive lanes on consecutive columns), so no dense
+// V x d gradient is materialised and no separate accumulation pass runs.  Ids outside [0, V) are
+// skipped (the forward gather has already rejected them).
+template <typename T>
+__global__ void embedding_grad_kernel(float* __restrict__ mg, const int64_t* __restrict__ ids,
+                                      const T* __restrict__ dy, int64_t N, int64_t V, int64_t d) {
+  for (int64_t r = blockIdx.x; r < N; r += gridDim.x) {
+    const int64_t v = ids[r];
+    if (v < 0 || v >= V) continue;
+    float* dst = mg + v * d;
+    const T* src = dy + r * d;
+    for (int64_t c = threadIdx.x; c < d; c += blockDim.x) atomicAdd(dst + c, to_f(src[c]));
+  }
+}
+
+void embedding_grad_accumulate(at::Tensor mg, at::Tensor ids, at::Tensor dy) {
+  c10::cuda::CUDAGuard guard(mg.device());
+  TORCH_CHECK(mg.is_contiguous() && mg.dim() == 2 && mg.scalar_type() == at::kFloat, "embedding grad: fp32 (V, d)");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && dy.is_contiguous() && dy.dim() == 2 &&
+              dy.size(0) == ids.numel() && dy.size(1) == mg.size(1), "embedding grad: ids (N,), dy (N, d)");
+  const int64_t N = ids.numel(), V = mg.size(0), d = mg.size(1);
+  if (N == 0) return;
+  const unsigned blocks = (unsigned)std::min<int64_t>(N, (int64_t)num_sms() * 16);
+  MAMF_DISPATCH_FLOAT_BF16(dy.scalar_type(), "embedding_grad", [&] {
+    embedding_grad_kernel<scalar_t><<<blocks, 256, 0, stream()>>>(mg.data_ptr<float>(), ids.data_ptr<int64_t>(),
+                                                                  (const scalar_t*)dy.data_ptr(), N, V, d);
+  });
+  MAMF_LAUNCH_CHECK();
+}
+
 }  // namespace mamf

@@ -69,11 +69,50 @@ class FusedLinear(nn.Linear):
         return linear(x, self.weight, self.bias)
 
 
+class _EmbeddingMG(torch.autograd.Function):
+    """Row gather whose weight gradient is scattered straight into ``W.main_grad`` (fp32) by the
+    native kernel (csrc/optim.cu): no dense vocab x d gradient, no accumulation pass."""
+
+    @staticmethod
+    def forward(ctx, ids, w):
+        ctx.save_for_backward(ids)
+        ctx.w = w
+        return F.embedding(ids, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (ids,) = ctx.saved_tensors
+        w = ctx.w
+        from mamformer_b200.ops._ext import require_native
+        require_native().embedding_grad_accumulate(w.main_grad, ids.reshape(-1).contiguous(),
+                                                   dy.reshape(-1, w.shape[1]).contiguous())
+        from mamformer_b200.optim import mark_grad_ready
+        mark_grad_ready(w)
+        return None, None
+
+
+class FusedEmbedding(nn.Embedding):
+    """``nn.Embedding`` whose weight gradient goes straight into the optimizer's fp32
+    ``weight.main_grad`` when there is one (CUDA, no padding index / max-norm / sparse options);
+    otherwise the plain module's behaviour.  Same parameters and state-dict keys."""
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        w = self.weight
+        if (w.requires_grad and torch.is_grad_enabled() and getattr(w, "main_grad", None) is not None
+                and w.is_cuda and self.padding_idx is None and self.max_norm is None and not self.sparse
+                and not self.scale_grad_by_freq):
+            return _EmbeddingMG.apply(ids, w)
+        return super().forward(ids)
+
+
 def use_native_linear(model: nn.Module) -> int:
-    """Switch every plain ``nn.Linear`` of ``model`` to :class:`FusedLinear`; returns the count."""
+    """Switch every plain ``nn.Linear`` of ``model`` to :class:`FusedLinear` and every plain
+    ``nn.Embedding`` to :class:`FusedEmbedding`; returns the number of linears switched."""
     n = 0
     for m in model.modules():
         if type(m) is nn.Linear:
             m.__class__ = FusedLinear
             n += 1
+        elif type(m) is nn.Embedding:
+            m.__class__ = FusedEmbedding
     return n

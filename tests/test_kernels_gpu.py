@@ -193,3 +193,23 @@ def test_selective_scan_reference_signature():
     _close(y, yr, 1e-4, 1e-5, "y")
     _close(hs, hsr, 1e-4, 1e-6, "hs")
     _close(fin, finr, 1e-4, 1e-6, "final")
+
+
+def test_embedding_gradient_goes_into_main_grad():
+    """FusedEmbedding scatters its weight gradient straight into the fp32 main_grad buffer (repeated
+    ids accumulate); no bf16 weight gradient is produced."""
+    from mamformer_b200.ops.linear import FusedEmbedding
+    torch.manual_seed(0)
+    emb = torch.nn.Embedding(1000, 256).to(_dev()).bfloat16()
+    emb.__class__ = FusedEmbedding
+    emb.weight.main_grad = torch.randn(1000, 256, device=_dev())
+    before = emb.weight.main_grad.clone()
+    ids = torch.randint(0, 1000, (3, 700), device=_dev())
+    ids[0, :50] = 7
+    y = emb(ids)
+    assert torch.equal(y, emb.weight.detach()[ids])
+    dy = torch.randn_like(y)
+    (y.float() * dy.float()).sum().backward()
+    assert emb.weight.grad is None
+    want = before.double().index_add(0, ids.reshape(-1), dy.reshape(-1, 256).double())
+    _close(emb.weight.main_grad, want, 1e-5, 1e-5, "main_grad")
