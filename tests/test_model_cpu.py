@@ -234,3 +234,23 @@ def test_full_layer_checkpointing_matches_plain_backward(moe):
         assert torch.allclose(g0[n], g1[n], rtol=1e-5, atol=1e-7), n
     for n in b0:
         assert torch.equal(b0[n], b1[n]), n
+
+
+def test_native_layer_switch_keeps_embedding_semantics_on_cpu(debug_cfg):
+    """use_native_linear also switches nn.Embedding to FusedEmbedding; on CPU (no main_grad
+    routing) the module behaves exactly like nn.Embedding and keeps its state-dict keys."""
+    from mamformer_b200.ops.linear import FusedEmbedding, use_native_linear
+    torch.manual_seed(0)
+    m = MamformerForCausalLM(debug_cfg)
+    keys = list(m.state_dict().keys())
+    ids = torch.randint(0, debug_cfg.vocab_size, (2, 9))
+    ref = m.model.embed_tokens.weight[ids].clone()
+    use_native_linear(m)
+    assert isinstance(m.model.embed_tokens, FusedEmbedding)
+    assert list(m.state_dict().keys()) == keys
+    y = m.model.embed_tokens(ids)
+    assert torch.equal(y, ref)
+    y.sum().backward()
+    g = m.model.embed_tokens.weight.grad
+    want = torch.zeros_like(g).index_add_(0, ids.reshape(-1), torch.ones(ids.numel(), g.shape[1]))
+    assert torch.equal(g, want)
