@@ -638,8 +638,12 @@ __global__ void conv_silu_fwd_vec_kernel(const T* __restrict__ x, const float* _
     }
   }
   const int t1 = min(S, t0 + CONV_TT);
+  float nxt[CV];                                          // x row of the next step, loaded one ahead
+  ld_cv(x + ((int64_t)b * S + t0) * xs + c0, nxt);
   for (int t = t0; t < t1; ++t) {
-    ld_cv(x + ((int64_t)b * S + t) * xs + c0, hist[K - 1]);
+#pragma unroll
+    for (int i = 0; i < CV; ++i) hist[K - 1][i] = nxt[i];
+    if (t + 1 < t1) ld_cv(x + ((int64_t)b * S + t + 1) * xs + c0, nxt);
     float o[CV];
 #pragma unroll
     for (int i = 0; i < CV; ++i) {
@@ -682,14 +686,15 @@ __global__ void conv_silu_bwd_vec_kernel(const T* __restrict__ x, const float* _
 #pragma unroll
   for (int j = 0; j < 2 * K; ++j) ldx(t0 - K + 1 + j, xw[j]);
   // d pre-activation at time u, from the window: pre(u) = sum_k w_k x[u - K + 1 + k]
-  auto dpre = [&](int u, int j0, float (&o)[CV]) {       // x[u - K + 1] is xw[j0]
-    if (u >= S) {
+  auto ldg = [&](int u, float (&o)[CV]) {
+    if (u < S) ld_cv(dy + ((int64_t)b * S + u) * C + c0, o);
+    else {
 #pragma unroll
       for (int i = 0; i < CV; ++i) o[i] = 0.f;
-      return;
     }
-    float g[CV];
-    ld_cv(dy + ((int64_t)b * S + u) * C + c0, g);
+  };
+  // g = dy[u] (zero past the end gives dpre = 0)
+  auto dpre = [&](int u, int j0, const float (&g)[CV], float (&o)[CV]) {   // x[u - K + 1] is xw[j0]
 #pragma unroll
     for (int i = 0; i < CV; ++i) {
       float pre = 0.f;
@@ -701,7 +706,13 @@ __global__ void conv_silu_bwd_vec_kernel(const T* __restrict__ x, const float* _
   };
   float dp[K][CV];                                        // dp[j] = dpre(t + j)
 #pragma unroll
-  for (int k = 0; k < K; ++k) dpre(t0 + k, k, dp[k]);
+  for (int k = 0; k < K; ++k) {
+    float g[CV];
+    ldg(t0 + k, g);
+    dpre(t0 + k, k, g, dp[k]);
+  }
+  float gn[CV];                                           // dy row of the next step's dpre, loaded one ahead
+  ldg(t0 + K, gn);
   float dwa[CV][K];
 #pragma unroll
   for (int i = 0; i < CV; ++i)
@@ -724,7 +735,11 @@ __global__ void conv_silu_bwd_vec_kernel(const T* __restrict__ x, const float* _
     for (int k = 0; k < K - 1; ++k)
 #pragma unroll
       for (int i = 0; i < CV; ++i) dp[k][i] = dp[k + 1][i];
-    dpre(t + K, K, dp[K - 1]);                            // x[t + 1 .. t + K] = xw[K .. 2K - 1]
+    float gc[CV];
+#pragma unroll
+    for (int i = 0; i < CV; ++i) gc[i] = gn[i];
+    ldg(t + K + 1, gn);
+    dpre(t + K, K, gc, dp[K - 1]);                        // x[t + 1 .. t + K] = xw[K .. 2K - 1]
 #pragma unroll
     for (int j = 0; j < 2 * K - 1; ++j)
 #pragma unroll
