@@ -231,6 +231,8 @@ class GradReducer:
         with rng(f"dp.bucket[{b.lo}:{b.hi}]"):
             if b.seg.symm is not None:
                 self._launch_p2p(b)
+            elif b.seg.sharded:
+                b.work = _reduce_to_owners(b.seg, b.lo, b.hi, b.group)
             else:
                 b.work = dist.all_reduce(b.seg.grad[b.lo:b.hi], group=b.group, async_op=True)
 
@@ -334,6 +336,33 @@ def dp_pull_allreduce(h, buf: torch.Tensor, lo: int, hi: int, barrier, tmp: dict
 def _use_nvls() -> bool:
     """NVSwitch multicast reduction for the peer-memory gradient all-reduce (opt-in)."""
     return os.environ.get("MAMF_DP_NVLS", "0") == "1"
+
+
+class _Works:
+    """Several collective handles behind one ``wait()``."""
+
+    def __init__(self, works):
+        self.works = works
+
+    def wait(self) -> None:
+        for w in self.works:
+            w.wait()
+
+
+def _reduce_to_owners(seg, lo: int, hi: int, group) -> _Works:
+    """ZeRO-1 bucket reduction: a rank's optimizer reads only its own slice [seg.lo, seg.hi) of
+    the summed gradient, so the bucket [lo, hi) is summed onto the owner of each slice it
+    overlaps (``dist.reduce``, about half the bytes an all-reduce moves).  The other ranks'
+    copies of those elements are left partial and are never read."""
+    sw = _group_size(group)
+    n = seg.numel
+    works = []
+    for q in range(sw):                       # the same owner order on every rank
+        a, z = max(lo, q * n // sw), min(hi, (q + 1) * n // sw)
+        if a < z:
+            dst = dist.get_global_rank(group, q) if group is not None else q
+            works.append(dist.reduce(seg.grad[a:z], dst=dst, group=group, async_op=True))
+    return _Works(works)
 
 
 class _StreamWork:
