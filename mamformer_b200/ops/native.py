@@ -355,8 +355,10 @@ class _DiffFlashTC(torch.autograd.Function):
             dq1, dk1, dv1 = _C.flash_attn_bwd(q1, k, v, o1, lse1, do1, *ctx.args)
             dq2, dk2, dv2 = _C.flash_attn_bwd(q2, k, v, o2, lse2, do2, *ctx.args)
             dk, dv = dk1 + dk2, dv1 + dv2
-        # in place on the fp32 copy of dout (not used below); od is promoted element by element
-        dlam = d32.mul_(od).sum(dim=(0, 1, 3)) * den * den    # the 1e-8 o2 term is below fp32 noise
+        # in place on the fp32 copy of dout (never on dout itself, which autograd may share with
+        # other branches); od is promoted element by element
+        prod = d32 if d32.data_ptr() != dout.data_ptr() else d32.clone()
+        dlam = prod.mul_(od).sum(dim=(0, 1, 3)) * den * den    # the 1e-8 o2 term is below fp32 noise
         return dq1, dq2, dk, dv, dlam.to(ctx.lam_dtype), None, None, None
 
 
