@@ -126,6 +126,23 @@ def dp_zero_worker(rank, world):
         _check("reloaded " + n, p.detach(), q.detach(), 0.0)
 
 
+def zero_reduce_worker(rank, world):
+    """ZeRO-1 bucket reduction onto slice owners: for buckets that overlap one, two or all
+    owners' slices, every owner ends up with the sum over ranks of its part of the bucket."""
+    from types import SimpleNamespace
+    from mamformer_b200.optim import _reduce_to_owners
+    n = 103                                    # slices of 34 / 34 / 35 elements at world 3
+    base = torch.arange(n, dtype=torch.float32)
+    want = sum(base * (r + 1) for r in range(world))
+    lo_own, hi_own = rank * n // world, (rank + 1) * n // world
+    for lo, hi in [(0, n), (10, 40), (35, 36), (60, 103)]:
+        seg = SimpleNamespace(numel=n, grad=base * (rank + 1))
+        _reduce_to_owners(seg, lo, hi, dist.group.WORLD).wait()
+        a, z = max(lo, lo_own), min(hi, hi_own)
+        if a < z:
+            assert torch.equal(seg.grad[a:z], want[a:z]), (rank, lo, hi)
+
+
 # ---- expert parallel ------------------------------------------------------------------------------
 def ep_worker(rank, world):
     from mamformer_b200.parallel import (DistributedCoordinator, ParallelConfig, expert_parameters)

@@ -64,6 +64,10 @@ def test_zero1_sharded_optimizer_matches_unsharded():
     _spawn(W.dp_zero_worker, 2)
 
 
+def test_zero1_bucket_reduction_reaches_every_slice_owner():
+    _spawn(W.zero_reduce_worker, 3)
+
+
 def test_expert_parallel_matches_single_process():
     _spawn(W.ep_worker, 2)
 
