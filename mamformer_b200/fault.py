@@ -7,7 +7,7 @@ the cache, zero the gradients, write ``checkpoint_oom_recovery_step_N.pt`` and c
 
 Added here (all detection happens on the host; nothing faults, traps or hangs a GPU):
 
-* every in-kernel cross-GPU wait (the expert-parallel / tensor-parallel barrier, the GEMM
+* every in-kernel wait (the expert-parallel / tensor-parallel barrier, the GEMM and attention
   pipeline waits) is bounded and records an error code instead of hanging;
   :func:`check_device_status` reads those words after the stream has drained and raises
   :class:`CommTimeoutError` / :class:`KernelTimeoutError`;
@@ -60,10 +60,19 @@ def check_device_status(clear: bool = True) -> None:
         C.comm_clear_error()
     if clear and gemm:
         C.gemm_clear_error()
+    # the attention kernels' words (forward, backward) are cleared by the read itself
+    attn = 0
+    for name in ("flash_tc_error", "flash_tc_bwd_error"):
+        fn = getattr(C, name, None)
+        if fn is not None:
+            attn = attn or int(fn())
     if comm:
         raise CommTimeoutError(f"cross-GPU barrier timed out waiting for peer {comm - 100}")
     if gemm:
         raise KernelTimeoutError(f"tcgen05 GEMM pipeline wait timed out (code {gemm})")
+    if attn:
+        raise KernelTimeoutError(f"tcgen05 attention kernel reported code {attn} "
+                                 "(a pipeline wait timed out, or a checked index was out of range)")
 
 
 class Heartbeat:
